@@ -1,0 +1,552 @@
+// bf16 GEMM on the 5th-generation tensor cores: C = epi(A * B^T).
+//
+// Design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte
+//               swizzle, STAGES-deep ring of shared-memory buffers guarded by
+//               full/empty mbarriers.
+//   warp 1      allocates TMEM, then one thread issues tcgen05.mma
+//               (M=128, N=BN, K=16, bf16 -> fp32) into one of two TMEM
+//               accumulators and releases stages with tcgen05.commit.
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, fused
+//               bias / residual / SwiGLU / GELU, bf16 stores.
+// The accumulator is double-buffered, so tile i's epilogue overlaps tile
+// i+1's main loop.
+//
+// Skinny problems (few token rows, the decode case) run "swapped": the weight
+// matrix feeds the 128-row MMA side and the tokens the N side, and the
+// epilogue writes the transpose.  When there are too few output tiles to
+// cover the SMs the K loop is split and fp32 partials go to a workspace that
+// a second kernel reduces while applying the epilogue.
+//
+// No TMA multicast is used (the library also runs in multi-GPU jobs).
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm.h"
+
+using namespace b200;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
+};
+
+struct Params {
+  int64_t rows;    // MMA M extent (rows of A)
+  int64_t cols;    // MMA N extent (rows of B)
+  int64_t K;
+  int tiles_m, tiles_n, splits, kb_total, kb_per_split;
+  __nv_bfloat16* C;
+  int64_t ldc;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* R;
+  int64_t ldr;
+  float* ws;  // split-K partials [splits][tokens][features]
+  unsigned* err;
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// Epilogue on 8 consecutive features f0..f0+7 of token `tok` (non-SwiGLU kinds).
+template <int EPI>
+__device__ __forceinline__ void epi8(float v[8], int64_t tok, int64_t f0, const Params& p) {
+  if (EPI == B200_EPI_BIAS || EPI == B200_EPI_BIAS_GELU || EPI == B200_EPI_BIAS_RESIDUAL) {
+    float b[8];
+    unpack8(*reinterpret_cast<const uint4*>(p.bias + f0), b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] += b[i];
+  }
+  if (EPI == B200_EPI_BIAS_GELU) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = gelu_tanh_f(v[i]);
+  }
+  if (EPI == B200_EPI_RESIDUAL || EPI == B200_EPI_BIAS_RESIDUAL) {
+    float r[8];
+    unpack8(*reinterpret_cast<const uint4*>(p.R + tok * p.ldr + f0), r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] += r[i];
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ float epi1(float v, int64_t tok, int64_t f, const Params& p) {
+  if (EPI == B200_EPI_BIAS || EPI == B200_EPI_BIAS_GELU || EPI == B200_EPI_BIAS_RESIDUAL) v += bf2f(p.bias[f]);
+  if (EPI == B200_EPI_BIAS_GELU) v = gelu_tanh_f(v);
+  if (EPI == B200_EPI_RESIDUAL || EPI == B200_EPI_BIAS_RESIDUAL) v += bf2f(p.R[tok * p.ldr + f]);
+  return v;
+}
+
+__device__ __forceinline__ void decode_unit(int w, const Params& p, int& tm, int& tn, int& kb0, int& kb1) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int split = w / tiles;
+  const int t = w % tiles;
+  const int group = kGroupM * p.tiles_n;
+  const int g = t / group;
+  const int first_m = g * kGroupM;
+  const int gm = min(p.tiles_m - first_m, kGroupM);
+  const int r = t % group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+  kb0 = split * p.kb_per_split;
+  kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+}
+
+template <int BN, int EPI, bool SWAP, bool PARTIAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const Params p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = p.tiles_m * p.tiles_n * p.splits;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x) {
+        int tm, tn, kb0, kb1;
+        decode_unit(w, p, tm, tn, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
+        int tm, tn, kb0, kb1;
+        decode_unit(w, p, tm, tn, kb0, kb1);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d_tmem, smem_desc_k128(a0 + k * 32), smem_desc_k128(b0 + k * 32), C::IDESC,
+                      (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int rit = q * 32 + lane;
+    int local = 0;
+    for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
+      int tm, tn, kb0, kb1;
+      decode_unit(w, p, tm, tn, kb0, kb1);
+      const int split = w / (p.tiles_m * p.tiles_n);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = (int64_t)tm * BM + rit;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        const int64_t col0 = (int64_t)tn * BN + ch * 32;
+        if (!SWAP) {
+          // row = token, columns = features
+          if (row < p.rows) {
+            if (PARTIAL) {
+              float* dst = p.ws + ((int64_t)split * p.rows + row) * p.cols;
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                if (col0 + g * 4 < p.cols)
+                  *reinterpret_cast<float4*>(dst + col0 + g * 4) =
+                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+            } else if (EPI == B200_EPI_SWIGLU) {
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int64_t c = col0 + g * 8;
+                if (c < p.cols) {
+                  uint2 o;
+                  o.x = pack2(silu_f(v[8 * g]) * v[8 * g + 1], silu_f(v[8 * g + 2]) * v[8 * g + 3]);
+                  o.y = pack2(silu_f(v[8 * g + 4]) * v[8 * g + 5], silu_f(v[8 * g + 6]) * v[8 * g + 7]);
+                  *reinterpret_cast<uint2*>(p.C + row * p.ldc + c / 2) = o;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int64_t c = col0 + g * 8;
+                if (c < p.cols) {
+                  float* vv = v + 8 * g;
+                  epi8<EPI>(vv, row, c, p);
+                  *reinterpret_cast<uint4*>(p.C + row * p.ldc + c) = pack8(vv);
+                }
+              }
+            }
+          }
+        } else {
+          // row = feature (lanes hold consecutive features), columns = tokens
+          if (PARTIAL) {
+            if (row < p.rows) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.cols) p.ws[((int64_t)split * p.cols + col0 + i) * p.rows + row] = v[i];
+            }
+          } else if (EPI == B200_EPI_SWIGLU) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+              if (!(lane & 1) && row < p.rows && col0 + i < p.cols)
+                p.C[(col0 + i) * p.ldc + row / 2] = f2bf(silu_f(v[i]) * up);
+            }
+          } else {
+            if (row < p.rows) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.cols) p.C[(col0 + i) * p.ldc + row] = f2bf(epi1<EPI>(v[i], col0 + i, row, p));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// Sum split-K partials ws[s][tok][feat] and apply the epilogue.
+// One thread per 8 features (SwiGLU: per 8 interleaved features -> 4 outputs).
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t tokens, int64_t feats,
+                                     Params p) {
+  const int64_t nv = feats / 8;
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (gid >= tokens * nv) return;
+  const int64_t tok = gid / nv, f0 = (gid % nv) * 8;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < splits; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(ws + ((int64_t)s * tokens + tok) * feats + f0);
+    const float4 a = src[0], b = src[1];
+    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  }
+  if (EPI == B200_EPI_SWIGLU) {
+    uint2 o;
+    o.x = pack2(silu_f(v[0]) * v[1], silu_f(v[2]) * v[3]);
+    o.y = pack2(silu_f(v[4]) * v[5], silu_f(v[6]) * v[7]);
+    *reinterpret_cast<uint2*>(p.C + tok * p.ldc + f0 / 2) = o;
+  } else {
+    epi8<EPI>(v, tok, f0, p);
+    *reinterpret_cast<uint4*>(p.C + tok * p.ldc + f0) = pack8(v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride ld,
+// box = box_rows x 64 elements (128 bytes, the swizzle span).
+bool make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+template <int BN, int EPI, bool SWAP, bool PARTIAL>
+int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int grid, cudaStream_t st) {
+  auto k = gemm_tcgen05_kernel<BN, EPI, SWAP, PARTIAL>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM) != cudaSuccess)
+      return B200_ERROR_UNSUPPORTED;
+    attr_set[dev] = true;
+  }
+  k<<<grid, kThreads, Cfg<BN>::SMEM, st>>>(a, b, p);
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+template <int BN, bool SWAP, bool PARTIAL>
+int launch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const Params& p, int grid, cudaStream_t st) {
+  if (PARTIAL) return launch_t<BN, B200_EPI_NONE, SWAP, true>(a, b, p, grid, st);
+  switch (epi) {
+    case B200_EPI_NONE: return launch_t<BN, B200_EPI_NONE, SWAP, false>(a, b, p, grid, st);
+    case B200_EPI_BIAS: return launch_t<BN, B200_EPI_BIAS, SWAP, false>(a, b, p, grid, st);
+    case B200_EPI_RESIDUAL: return launch_t<BN, B200_EPI_RESIDUAL, SWAP, false>(a, b, p, grid, st);
+    case B200_EPI_SWIGLU: return launch_t<BN, B200_EPI_SWIGLU, SWAP, false>(a, b, p, grid, st);
+    case B200_EPI_BIAS_GELU: return launch_t<BN, B200_EPI_BIAS_GELU, SWAP, false>(a, b, p, grid, st);
+    case B200_EPI_BIAS_RESIDUAL: return launch_t<BN, B200_EPI_BIAS_RESIDUAL, SWAP, false>(a, b, p, grid, st);
+  }
+  return B200_ERROR_INVALID_PARAM;
+}
+
+int launch_reduce(int epi, const Params& p, int64_t tokens, int64_t feats, cudaStream_t st) {
+  const int64_t n = tokens * (feats / 8);
+  const unsigned g = (unsigned)((n + 255) / 256);
+  switch (epi) {
+    case B200_EPI_NONE: splitk_reduce_kernel<B200_EPI_NONE><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    case B200_EPI_BIAS: splitk_reduce_kernel<B200_EPI_BIAS><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    case B200_EPI_RESIDUAL: splitk_reduce_kernel<B200_EPI_RESIDUAL><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    case B200_EPI_SWIGLU: splitk_reduce_kernel<B200_EPI_SWIGLU><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    case B200_EPI_BIAS_GELU: splitk_reduce_kernel<B200_EPI_BIAS_GELU><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    case B200_EPI_BIAS_RESIDUAL: splitk_reduce_kernel<B200_EPI_BIAS_RESIDUAL><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
+    default: return B200_ERROR_INVALID_PARAM;
+  }
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+}  // namespace
+
+namespace b200 {
+
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
+  GemmPlan g;
+  g.swap = M <= 128;
+  const int64_t mma_rows = g.swap ? N : M;
+  const int64_t mma_cols = g.swap ? M : N;
+  if (g.swap) g.bn = mma_cols <= 64 ? 64 : 128;
+  else g.bn = (mma_cols >= 2048 || mma_cols > 128) ? 256 : 128;
+  g.tiles_m = (int)((mma_rows + BM - 1) / BM);
+  g.tiles_n = (int)((mma_cols + g.bn - 1) / g.bn);
+  g.kb_total = (int)((K + BK - 1) / BK);
+  const int tiles = g.tiles_m * g.tiles_n;
+  // Split K only when the output tiles leave SMs idle: pick the split count
+  // (<= 16, >= 4 k-blocks per split) with the best wave efficiency.
+  int best = 1;
+  double best_eff = (double)tiles / ((double)sms * ((tiles + sms - 1) / sms));
+  if (tiles < 2 * sms) {
+    for (int s = 2; s <= 16; ++s) {
+      if (g.kb_total / s < 4) break;
+      const int u = tiles * s;
+      const double eff = (double)u / ((double)sms * ((u + sms - 1) / sms));
+      if (eff > best_eff + 0.05) {
+        best_eff = eff;
+        best = s;
+      }
+    }
+  }
+  g.splits = best;
+  g.kb_per_split = (g.kb_total + best - 1) / best;
+  g.splits = (g.kb_total + g.kb_per_split - 1) / g.kb_per_split;
+  g.ws_bytes = g.splits > 1 ? (int64_t)g.splits * M * N * (int64_t)sizeof(float) : 0;
+  (void)epilogue;
+  return g;
+}
+
+int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
+             int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
+             cudaStream_t st) {
+  if (!A || !B || !Cp || M < 0 || N < 0 || K <= 0) return B200_ERROR_INVALID_PARAM;
+  if (epi < B200_EPI_NONE || epi > B200_EPI_BIAS_RESIDUAL) return B200_ERROR_INVALID_PARAM;
+  if (K % 8 || lda % 8 || ldb % 8 || ldc % 8 || lda < K || ldb < K || N % 8) return B200_ERROR_INVALID_PARAM;
+  const int64_t outN = epi == B200_EPI_SWIGLU ? N / 2 : N;
+  if (epi == B200_EPI_SWIGLU && N % 16) return B200_ERROR_INVALID_PARAM;
+  if (ldc < outN) return B200_ERROR_INVALID_PARAM;
+  const bool needs_bias = epi == B200_EPI_BIAS || epi == B200_EPI_BIAS_GELU || epi == B200_EPI_BIAS_RESIDUAL;
+  const bool needs_res = epi == B200_EPI_RESIDUAL || epi == B200_EPI_BIAS_RESIDUAL;
+  if ((needs_bias && !bias) || (needs_res && (!R || ldr % 8 || ldr < N))) return B200_ERROR_INVALID_PARAM;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(A) || !al(B) || !al(Cp) || (bias && !al(bias)) || (R && !al(R)) || (ws && !al(ws)))
+    return B200_ERROR_INVALID_PARAM;
+  if (M == 0 || N == 0) return B200_OK;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return B200_ERROR_UNSUPPORTED;
+
+  const int sms = num_sms();
+  GemmPlan g = plan_gemm(M, N, K, epi, sms);
+  if (g.splits > 1 && (!ws || ws_bytes < g.ws_bytes)) {
+    g.splits = 1;
+    g.kb_per_split = g.kb_total;
+  }
+  Params p;
+  p.rows = g.swap ? N : M;
+  p.cols = g.swap ? M : N;
+  p.K = K;
+  p.tiles_m = g.tiles_m;
+  p.tiles_n = g.tiles_n;
+  p.splits = g.splits;
+  p.kb_total = g.kb_total;
+  p.kb_per_split = g.kb_per_split;
+  p.C = static_cast<__nv_bfloat16*>(Cp);
+  p.ldc = ldc;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.R = static_cast<const __nv_bfloat16*>(R);
+  p.ldr = ldr;
+  p.ws = static_cast<float*>(ws);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  p.err = error_word(dev);
+
+  CUtensorMap ta, tb;
+  const void* mA = g.swap ? B : A;  // operand on the 128-row MMA side
+  const void* mB = g.swap ? A : B;
+  const int64_t ldmA = g.swap ? ldb : lda, ldmB = g.swap ? lda : ldb;
+  if (!make_tmap(&ta, mA, p.rows, K, ldmA, BM) || !make_tmap(&tb, mB, p.cols, K, ldmB, g.bn))
+    return B200_ERROR_UNSUPPORTED;
+  const int units = g.tiles_m * g.tiles_n * g.splits;
+  const int grid = std::min(units, sms);
+  const bool partial = g.splits > 1;
+  int rc;
+  if (g.bn == 256) {
+    rc = partial ? launch_epi<256, false, true>(epi, ta, tb, p, grid, st) : launch_epi<256, false, false>(epi, ta, tb, p, grid, st);
+  } else if (g.bn == 128) {
+    if (g.swap)
+      rc = partial ? launch_epi<128, true, true>(epi, ta, tb, p, grid, st) : launch_epi<128, true, false>(epi, ta, tb, p, grid, st);
+    else
+      rc = partial ? launch_epi<128, false, true>(epi, ta, tb, p, grid, st) : launch_epi<128, false, false>(epi, ta, tb, p, grid, st);
+  } else {
+    rc = partial ? launch_epi<64, true, true>(epi, ta, tb, p, grid, st) : launch_epi<64, true, false>(epi, ta, tb, p, grid, st);
+  }
+  if (rc != B200_OK || !partial) return rc;
+  return launch_reduce(epi, p, M, N, st);
+}
+
+}  // namespace b200
+
+extern "C" int b200_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                              int64_t N, int64_t K, int epilogue, const void* bias, const void* residual, int64_t ldr,
+                              void* workspace, int64_t workspace_bytes, b200_stream_t stream) {
+  return b200::gemm_run(A, lda, B, ldb, C, ldc, M, N, K, epilogue, bias, residual, ldr, workspace, workspace_bytes,
+                        stream);
+}
+
+extern "C" int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int epilogue) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return b200::plan_gemm(M, N, K, epilogue, num_sms()).ws_bytes;
+}

@@ -1,0 +1,188 @@
+/*
+ * b200_llm.h — C ABI of the B200 (sm_100a) transformer-layer library.
+ *
+ * Every entry point takes raw device pointers, int64 sizes/strides and a CUDA
+ * stream, launches asynchronously on that stream and returns an int status
+ * (B200_OK or a negative code; shape / alignment violations return
+ * B200_ERROR_INVALID_PARAM and launch nothing).  No C++ or torch types cross
+ * this boundary and no exception escapes it.
+ *
+ * Storage type is bf16 (passed as void*); accumulation is fp32.  Each
+ * declaration names the reference interface it replaces: the reference
+ * (atb_cpp_llm) builds these steps from closed ATB operators created in
+ * atb_cpp_llm/src/ops/*.cpp and wired by the graph builders in
+ * atb_cpp_llm/src/components/.
+ */
+#ifndef B200_LLM_H_
+#define B200_LLM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+typedef struct CUstream_st* b200_stream_t; /* == cudaStream_t */
+
+/* Status codes mirror atb_llm::Status (atb_cpp_llm/include/atb_llm/types.h:76-86);
+ * a CUDA error e is reported as B200_ERROR_CUDA_BASE - e, the way the reference
+ * adds the backend's code to ERROR_ATB_BASE (atb_cpp_llm/src/core/context_manager.cpp:97). */
+enum b200_status {
+  B200_OK = 0,
+  B200_ERROR_INVALID_PARAM = -1,
+  B200_ERROR_FILE_NOT_FOUND = -2,
+  B200_ERROR_WEIGHT_LOAD = -3,
+  B200_ERROR_GRAPH_BUILD = -4,
+  B200_ERROR_DEVICE_MEMORY = -5,
+  B200_ERROR_INFERENCE = -6,
+  B200_ERROR_UNSUPPORTED = -7,
+  B200_ERROR_CUDA_BASE = -1000
+};
+
+/* ---------------------------------------------------------------- library */
+
+/* ABI version of this header (major*100 + minor). */
+B200_API int b200_abi_version(void);
+
+/* Read (and optionally clear) the device error word of the current device:
+ * bit 0 = a bounded device wait timed out, bit 1 = a device-side index check
+ * failed.  Synchronises `stream`.  No reference counterpart: the reference
+ * relies on ATB's own status codes (atb_cpp_llm/include/atb_llm/types.h:76-86). */
+B200_API int b200_device_error_read(unsigned* out_bits, int clear, b200_stream_t stream);
+
+/* ------------------------------------------------------------ norms / rope */
+
+/* RMSNorm over the last dim, optionally fused with a residual add.
+ *   residual == NULL : out = rmsnorm(x) * w                       (NORM)
+ *   residual != NULL : h = x + residual; out = rmsnorm(h) * w;
+ *                      residual_out (if not NULL) = h              (PRENORM / POSTNORM)
+ * x / residual / residual_out / out are [rows, dim] with row stride `stride`
+ * (elements); residual_out may alias residual.  dim % 8 == 0.
+ * Replaces RmsNormOp::Create (atb_cpp_llm/src/ops/rms_norm_op.cpp:7-19) and
+ * RmsNormGraph::Build (atb_cpp_llm/src/components/common/rms_norm_graph.cpp:59-84). */
+B200_API int b200_rmsnorm(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                 int64_t rows, int64_t dim, int64_t stride, float eps, b200_stream_t stream);
+
+/* LayerNorm with gamma/beta over the last dim ([rows, dim], contiguous, dim % 8 == 0).
+ * Replaces LayerNormOp::Create (atb_cpp_llm/src/ops/layer_norm_op.cpp:7-22). */
+B200_API int b200_layernorm(const void* x, const void* gamma, const void* beta, void* out, int64_t rows, int64_t dim,
+                   float eps, b200_stream_t stream);
+
+/* cos/sin tables [T, head_dim] (fp32) for interleaved 3-section mrope from
+ * position ids [3, T] (int64, planes t, h, w).
+ * Replaces MRoPE::Compute (atb_cpp_llm/src/components/common/mrope.cpp:27-96). */
+B200_API int b200_rope_table_mrope(const int64_t* position_ids, int64_t T, int head_dim, float theta, int section_t,
+                          int section_h, int section_w, float* cos_out, float* sin_out, b200_stream_t stream);
+
+/* cos/sin tables [T, head_dim] (fp32) for standard 1-D rope from positions [T].
+ * Replaces Rope1D::Compute (atb_cpp_llm/src/components/common/rope_1d.h:23-167). */
+B200_API int b200_rope_table_1d(const int64_t* positions, int64_t T, int head_dim, float theta, float* cos_out,
+                       float* sin_out, b200_stream_t stream);
+
+/* In place on the fused projection output qkv [T, row_stride] laid out as
+ * [q heads | k heads | v heads] x head_dim: per-head RMSNorm of q and k
+ * (skipped when the norm weight is NULL), then the half rotation
+ * x*cos + cat(-x2, x1)*sin with cos/sin [T, head_dim] fp32.  When
+ * slot_mapping is not NULL, the rotated k and the untouched v of token t are
+ * also written to k_cache / v_cache ([num_blocks, nkv, block_size, head_dim])
+ * at slot slot_mapping[t] (negative slot = skip).
+ * Replaces the RmsNorm -> Rope steps of GqaAttentionBuilder::Build
+ * (atb_cpp_llm/src/components/common/gqa_attention_builder.cpp:60-130) and
+ * RopeOp::Create(rotaryCoeff=2) (atb_cpp_llm/src/ops/rope_op.cpp:7-18). */
+B200_API int b200_qk_norm_rope(void* qkv, int64_t T, int nq, int nkv, int head_dim, int64_t row_stride,
+                      const void* q_norm_w, const void* k_norm_w, float eps, const float* cos_tab,
+                      const float* sin_tab, const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                      int64_t num_blocks, int block_size, b200_stream_t stream);
+
+/* ------------------------------------------------------------------- GEMM */
+
+enum b200_epilogue {
+  B200_EPI_NONE = 0,          /* C = A B^T                                   */
+  B200_EPI_BIAS = 1,          /* C = A B^T + bias[n]                         */
+  B200_EPI_RESIDUAL = 2,      /* C = A B^T + R[m, n]   (R may alias C)       */
+  B200_EPI_SWIGLU = 3,        /* rows of B interleave gate/up: C[m, j] = silu(G[m,2j]) * G[m,2j+1], C is [M, N/2] */
+  B200_EPI_BIAS_GELU = 4,     /* C = gelu_tanh(A B^T + bias[n])              */
+  B200_EPI_BIAS_RESIDUAL = 5  /* C = A B^T + bias[n] + R[m, n]               */
+};
+
+/* C[M, N] = epilogue(A[M, K] * B[N, K]^T), bf16 in / fp32 accumulate / bf16 out,
+ * on tcgen05 tensor cores with TMEM accumulators and TMA-fed shared memory.
+ * Row strides lda/ldb/ldc/ldr in elements; K, lda, ldb, ldc, ldr multiples of 8;
+ * 16-byte aligned base pointers.  `workspace` (may be NULL) enables split-K
+ * for skinny problems; b200_gemm_workspace_bytes() gives the size it can use.
+ * Replaces LinearOp::Create(transB=true) (atb_cpp_llm/src/ops/linear_op.cpp:7-20)
+ * and the SiLU/Mul/Add ops fused into its consumers
+ * (atb_cpp_llm/src/components/common/mlp_builder.cpp:12-56). */
+B200_API int b200_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                   int64_t N, int64_t K, int epilogue, const void* bias, const void* residual, int64_t ldr,
+                   void* workspace, int64_t workspace_bytes, b200_stream_t stream);
+
+/* Bytes of workspace b200_gemm_bf16 uses for split-K at this shape (0 = none). */
+B200_API int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int epilogue);
+
+/* -------------------------------------------------------------- attention */
+
+/* Prefill attention over packed sequences: softmax(q k^T * scale [+ causal]) v,
+ * GQA with nq % nkv == 0.  Sequence i owns rows cu_seqlens[i]..cu_seqlens[i+1]
+ * of q [T, q_stride], k/v [T, kv_stride] (head h at column h*head_dim) and of
+ * out [T, out_stride].  head_dim in {32, 64, 128}.  The causal rule (key j
+ * masked for query i when j > i) is applied in-kernel; no S x S mask exists.
+ * Replaces SelfAttentionOp::Create (PA_ENCODER, BSND, MASK_TYPE_NORM)
+ * (atb_cpp_llm/src/ops/self_attention_op.cpp:8-30) fed by
+ * MakeCausalMaskFp16 (atb_cpp_llm/src/runners/text_runner.cpp:74-85). */
+B200_API int b200_flash_prefill(const void* q, int64_t q_stride, const void* k, const void* v, int64_t kv_stride,
+                       void* out, int64_t out_stride, const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
+                       int nq, int nkv, int head_dim, float scale, int causal, b200_stream_t stream);
+
+/* Single-token decode attention over a paged KV cache
+ * (k_cache/v_cache [num_blocks, nkv, block_size, head_dim], block_size 128 or 64):
+ * sequence b attends to its first context_lens[b] cached positions through
+ * block_tables[b, 0..max_blocks_per_seq).  q [batch, q_stride] (head h at h*head_dim),
+ * out [batch, out_stride].  head_dim == 128.  Uses split-KV with `workspace`
+ * (size from b200_paged_decode_workspace_bytes; NULL disables splitting).
+ * No reference counterpart: the reference's KV cache is a stub
+ * (atb_cpp_llm/include/atb_llm/kv_cache.h:23-35, atb_cpp_llm/src/core/kv_cache_manager.h:25-76). */
+B200_API int b200_paged_decode(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                      const int32_t* block_tables, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                      int nq, int nkv, int head_dim, int block_size, int64_t num_blocks, float scale, void* out,
+                      int64_t out_stride, void* workspace, int64_t workspace_bytes, int max_context,
+                      b200_stream_t stream);
+
+B200_API int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head_dim, int max_context);
+
+/* slots[t] = block_tables[seq_ids[t], positions[t] / block_size] * block_size
+ *            + positions[t] % block_size   (int64, bit-exact).
+ * No reference counterpart (the reference has no paged KV cache,
+ * atb_cpp_llm/include/atb_llm/kv_cache.h:23-35). */
+B200_API int b200_slot_mapping(const int32_t* block_tables, int max_blocks_per_seq, const int32_t* seq_ids,
+                      const int64_t* positions, int64_t T, int block_size, int64_t* slots, b200_stream_t stream);
+
+/* ------------------------------------------------------------ elementwise */
+
+/* out[t] = table[ids[t]] ([vocab, dim] bf16); ids outside [0, vocab) give zeros.
+ * Replaces BaseModel::EmbeddingLookup (atb_cpp_llm/src/families/base_model.cpp:99-116),
+ * which the reference runs on the host. */
+B200_API int b200_embedding(const int64_t* ids, int64_t T, const void* table, int64_t vocab, int64_t dim, void* out,
+                   b200_stream_t stream);
+
+/* hidden[idx[i], :] += alpha * feat[i, :] for i < n (hidden [rows, dim]); indices
+ * must be unique.  Replaces IndexAddOp (atb_cpp_llm/src/ops/index_add_op.cpp:7-19)
+ * as used by DeepstackFusion::InjectFeatures
+ * (atb_cpp_llm/src/components/common/deepstack_fusion.cpp:188-195). */
+B200_API int b200_scatter_add_rows(void* hidden, int64_t rows, int64_t dim, const int32_t* idx, const void* feat, int64_t n,
+                          float alpha, b200_stream_t stream);
+
+/* out[r] = argmax_j logits[r, j] (lowest index on ties), logits [rows, vocab] bf16. */
+B200_API int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t ld, int64_t* out, b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_LLM_H_ */
