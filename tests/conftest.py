@@ -17,6 +17,13 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
 
 
+@pytest.fixture(autouse=True)
+def _release_device_buffers(request):
+    yield
+    if "gpu_util" in sys.modules:
+        sys.modules["gpu_util"].release()
+
+
 def load_fixture(name):
     return dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
 

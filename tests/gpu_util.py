@@ -17,21 +17,38 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+# Device tensors made by the helpers below stay referenced here until
+# release() (called after every test): a kernel is often handed
+# `bf16(x).data_ptr()`, and without this reference the temporary would go back
+# to torch's caching allocator — and be reused — before the kernel runs.
+_held = []
+
+
+def _keep(t):
+    _held.append(t)
+    return t
+
+
+def release():
+    torch.cuda.synchronize()
+    _held.clear()
+
+
 def bf16(a):
     """numpy fp32/fp16 -> bf16 device tensor (round to nearest even)."""
-    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(DEV).to(torch.bfloat16)
+    return _keep(torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(DEV).to(torch.bfloat16))
 
 
 def f32(a):
-    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(DEV)
+    return _keep(torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(DEV))
 
 
 def i64(a):
-    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.int64))).to(DEV)
+    return _keep(torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.int64))).to(DEV))
 
 
 def i32(a):
-    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.int32))).to(DEV)
+    return _keep(torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.int32))).to(DEV))
 
 
 def host(t):
