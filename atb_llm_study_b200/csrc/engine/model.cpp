@@ -1,0 +1,469 @@
+#include "engine/model.h"
+
+#include <cmath>
+#include <cstring>
+#include <set>
+
+#include "engine/engine_kernels.h"
+
+namespace b200 {
+unsigned* error_word(int device);
+}
+
+namespace b200llm {
+
+namespace {
+constexpr int B200_EPI_NONE_ = B200_EPI_NONE;
+bool starts_with(const std::string& s, const std::string& p) { return s.compare(0, p.size(), p) == 0; }
+}  // namespace
+
+// ---------------------------------------------------------------- config
+
+Status ModelConfig::FromJson(const JsonConfig& root, ModelConfig& c) {
+  if (!root.IsValid()) return ERROR_INVALID_PARAM;
+  c = ModelConfig();
+  c.model_type = root.GetString("model_type");
+  JsonConfig t = root;
+  if (root.HasKey("text_config")) t = root.GetSubConfig("text_config");
+  c.hidden = t.GetInt("hidden_size");
+  c.layers = t.GetInt("num_hidden_layers");
+  c.heads = t.GetInt("num_attention_heads");
+  c.kv_heads = t.GetInt("num_key_value_heads", c.heads);
+  c.head_dim = t.GetInt("head_dim", c.heads > 0 ? c.hidden / c.heads : 0);
+  c.intermediate = t.GetInt("intermediate_size");
+  c.vocab = t.GetInt64("vocab_size");
+  c.eps = t.GetFloat("rms_norm_eps", 1e-6f);
+  c.rope_theta = t.GetFloat("rope_theta", 1e6f);
+  c.tie_embeddings = root.GetBool("tie_word_embeddings", t.GetBool("tie_word_embeddings", false));
+  c.qk_norm = starts_with(c.model_type, "qwen3");
+  if (t.HasKey("rope_scaling")) {
+    JsonConfig rs = t.GetSubConfig("rope_scaling");
+    std::vector<int> sec = rs.GetIntArray("mrope_section");
+    if (sec.size() == 3) {
+      c.mrope = true;
+      for (int i = 0; i < 3; ++i) c.mrope_section[i] = sec[i];
+    }
+  }
+  if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.head_dim <= 0 ||
+      c.intermediate <= 0 || c.vocab <= 0)
+    return ERROR_INVALID_PARAM;
+  if (c.hidden % 8 || c.intermediate % 8 || c.head_dim != 128) return ERROR_UNSUPPORTED;
+  return STATUS_OK;
+}
+
+// ---------------------------------------------------------------- setup
+
+DecoderModel::~DecoderModel() {
+  if (ctx_) cudaSetDevice(ctx_->GetDeviceId());
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.second);
+  graphs_.clear();
+  if (ctx_) ctx_->Synchronize();
+  if (pinned_) cudaFreeHost(pinned_);
+  alloc_.reset();
+  ctx_.reset();
+}
+
+Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
+  cfg_ = cfg;
+  opt_ = opt;
+  if (opt.max_batch <= 0 || opt.max_context <= 0 || opt.max_prefill_tokens <= 0 ||
+      (opt.block_size != 64 && opt.block_size != 128))
+    return ERROR_INVALID_PARAM;
+  B200_RETURN_IF(ContextManager::Create(opt.device, ctx_));
+  alloc_.reset(new TensorAllocator(ctx_->GetStream()));
+  err_ = b200::error_word(opt.device);
+  const int64_t H = cfg.hidden, L = cfg.layers, hd = cfg.head_dim, I = cfg.intermediate, V = cfg.vocab;
+  const int64_t QKV = cfg.qkv_dim(), AO = (int64_t)cfg.heads * hd;
+  max_t_ = std::max<int64_t>(opt.max_prefill_tokens, opt.max_batch);
+  max_blocks_ = (opt.max_context + opt.block_size - 1) / opt.block_size;
+  num_blocks_ = (int64_t)opt.max_batch * max_blocks_;
+  auto A = [&](DeviceTensor& t, DType d, std::vector<int64_t> s) { return alloc_->Alloc(t, d, std::move(s)); };
+
+  B200_RETURN_IF(A(embed_, DType::BF16, {V, H}));
+  if (!cfg.tie_embeddings) B200_RETURN_IF(A(lm_head_, DType::BF16, {V, H}));
+  else lm_head_ = embed_;
+  B200_RETURN_IF(A(final_norm_, DType::BF16, {H}));
+  B200_RETURN_IF(A(wqkv_, DType::BF16, {L, QKV, H}));
+  B200_RETURN_IF(A(wo_, DType::BF16, {L, H, AO}));
+  B200_RETURN_IF(A(wgu_, DType::BF16, {L, 2 * I, H}));
+  B200_RETURN_IF(A(wdown_, DType::BF16, {L, H, I}));
+  B200_RETURN_IF(A(qnorm_, DType::BF16, {L, hd}));
+  B200_RETURN_IF(A(knorm_, DType::BF16, {L, hd}));
+  B200_RETURN_IF(A(iln_, DType::BF16, {L, H}));
+  B200_RETURN_IF(A(pln_, DType::BF16, {L, H}));
+  weight_bytes_ = alloc_->BytesInUse();
+
+  B200_RETURN_IF(A(kv_, DType::BF16, {L, 2, num_blocks_, cfg.kv_heads, opt.block_size, hd}));
+  kv_bytes_ = kv_.bytes();
+  // finite contents everywhere: tiles past a sequence's end are read (and masked)
+  B200_RETURN_IF(FromCuda(cudaMemsetAsync(kv_.data, 0, kv_.bytes(), ctx_->GetStream())));
+  B200_RETURN_IF(A(block_tables_, DType::INT32, {opt.max_batch, max_blocks_}));
+  B200_RETURN_IF(A(ctx_lens_, DType::INT32, {opt.max_batch}));
+  {
+    // slot s owns blocks [s * max_blocks, (s + 1) * max_blocks)
+    std::vector<int32_t> bt((size_t)opt.max_batch * max_blocks_);
+    for (size_t i = 0; i < bt.size(); ++i) bt[i] = (int32_t)i;
+    B200_RETURN_IF(alloc_->CopyToDevice(block_tables_, bt.data(), bt.size() * 4));
+  }
+  host_ctx_.assign(opt.max_batch, 0);
+  B200_RETURN_IF(FromCuda(cudaMemsetAsync(ctx_lens_.data, 0, ctx_lens_.bytes(), ctx_->GetStream())));
+
+  B200_RETURN_IF(A(ids_, DType::INT64, {max_t_}));
+  B200_RETURN_IF(A(hidden_, DType::BF16, {max_t_, H}));
+  B200_RETURN_IF(A(normed_, DType::BF16, {max_t_, H}));
+  B200_RETURN_IF(A(qkv_, DType::BF16, {max_t_, QKV}));
+  B200_RETURN_IF(A(attn_, DType::BF16, {max_t_, AO}));
+  B200_RETURN_IF(A(act_, DType::BF16, {max_t_, I}));
+  B200_RETURN_IF(A(cos_, DType::FP32, {max_t_, hd}));
+  B200_RETURN_IF(A(sin_, DType::FP32, {max_t_, hd}));
+  B200_RETURN_IF(A(pos_, DType::INT64, {3, max_t_}));
+  B200_RETURN_IF(A(slots_, DType::INT64, {max_t_}));
+  B200_RETURN_IF(A(cu_, DType::INT32, {opt.max_batch + 1}));
+  B200_RETURN_IF(A(last_idx_, DType::INT32, {opt.max_batch}));
+  B200_RETURN_IF(A(last_hidden_, DType::BF16, {opt.max_batch, H}));
+  B200_RETURN_IF(A(logits_, DType::BF16, {opt.max_batch, V}));
+  B200_RETURN_IF(A(next_, DType::INT64, {opt.max_batch}));
+  B200_RETURN_IF(A(seq_slots_, DType::INT32, {opt.max_batch}));
+  B200_RETURN_IF(A(ctx_batch_, DType::INT32, {opt.max_batch}));
+  B200_RETURN_IF(A(bt_batch_, DType::INT32, {opt.max_batch, max_blocks_}));
+
+  // split-K workspace: the largest any decode-sized projection asks for
+  int64_t ws = 0;
+  const int64_t shapes[5][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}};
+  for (int64_t m : {(int64_t)1, (int64_t)opt.max_batch})
+    for (auto& s : shapes) ws = std::max(ws, b200_gemm_workspace_bytes(m, s[0], s[1], B200_EPI_NONE_));
+  gemm_ws_bytes_ = ws;
+  if (ws > 0) B200_RETURN_IF(A(gemm_ws_, DType::FP32, {(ws + 3) / 4}));
+  attn_ws_bytes_ = b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
+  if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
+
+  pinned_bytes_ = (size_t)max_t_ * 8 * 5 + (size_t)(opt.max_batch + 1) * 16 + 4096;
+  B200_RETURN_IF(FromCuda(cudaMallocHost(&pinned_, pinned_bytes_)));
+  return ctx_->Synchronize();
+}
+
+Status DecoderModel::InitRandomWeights(uint64_t seed, float std) {
+  cudaStream_t st = ctx_->GetStream();
+  uint64_t k = seed * 1000003ull;
+  auto N = [&](DeviceTensor& t) { return FillNormalBf16(t.data, t.numel(), 0.f, std, ++k, st); };
+  auto O = [&](DeviceTensor& t) { return FillConstBf16(t.data, t.numel(), 1.f, st); };
+  B200_RETURN_IF(N(embed_));
+  if (!cfg_.tie_embeddings) B200_RETURN_IF(N(lm_head_));
+  B200_RETURN_IF(N(wqkv_));
+  B200_RETURN_IF(N(wo_));
+  B200_RETURN_IF(N(wgu_));
+  B200_RETURN_IF(N(wdown_));
+  B200_RETURN_IF(O(final_norm_));
+  B200_RETURN_IF(O(qnorm_));
+  B200_RETURN_IF(O(knorm_));
+  B200_RETURN_IF(O(iln_));
+  B200_RETURN_IF(O(pln_));
+  return ctx_->Synchronize();
+}
+
+Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DType dtype, int64_t numel) {
+  if (!host || numel <= 0) return ERROR_INVALID_PARAM;
+  std::string name = name_in;
+  if (starts_with(name, "model.language_model.")) name = "model." + name.substr(21);
+  std::vector<uint16_t> b16;
+  const char* dt = dtype == DType::BF16 ? "BF16" : dtype == DType::FP16 ? "F16" : dtype == DType::FP32 ? "F32" : "";
+  B200_RETURN_IF(ToBf16(static_cast<const uint8_t*>(host), dt, (size_t)numel, b16));
+  const int64_t H = cfg_.hidden, hd = cfg_.head_dim, I = cfg_.intermediate, QKV = cfg_.qkv_dim();
+  const int64_t AO = (int64_t)cfg_.heads * hd;
+  cudaStream_t st = ctx_->GetStream();
+  auto put = [&](const DeviceTensor& t, int64_t elem_off, int64_t expect) -> Status {
+    if (numel != expect) return ERROR_INVALID_PARAM;
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(static_cast<uint16_t*>(t.data) + elem_off, b16.data(),
+                                            (size_t)numel * 2, cudaMemcpyHostToDevice, st)));
+    return ctx_->Synchronize();
+  };
+  if (name == "model.embed_tokens.weight") {
+    Status s = put(embed_, 0, cfg_.vocab * H);
+    return s;
+  }
+  if (name == "lm_head.weight") {
+    if (cfg_.tie_embeddings) return STATUS_OK;
+    return put(lm_head_, 0, cfg_.vocab * H);
+  }
+  if (name == "model.norm.weight") return put(final_norm_, 0, H);
+  const std::string pre = "model.layers.";
+  if (!starts_with(name, pre)) return ERROR_WEIGHT_LOAD;
+  size_t dot = name.find('.', pre.size());
+  if (dot == std::string::npos) return ERROR_WEIGHT_LOAD;
+  const int l = std::atoi(name.substr(pre.size(), dot - pre.size()).c_str());
+  if (l < 0 || l >= cfg_.layers) return ERROR_WEIGHT_LOAD;
+  const std::string leaf = name.substr(dot + 1);
+  const int64_t nq = (int64_t)cfg_.heads * hd, nk = (int64_t)cfg_.kv_heads * hd;
+  if (leaf == "self_attn.q_proj.weight") return put(wqkv_, (int64_t)l * QKV * H, nq * H);
+  if (leaf == "self_attn.k_proj.weight") return put(wqkv_, (int64_t)l * QKV * H + nq * H, nk * H);
+  if (leaf == "self_attn.v_proj.weight") return put(wqkv_, (int64_t)l * QKV * H + (nq + nk) * H, nk * H);
+  if (leaf == "self_attn.o_proj.weight") return put(wo_, (int64_t)l * H * AO, H * AO);
+  if (leaf == "self_attn.q_norm.weight") return put(qnorm_, (int64_t)l * hd, hd);
+  if (leaf == "self_attn.k_norm.weight") return put(knorm_, (int64_t)l * hd, hd);
+  if (leaf == "input_layernorm.weight") return put(iln_, (int64_t)l * H, H);
+  if (leaf == "post_attention_layernorm.weight") return put(pln_, (int64_t)l * H, H);
+  if (leaf == "mlp.down_proj.weight") return put(wdown_, (int64_t)l * H * I, H * I);
+  if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight") {
+    // rows 2j / 2j+1 of the fused matrix hold gate[j] / up[j] (SwiGLU epilogue layout)
+    if (numel != I * H) return ERROR_INVALID_PARAM;
+    uint16_t* dst = static_cast<uint16_t*>(wgu_.data) + (int64_t)l * 2 * I * H + (leaf[4] == 'u' ? H : 0);
+    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(dst, (size_t)2 * H * 2, b16.data(), (size_t)H * 2, (size_t)H * 2,
+                                              (size_t)I, cudaMemcpyHostToDevice, st)));
+    return ctx_->Synchronize();
+  }
+  return ERROR_WEIGHT_LOAD;
+}
+
+Status DecoderModel::LoadSafetensors(const SafetensorsReader& r, const std::string& prefix) {
+  for (const std::string& key : r.GetAllKeys()) {
+    if (!prefix.empty() && !starts_with(key, prefix)) continue;
+    WeightInfo w;
+    B200_RETURN_IF(r.GetTensor(key, w));
+    DType dt;
+    if (w.dtype == "BF16") dt = DType::BF16;
+    else if (w.dtype == "F16") dt = DType::FP16;
+    else if (w.dtype == "F32") dt = DType::FP32;
+    else continue;
+    int64_t numel = 1;
+    for (auto s : w.shape) numel *= s;
+    Status s = SetWeight(key, r.GetTensorData(key), dt, numel);
+    if (s == ERROR_WEIGHT_LOAD) continue;  // not a decoder weight (e.g. vision tower)
+    B200_RETURN_IF(s);
+  }
+  return STATUS_OK;
+}
+
+Status DecoderModel::ResetSlots() {
+  std::fill(host_ctx_.begin(), host_ctx_.end(), 0);
+  B200_RETURN_IF(FromCuda(cudaMemsetAsync(ctx_lens_.data, 0, ctx_lens_.bytes(), ctx_->GetStream())));
+  return ctx_->Synchronize();
+}
+
+// ---------------------------------------------------------------- forward
+
+Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, hd = cfg_.head_dim, I = cfg_.intermediate, QKV = cfg_.qkv_dim();
+  const int64_t AO = (int64_t)cfg_.heads * hd;
+  const int nq = cfg_.heads, nkv = cfg_.kv_heads, L = cfg_.layers;
+  const float scale = 1.0f / std::sqrt((float)hd);
+  auto gemm = [&](const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
+                  int64_t K, int epi, const void* R, int64_t ldr) {
+    return b200_gemm_bf16(A, lda, B, ldb, C, ldc, M, N, K, epi, nullptr, R, ldr, gemm_ws_.data, gemm_ws_bytes_, st);
+  };
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;
+  for (int l = 0; l < L; ++l) {
+    if (l == 0)
+      B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, 0), normed_.data, nullptr, T, H, H, cfg_.eps, st));
+    B200_RETURN_IF(gemm(normed_.data, H, bf(wqkv_, (int64_t)l * QKV * H), H, qkv_.data, QKV, T, QKV, H,
+                        B200_EPI_NONE, nullptr, 0));
+    uint16_t* kc = bf(kv_, (int64_t)l * kv_layer);
+    uint16_t* vc = kc + kv_layer / 2;
+    B200_RETURN_IF(b200_qk_norm_rope(qkv_.data, T, nq, nkv, (int)hd, QKV, cfg_.qk_norm ? bf(qnorm_, l * hd) : nullptr,
+                                     cfg_.qk_norm ? bf(knorm_, l * hd) : nullptr, cfg_.eps, cos_.as<float>(),
+                                     sin_.as<float>(), slots_.as<int64_t>(), kc, vc, num_blocks_, opt_.block_size,
+                                     st));
+    uint16_t* q = static_cast<uint16_t*>(qkv_.data);
+    if (!decode) {
+      B200_RETURN_IF(b200_flash_prefill(q, QKV, q + nq * hd, q + (nq + nkv) * hd, QKV, attn_.data, AO,
+                                        cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, nq, nkv, (int)hd, scale, 1,
+                                        st));
+    } else {
+      B200_RETURN_IF(b200_paged_decode(q, QKV, kc, vc, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(),
+                                       batch, nq, nkv, (int)hd, opt_.block_size, num_blocks_, scale, attn_.data, AO,
+                                       attn_ws_.data, attn_ws_bytes_, opt_.max_context, st));
+    }
+    B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, T, H, AO,
+                           B200_EPI_RESIDUAL, hidden_.data, H));
+    B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(pln_, (int64_t)l * H), normed_.data, nullptr, T, H, H,
+                                cfg_.eps, st));
+    B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, (int64_t)l * 2 * I * H), H, act_.data, I, T, 2 * I, H,
+                           B200_EPI_SWIGLU, nullptr, 0));
+    B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, (int64_t)l * H * I), I, hidden_.data, H, T, H, I,
+                           B200_EPI_RESIDUAL, hidden_.data, H));
+    if (l + 1 < L)
+      B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, (int64_t)(l + 1) * H), normed_.data, nullptr, T, H,
+                                  H, cfg_.eps, st));
+  }
+  return STATUS_OK;
+}
+
+Status DecoderModel::Head(int64_t rows, bool gather, int64_t* next_tokens, bool next_on_device, void* logits) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, V = cfg_.vocab;
+  const void* src = hidden_.data;
+  if (gather) {
+    B200_RETURN_IF(GatherRows(hidden_.data, last_idx_.as<int32_t>(), rows, H, last_hidden_.data, st));
+    src = last_hidden_.data;
+  }
+  B200_RETURN_IF(b200_rmsnorm(src, nullptr, final_norm_.data, normed_.data, nullptr, rows, H, H, cfg_.eps, st));
+  B200_RETURN_IF(b200_gemm_bf16(normed_.data, H, lm_head_.data, H, logits_.data, V, rows, V, H, B200_EPI_NONE, nullptr,
+                                nullptr, 0, gemm_ws_.data, gemm_ws_bytes_, st));
+  B200_RETURN_IF(b200_argmax(logits_.data, rows, V, V, next_.as<int64_t>(), st));
+  (void)next_tokens;
+  (void)next_on_device;
+  (void)logits;
+  return STATUS_OK;
+}
+
+Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32_t* seq_lens, const int32_t* slots,
+                             int num_seqs, const int64_t* position_ids, int64_t* next_tokens, bool next_on_device,
+                             void* logits) {
+  if (!ids || !seq_lens || !slots || !next_tokens || num_seqs <= 0 || num_seqs > opt_.max_batch)
+    return ERROR_INVALID_PARAM;
+  int64_t T = 0;
+  int max_len = 0;
+  std::set<int> seen;
+  for (int i = 0; i < num_seqs; ++i) {
+    if (seq_lens[i] <= 0 || seq_lens[i] > opt_.max_context) return ERROR_INVALID_PARAM;
+    if (slots[i] < 0 || slots[i] >= opt_.max_batch || !seen.insert(slots[i]).second) return ERROR_INVALID_PARAM;
+    T += seq_lens[i];
+    max_len = std::max(max_len, seq_lens[i]);
+  }
+  if (T > max_t_) return ERROR_INVALID_PARAM;
+  cudaStream_t st = ctx_->GetStream();
+  // host-side metadata staged in pinned memory
+  uint8_t* pin = static_cast<uint8_t*>(pinned_);
+  int64_t* h_pos = reinterpret_cast<int64_t*>(pin);
+  int64_t* h_slot = h_pos + 3 * T;
+  int32_t* h_cu = reinterpret_cast<int32_t*>(h_slot + T);
+  int32_t* h_last = h_cu + num_seqs + 1;
+  int64_t* h_ids = reinterpret_cast<int64_t*>(pin + ((((uint8_t*)(h_last + num_seqs) - pin) + 15) / 16) * 16);
+  int64_t t = 0;
+  h_cu[0] = 0;
+  for (int i = 0; i < num_seqs; ++i) {
+    for (int j = 0; j < seq_lens[i]; ++j, ++t) {
+      for (int p = 0; p < 3; ++p) h_pos[p * T + t] = position_ids ? position_ids[p * T + t] : j;
+      h_slot[t] = (int64_t)slots[i] * max_blocks_ * opt_.block_size + j;  // block j/bs of slot i's table, offset j%bs
+    }
+    h_cu[i + 1] = (int32_t)t;
+    h_last[i] = (int32_t)(t - 1);
+  }
+  if (!ids_on_device) std::memcpy(h_ids, ids, (size_t)T * 8);
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(pos_.data, h_pos, (size_t)3 * T * 8, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(slots_.data, h_slot, (size_t)T * 8, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(cu_.data, h_cu, (size_t)(num_seqs + 1) * 4, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(last_idx_.data, h_last, (size_t)num_seqs * 4, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(ids_.data, ids_on_device ? (const void*)ids : (const void*)h_ids,
+                                          (size_t)T * 8, ids_on_device ? cudaMemcpyDeviceToDevice
+                                                                       : cudaMemcpyHostToDevice, st)));
+  for (int i = 0; i < num_seqs; ++i) host_ctx_[slots[i]] = seq_lens[i];
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(ctx_lens_.data, host_ctx_.data(), host_ctx_.size() * 4,
+                                          cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(ctx_->Synchronize());  // pinned staging is reused by the next call
+  cur_num_seqs_ = num_seqs;
+  cur_max_len_ = max_len;
+
+  const int hd = cfg_.head_dim;
+  if (cfg_.mrope)
+    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cfg_.mrope_section[0],
+                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
+                                         sin_.as<float>(), st));
+  else
+    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
+                                      st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), T, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  B200_RETURN_IF(RunLayers(T, false, 0));
+  B200_RETURN_IF(Head(num_seqs, true, next_tokens, next_on_device, logits));
+  if (logits)
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(logits, logits_.data, (size_t)num_seqs * cfg_.vocab * 2,
+                                            cudaMemcpyDeviceToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(next_tokens, next_.data, (size_t)num_seqs * 8,
+                                          next_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st)));
+  if (!next_on_device) B200_RETURN_IF(ctx_->Synchronize());
+  return FromCuda(cudaGetLastError());
+}
+
+Status DecoderModel::DecodeDevice(int batch) {
+  cudaStream_t st = ctx_->GetStream();
+  B200_RETURN_IF(DecodePrepare(seq_slots_.as<int32_t>(), batch, ctx_lens_.as<int32_t>(), block_tables_.as<int32_t>(),
+                               max_blocks_, opt_.block_size, pos_.as<int64_t>(), slots_.as<int64_t>(),
+                               ctx_batch_.as<int32_t>(), bt_batch_.as<int32_t>(), err_, st));
+  const int hd = cfg_.head_dim;
+  if (cfg_.mrope)
+    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), batch, hd, cfg_.rope_theta, cfg_.mrope_section[0],
+                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
+                                         sin_.as<float>(), st));
+  else
+    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), batch, hd, cfg_.rope_theta, cos_.as<float>(),
+                                      sin_.as<float>(), st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), batch, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  B200_RETURN_IF(RunLayers(batch, true, batch));
+  return Head(batch, false, nullptr, true, nullptr);
+}
+
+Status DecoderModel::Decode(const int64_t* ids, bool ids_on_device, const int32_t* slots, int batch,
+                            int64_t* next_tokens, bool next_on_device, void* logits) {
+  if (!ids || !slots || !next_tokens || batch <= 0 || batch > opt_.max_batch) return ERROR_INVALID_PARAM;
+  std::set<int> seen;
+  for (int i = 0; i < batch; ++i) {
+    if (slots[i] < 0 || slots[i] >= opt_.max_batch || !seen.insert(slots[i]).second) return ERROR_INVALID_PARAM;
+    if (host_ctx_[slots[i]] <= 0) return ERROR_INVALID_PARAM;  // slot holds no prefilled sequence
+    if (host_ctx_[slots[i]] + 1 > opt_.max_context) return ERROR_INVALID_PARAM;
+  }
+  cudaStream_t st = ctx_->GetStream();
+  uint8_t* pin = static_cast<uint8_t*>(pinned_);
+  int32_t* h_slots = reinterpret_cast<int32_t*>(pin);
+  int64_t* h_ids = reinterpret_cast<int64_t*>(pin + ((batch * 4 + 15) / 16) * 16);
+  int64_t* h_next = h_ids + batch;
+  std::memcpy(h_slots, slots, (size_t)batch * 4);
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(seq_slots_.data, h_slots, (size_t)batch * 4, cudaMemcpyHostToDevice, st)));
+  if (ids_on_device) {
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(ids_.data, ids, (size_t)batch * 8, cudaMemcpyDeviceToDevice, st)));
+  } else {
+    std::memcpy(h_ids, ids, (size_t)batch * 8);
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(ids_.data, h_ids, (size_t)batch * 8, cudaMemcpyHostToDevice, st)));
+  }
+  static const bool no_graph = EnvInt("B200_DISABLE_GRAPHS", 0) != 0;
+  auto it = graphs_.find(batch);
+  if (it != graphs_.end()) {
+    B200_RETURN_IF(FromCuda(cudaGraphLaunch(it->second, st)));
+  } else if (!no_graph && ++decode_calls_[batch] >= 2) {
+    B200_RETURN_IF(FromCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed)));
+    Status s = DecodeDevice(batch);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (s != STATUS_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return s != STATUS_OK ? s : FromCuda(e);
+    }
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    B200_RETURN_IF(FromCuda(e));
+    graphs_[batch] = ex;
+    B200_RETURN_IF(FromCuda(cudaGraphLaunch(ex, st)));
+  } else {
+    B200_RETURN_IF(DecodeDevice(batch));
+  }
+  for (int i = 0; i < batch; ++i) host_ctx_[slots[i]] += 1;
+  if (logits)
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(logits, logits_.data, (size_t)batch * cfg_.vocab * 2,
+                                            cudaMemcpyDeviceToDevice, st)));
+  if (next_on_device) {
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(next_tokens, next_.data, (size_t)batch * 8, cudaMemcpyDeviceToDevice, st)));
+    return STATUS_OK;
+  }
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(h_next, next_.data, (size_t)batch * 8, cudaMemcpyDeviceToHost, st)));
+  B200_RETURN_IF(ctx_->Synchronize());
+  std::memcpy(next_tokens, h_next, (size_t)batch * 8);
+  return STATUS_OK;
+}
+
+int DecoderModel::DecodeLaunches() const {
+  // prepare + rope table + embedding; per layer: 2 norms, qk-norm-rope,
+  // attention (+ combine), 4 GEMMs (+ split-K reduces); head: norm, GEMM(s), argmax
+  const int B = opt_.max_batch;
+  const int64_t H = cfg_.hidden, I = cfg_.intermediate, QKV = cfg_.qkv_dim(), AO = (int64_t)cfg_.heads * 128;
+  auto g = [&](int64_t N, int64_t K) { return b200_gemm_workspace_bytes(B, N, K, 0) > 0 ? 2 : 1; };
+  const int attn = b200_paged_decode_workspace_bytes(B, cfg_.heads, 128, opt_.max_context) > 0 ? 2 : 1;
+  const int per_layer = 2 + 1 + attn + g(QKV, H) + g(H, AO) + g(2 * I, H) + g(H, I);
+  return 3 + cfg_.layers * per_layer + 2 + g(cfg_.vocab, H);
+}
+
+int DecoderModel::PrefillLaunches() const {
+  return 2 + cfg_.layers * 8 + 4;
+}
+
+}  // namespace b200llm

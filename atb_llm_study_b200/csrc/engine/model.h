@@ -1,0 +1,119 @@
+// Dense GQA decoder model runner (Qwen3 and the Qwen3-VL text decoder).
+//
+// Replaces the reference's per-model layer graph + runner + layer loop
+// (TextDecoderLayerGraph::Build, atb_cpp_llm/src/components/text/
+// decoder_layer_graph.cpp:13-154; TextRunner, atb_cpp_llm/src/runners/
+// text_runner.cpp:12-61; Qwen3VLModel::ForwardWithTiming text stage,
+// atb_cpp_llm/src/adapters/qwen3vl_embedding/qwen3vl_model.cpp:685-768) and
+// adds what the reference only stubs: a paged KV cache and single-token decode.
+//
+// All activations live in buffers sized once at Init (no per-layer
+// allocation); the decode step is captured in a CUDA graph per batch size.
+#pragma once
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "engine/core.h"
+#include "engine/json_config.h"
+#include "engine/safetensors.h"
+
+namespace b200llm {
+
+struct ModelConfig {
+  std::string model_type;
+  int hidden = 0, layers = 0, heads = 0, kv_heads = 0, head_dim = 0, intermediate = 0;
+  int64_t vocab = 0;
+  float eps = 1e-6f, rope_theta = 1e6f;
+  bool qk_norm = true, tie_embeddings = false;
+  bool mrope = false;
+  int mrope_section[3] = {0, 0, 0};
+
+  // Reads a HF config.json (Qwen3 "qwen3", or the "text_config" of "qwen3_vl").
+  static Status FromJson(const JsonConfig& cfg, ModelConfig& out);
+  int qkv_dim() const { return (heads + 2 * kv_heads) * head_dim; }
+};
+
+struct EngineOptions {
+  int device = 0;
+  int max_batch = 64;          // KV-cache sequence slots
+  int max_context = 4096;      // tokens per slot
+  int max_prefill_tokens = 16384;
+  int block_size = 128;
+  uint64_t seed = 0;
+  float init_std = 0.02f;
+};
+
+class DecoderModel {
+ public:
+  DecoderModel() = default;
+  ~DecoderModel();
+
+  Status Init(const ModelConfig& cfg, const EngineOptions& opt);
+  Status InitRandomWeights(uint64_t seed, float std);
+  Status LoadSafetensors(const SafetensorsReader& r, const std::string& prefix);
+  // Set one weight from host memory by its HF name (dtype: BF16/FP16/FP32).
+  Status SetWeight(const std::string& name, const void* host, DType dtype, int64_t numel);
+
+  // Prefill fresh sequences.  ids: T = sum(seq_lens) token ids (host or
+  // device); slots: the KV slot of each sequence; position_ids: optional
+  // [3, T] host array (mrope) — default 0..len-1 per sequence.  Writes each
+  // sequence's greedy next token to next_tokens (host or device) and, if
+  // logits is not null, the last-token logits [num_seqs, vocab] (device, bf16).
+  Status Prefill(const int64_t* ids, bool ids_on_device, const int32_t* seq_lens, const int32_t* slots, int num_seqs,
+                 const int64_t* position_ids, int64_t* next_tokens, bool next_on_device, void* logits);
+  // One decode step for `batch` sequences (one token each).
+  Status Decode(const int64_t* ids, bool ids_on_device, const int32_t* slots, int batch, int64_t* next_tokens,
+                bool next_on_device, void* logits);
+
+  cudaStream_t stream() const { return ctx_ ? ctx_->GetStream() : nullptr; }
+  const ModelConfig& config() const { return cfg_; }
+  size_t WeightBytes() const { return weight_bytes_; }
+  size_t KvBytes() const { return kv_bytes_; }
+  int64_t ContextLen(int slot) const { return slot >= 0 && slot < (int)host_ctx_.size() ? host_ctx_[slot] : -1; }
+  // GPU kernel launches per Decode / Prefill call (for reporting).
+  int DecodeLaunches() const;
+  int PrefillLaunches() const;
+  Status ResetSlots();
+
+ private:
+  Status RunLayers(int64_t T, bool decode, int batch);
+  Status Head(int64_t rows, bool gather, int64_t* next_tokens, bool next_on_device, void* logits);
+  Status DecodeDevice(int batch);
+  void* LayerPtr(const DeviceTensor& t, int l, int64_t per_layer_elems) const {
+    return static_cast<uint16_t*>(t.data) + (int64_t)l * per_layer_elems;
+  }
+
+  ModelConfig cfg_;
+  EngineOptions opt_;
+  std::unique_ptr<ContextManager> ctx_;
+  std::unique_ptr<TensorAllocator> alloc_;
+  size_t weight_bytes_ = 0, kv_bytes_ = 0;
+  int max_blocks_ = 0;
+  int64_t num_blocks_ = 0, max_t_ = 0;
+  int cur_num_seqs_ = 0, cur_max_len_ = 0;  // shape of the prefill in flight
+
+  // weights (all layers stacked)
+  DeviceTensor embed_, lm_head_, final_norm_;
+  DeviceTensor wqkv_, wo_, wgu_, wdown_, qnorm_, knorm_, iln_, pln_;
+  // KV cache [layers][2][num_blocks][kv_heads][block_size][head_dim]
+  DeviceTensor kv_;
+  DeviceTensor block_tables_, ctx_lens_;
+  // activations / scratch
+  DeviceTensor ids_, hidden_, normed_, qkv_, attn_, act_, cos_, sin_, pos_, slots_, cu_, last_idx_, last_hidden_,
+      logits_, next_, seq_slots_, ctx_batch_, bt_batch_, gemm_ws_, attn_ws_;
+  int64_t gemm_ws_bytes_ = 0, attn_ws_bytes_ = 0;
+  std::vector<int32_t> host_ctx_;
+  // pinned staging for host <-> device copies
+  void* pinned_ = nullptr;
+  size_t pinned_bytes_ = 0;
+  // decode CUDA graphs keyed by batch size; a batch size is captured on its
+  // second call (the first runs eagerly and initialises lazy state)
+  std::map<int, cudaGraphExec_t> graphs_;
+  std::map<int, int> decode_calls_;
+  unsigned* err_ = nullptr;
+};
+
+}  // namespace b200llm

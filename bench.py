@@ -1,0 +1,482 @@
+"""Qwen3-8B bf16 decode & prefill throughput on B200 through the engine's C ABI.
+
+Workload (synthetic, seeded, random-init N(0, 0.02) weights generated on the
+device; no checkpoint or dataset):
+  * model: hidden 4096, 36 layers, 32 q / 8 kv heads x 128, intermediate
+    12288, vocab 151936, QK-norm, rope theta 1e6;
+  * prefill: 8 sequences x 2048 tokens per step (token ids U[0, vocab));
+    8 such steps fill a 64-slot paged KV cache (block 128);
+  * decode (the headline `value`): batch 64, one token per sequence per step,
+    every sequence at context 2048 (+ the tokens decoded so far).
+
+`value` = decode tokens/s with inputs resident in HBM (device ids in, device
+next tokens out), timed with CUDA events on the engine stream, max over ranks.
+`e2e` = the same decode steps through the same C call with host token ids in
+and host next tokens out (pinned staging, H2D + D2H inside the timed region).
+Multi-GPU: one independent replica per GPU (data parallel, weak scaling).
+
+`--impl reference` times the CPU restatement of the same decode step (numpy
+fp32, one layer timed and scaled to 36 layers + lm_head) on the host cores.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+QWEN3_8B = dict(model_type="qwen3", hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
+                num_key_value_heads=8, head_dim=128, intermediate_size=12288, vocab_size=151936,
+                rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=False)
+METRIC = "Qwen3-8B bf16 decode & prefill tok/s at 1/2/4/8 B200; kernel % of roofline"
+PREFILL_SEQS, PREFILL_LEN, DECODE_BATCH, DECODE_CTX, BLOCK = 8, 2048, 64, 2048, 128
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 8 and f[1].replace(".", "").isdigit():
+                    rows.append(f)
+        except Exception:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.remove(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = [n for i, n in enumerate(names) if any(r[4 + i].lower().startswith("active") for r in rows)]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# --------------------------------------------------------------------- CPU leg
+
+def cpu_decode_layer_seconds(threads_note):
+    """Time one decode layer (batch 64, context 2048) of the numpy oracle."""
+    import numpy as np
+
+    import oracle
+
+    c = QWEN3_8B
+    H, nq, nkv, hd, I = c["hidden_size"], c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"], c[
+        "intermediate_size"]
+    rng = np.random.default_rng(0)
+    B, ctx = DECODE_BATCH, DECODE_CTX
+    f = np.float32
+    w = {
+        "q_w": rng.standard_normal((nq * hd, H), f) * 0.02, "k_w": rng.standard_normal((nkv * hd, H), f) * 0.02,
+        "v_w": rng.standard_normal((nkv * hd, H), f) * 0.02, "o_w": rng.standard_normal((H, nq * hd), f) * 0.02,
+        "gate_w": rng.standard_normal((I, H), f) * 0.02, "up_w": rng.standard_normal((I, H), f) * 0.02,
+        "down_w": rng.standard_normal((H, I), f) * 0.02, "qn_w": np.ones(hd, f), "kn_w": np.ones(hd, f),
+        "iln_w": np.ones(H, f), "pln_w": np.ones(H, f),
+    }
+    nblk = ctx // BLOCK + 1
+    kc = rng.standard_normal((B * nblk, nkv, BLOCK, hd), f)
+    vc = rng.standard_normal((B * nblk, nkv, BLOCK, hd), f)
+    tables = np.arange(B * nblk).reshape(B, nblk)
+    x = rng.standard_normal((B, H), f)
+    cos, sin = oracle.rope1d_cos_sin(np.full(B, ctx), hd, c["rope_theta"])
+
+    def layer():
+        n = oracle.rms_norm(x, w["iln_w"], 1e-6)
+        q = oracle.rms_norm(oracle.linear(n, w["q_w"]).reshape(B, nq, hd), w["qn_w"], 1e-6)
+        k = oracle.rms_norm(oracle.linear(n, w["k_w"]).reshape(B, nkv, hd), w["kn_w"], 1e-6)
+        v = oracle.linear(n, w["v_w"]).reshape(B, nkv, hd)
+        q, k = oracle.rope_half(q, cos, sin), oracle.rope_half(k, cos, sin)
+        slots = oracle.slot_mapping(tables[0], np.array([ctx]), BLOCK)  # representative cache write
+        oracle.kv_cache_write(kc, k[:1], slots)
+        oracle.kv_cache_write(vc, v[:1], slots)
+        a = oracle.paged_decode_attention(q, kc, vc, tables, np.full(B, ctx + 1))
+        h = x + oracle.linear(a.reshape(B, -1), w["o_w"])
+        return h + oracle.swiglu_mlp(oracle.rms_norm(h, w["pln_w"], 1e-6), w["gate_w"], w["up_w"], w["down_w"])
+
+    layer()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        layer()
+        reps += 1
+        if time.perf_counter() - t0 > 4.0 or reps >= 5:
+            break
+    t_layer = (time.perf_counter() - t0) / reps
+    lm = rng.standard_normal((c["vocab_size"] // 8, H), f) * 0.02  # 1/8 of lm_head, scaled x8
+    t0 = time.perf_counter()
+    oracle.linear(x, lm)
+    t_head = (time.perf_counter() - t0) * 8
+    return t_layer, t_head, reps
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_baseline():
+    t_layer, t_head, reps = cpu_decode_layer_seconds(None)
+    step = 36 * t_layer + t_head
+    return {"value": DECODE_BATCH / step, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+            "sample": f"numpy fp32 oracle: one decode layer (batch 64, context 2048) timed x{reps}, "
+                      f"scaled to 36 layers + lm_head (extrapolated); {t_layer * 1e3:.1f} ms/layer"}
+
+
+# --------------------------------------------------------------------- GPU leg
+
+class EngineConfig(ctypes.Structure):
+    _fields_ = [("model_dir", ctypes.c_char_p), ("config_json", ctypes.c_char_p), ("device_id", ctypes.c_int),
+                ("max_batch", ctypes.c_int), ("max_context", ctypes.c_int), ("max_prefill_tokens", ctypes.c_int),
+                ("kv_block_size", ctypes.c_int), ("init_seed", ctypes.c_uint64), ("init_std", ctypes.c_float)]
+
+
+def check(rc, what):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with status {rc}")
+
+
+def kernel_roofline_decode_attention(L, torch, dev, reps=20):
+    """Paged decode attention alone at the decode shape (B 64, ctx 2048, 32/8 heads):
+    algorithmic bytes = K + V of every context token = 64*2048*8*128*2*2 B."""
+    B, nq, nkv, hd, ctx = DECODE_BATCH, 32, 8, 128, DECODE_CTX
+    nblk_seq = (ctx + BLOCK - 1) // BLOCK
+    nblk = B * nblk_seq
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = (torch.randn(nblk, nkv, BLOCK, hd, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(nblk, nkv, BLOCK, hd, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    tables = torch.randperm(nblk, device=dev, generator=g).to(torch.int32).reshape(B, nblk_seq)
+    ctxl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, nq * hd, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    wsb = L.b200_paged_decode_workspace_bytes(B, nq, hd, ctx)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def run():
+        check(L.b200_paged_decode(q.data_ptr(), nq * hd, kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), nblk_seq,
+                                  ctxl.data_ptr(), B, nq, nkv, hd, BLOCK, nblk, hd ** -0.5, out.data_ptr(), nq * hd,
+                                  ws.data_ptr(), wsb, ctx, st.cuda_stream), "paged_decode")
+
+    for _ in range(3):
+        run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for _ in range(reps):
+        run()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    algo = B * ctx * nkv * hd * 2 * 2
+    del kc, vc
+    return ms, algo
+
+
+def kernel_roofline_prefill_gemm(L, torch, dev, reps=10):
+    """gate/up projection with the fused SwiGLU epilogue at the prefill shape
+    (M 16384, N 2 x 12288, K 4096): 2*M*N*K flops per launch."""
+    M, N, K = PREFILL_SEQS * PREFILL_LEN, 2 * 12288, 4096
+    g = torch.Generator(device=dev).manual_seed(1)
+    A = (torch.randn(M, K, device=dev, generator=g)).to(torch.bfloat16)
+    B = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    C = torch.empty(M, N // 2, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def run():
+        check(L.b200_gemm_bf16(A.data_ptr(), K, B.data_ptr(), K, C.data_ptr(), N // 2, M, N, K, 3, None, None, 0,
+                               None, 0, st.cuda_stream), "gemm")
+
+    for _ in range(3):
+        run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for _ in range(reps):
+        run()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    del A, B, C
+    return ms, 2.0 * M * N * K
+
+
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    from atb_llm_study_b200 import capi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    L = capi.lib()
+    steps, warm = args.steps, args.warmup
+    max_ctx = DECODE_CTX + warm + 2 * steps + 16
+    cfg = EngineConfig(None, json.dumps(QWEN3_8B).encode(), local_rank, DECODE_BATCH, max_ctx,
+                       PREFILL_SEQS * PREFILL_LEN, BLOCK, 1234 + rank, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create")
+    raw = ctypes.c_void_p()
+    check(L.b200_engine_stream(eng, ctypes.byref(raw)), "engine_stream")
+    est = torch.cuda.ExternalStream(raw.value, device=dev)
+
+    def q(k):
+        v = ctypes.c_int64()
+        check(L.b200_engine_query(eng, k, ctypes.byref(v)), "query")
+        return v.value
+
+    V = QWEN3_8B["vocab_size"]
+    rng = np.random.default_rng(2 + rank)
+    T = PREFILL_SEQS * PREFILL_LEN
+    lens = np.full(PREFILL_SEQS, PREFILL_LEN, np.int32)
+    groups = DECODE_BATCH // PREFILL_SEQS
+    ids_host = [rng.integers(0, V, T).astype(np.int64) for _ in range(groups)]
+    ids_dev = [torch.from_numpy(a).to(dev) for a in ids_host]
+    next_dev = torch.empty(DECODE_BATCH, dtype=torch.int64, device=dev)
+    filled = set()
+
+    def prefill(step, on_device):
+        gi = step % groups
+        slots = np.arange(gi * PREFILL_SEQS, (gi + 1) * PREFILL_SEQS, dtype=np.int32)
+        nxt = np.zeros(PREFILL_SEQS, np.int64)
+        if on_device:
+            check(L.b200_engine_prefill(eng, ids_dev[gi].data_ptr(), 1, lens.ctypes.data, slots.ctypes.data,
+                                        PREFILL_SEQS, None, next_dev[gi * PREFILL_SEQS:].data_ptr(), 1, None),
+                  "prefill")
+        else:
+            check(L.b200_engine_prefill(eng, ids_host[gi].ctypes.data, 0, lens.ctypes.data, slots.ctypes.data,
+                                        PREFILL_SEQS, None, nxt.ctypes.data, 0, None), "prefill")
+            next_dev[gi * PREFILL_SEQS:(gi + 1) * PREFILL_SEQS].copy_(torch.from_numpy(nxt))
+        filled.add(gi)
+
+    def timed(fn, n, offset):
+        """Barrier + sync, CUDA events on the engine stream around n calls, max over ranks."""
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(est)
+        for i in range(n):
+            fn(offset + i)
+        e1.record(est)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # ---- prefill ----
+    for i in range(warm):
+        prefill(i, True)
+    pf_ms = timed(lambda i: prefill(i, True), steps, warm)
+    pf_e2e_ms = timed(lambda i: prefill(i, False), max(1, min(steps, 3)), warm + steps)
+    for gi in range(groups):
+        if gi not in filled:
+            prefill(gi, True)
+    torch.cuda.synchronize(dev)
+    check(L.b200_engine_reset(eng), "reset")  # every slot restarts at context 2048 below
+    for gi in range(groups):
+        prefill(gi, True)
+    torch.cuda.synchronize(dev)
+
+    # ---- decode ----
+    slots_all = np.arange(DECODE_BATCH, dtype=np.int32)
+    ids_d = next_dev.clone()
+    out_d = torch.empty_like(ids_d)
+    host_ids = np.zeros(DECODE_BATCH, np.int64)
+    host_next = np.zeros(DECODE_BATCH, np.int64)
+
+    def decode_dev(_):
+        nonlocal ids_d, out_d
+        check(L.b200_engine_decode(eng, ids_d.data_ptr(), 1, slots_all.ctypes.data, DECODE_BATCH, out_d.data_ptr(), 1,
+                                   None), "decode")
+        ids_d, out_d = out_d, ids_d
+
+    def decode_host(_):
+        check(L.b200_engine_decode(eng, host_ids.ctypes.data, 0, slots_all.ctypes.data, DECODE_BATCH,
+                                   host_next.ctypes.data, 0, None), "decode")
+        host_ids[:] = host_next
+
+    for i in range(warm):
+        decode_dev(i)
+    with ClockSampler(local_rank) as clk:
+        dec_ms = timed(decode_dev, steps, 0)
+    clocks = clk.summary()
+    host_ids[:] = ids_d.cpu().numpy()
+    dec_e2e_ms = timed(decode_host, steps, 0)
+    launches_per_step = q(2)
+    prefill_launches = q(3)
+
+    # ---- dominant-kernel rooflines, measured live on this GPU ----
+    hbm, tf_burst, tf_sus, src = peaks()
+    att_ms, att_bytes = kernel_roofline_decode_attention(L, torch, dev)
+    gemm_ms, gemm_flops = kernel_roofline_prefill_gemm(L, torch, dev)
+    L.b200_engine_destroy(eng)
+
+    dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
+    pf_tok_s = world * T * steps / (pf_ms / 1e3)
+    result = {
+        "metric": METRIC,
+        "value": dec_tok_s,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": dec_ms / steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: token ids U[0,151936) seeded; random-init N(0,0.02) weights generated on device",
+        "config": {
+            "workload": "Qwen3-8B decode, batch 64 at context 2048 (paged KV, block 128), greedy; "
+                        "prefill 8x2048 per step fills the cache",
+            "model": "Qwen3-8B", "global_batch": world * DECODE_BATCH, "seq_len": DECODE_CTX,
+            "decode_context": f"{DECODE_CTX}..{DECODE_CTX + warm + steps}",
+            "parallelism": f"dp{world} (independent replicas)",
+            "l2": "not flushed: each decode step streams 16 GB of weights + 19 GB of KV (> 126 MB L2)",
+        },
+        "prefill": {
+            "value": pf_tok_s, "unit": "tok/s", "ms_per_step": pf_ms / steps, "tokens_per_step": T,
+            "e2e_tok_s": world * T * max(1, min(steps, 3)) / (pf_e2e_ms / 1e3),
+            "roofline": {"kernel": "gemm_tcgen05 gate/up + SwiGLU epilogue, M16384 N24576 K4096",
+                         "bound": "tensor", "achieved": gemm_flops / (gemm_ms / 1e3) / 1e12, "peak": tf_burst,
+                         "unit": "TFLOP/s", "frac": gemm_flops / (gemm_ms / 1e3) / 1e12 / tf_burst,
+                         "peak_source": f"{src} bf16 burst", "ms": gemm_ms},
+        },
+        "roofline": {"kernel": "paged_decode_kernel (+combine), B64 ctx2048 32q/8kv", "bound": "hbm",
+                     "achieved": att_bytes / (att_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": att_bytes / (att_ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "peak_source": f"{src} copy bandwidth", "ms": att_ms, "bytes_per_launch": att_bytes},
+        "e2e": {"value": world * DECODE_BATCH * steps / (dec_e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": DECODE_BATCH * 8 + DECODE_BATCH * 4, "d2h_bytes_per_step": DECODE_BATCH * 8},
+        "gpu_launches": launches_per_step * steps,
+        "gpu_launches_note": f"{launches_per_step} kernels per decode step (CUDA graph); prefill step "
+                             f"{prefill_launches}",
+        "clocks": clocks,
+    }
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            try:
+                result["cpu_baseline"] = cpu_baseline()
+            except Exception as e:  # the CPU leg must not sink the GPU number
+                result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    times = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        cb = cpu_baseline()
+        if i >= args.warmup:
+            times.append(DECODE_BATCH / cb["value"])
+    step_s = statistics.mean(times)
+    val = DECODE_BATCH / step_s
+    out = {
+        "metric": METRIC, "impl": "reference", "value": val, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "Qwen3-8B decode, batch 64 at context 2048 (one layer timed, x36 + lm_head)",
+                   "model": "Qwen3-8B", "global_batch": DECODE_BATCH, "seq_len": DECODE_CTX,
+                   "parallelism": "host CPU"},
+        "cpu_baseline": {"kind": cb["kind"], "cores": cb["cores"], "sample": cb["sample"], "value": val},
+        "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Ascend ATB) cannot run here; this is the repo's numpy restatement of the "
+                "reference's CPU decoder-layer math (oracle/), timed on the host cores",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_b200(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -181,6 +181,79 @@ B200_API int b200_scatter_add_rows(void* hidden, int64_t rows, int64_t dim, cons
 /* out[r] = argmax_j logits[r, j] (lowest index on ties), logits [rows, vocab] bf16. */
 B200_API int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t ld, int64_t* out, b200_stream_t stream);
 
+/* ----------------------------------------------------------------- engine */
+
+/* A decoder model on one GPU: weights, a paged KV cache of max_batch slots x
+ * max_context tokens, activation buffers sized once, and the layer loop.
+ * Replaces LLMEngine::Create / Forward (atb_cpp_llm/include/atb_llm/engine.h:8-24,
+ * atb_cpp_llm/src/engine/llm_engine.cpp:22-108) with EngineConfig
+ * (atb_cpp_llm/include/atb_llm/types.h:70-74) extended by the KV-cache sizes
+ * the reference leaves unimplemented (atb_cpp_llm/include/atb_llm/runtime.h:45-54).
+ * Not thread-safe: one engine per thread, as the reference's models
+ * (atb_cpp_llm/include/atb_llm/model.h:33-36). */
+typedef struct b200_engine_s* b200_engine_t;
+
+typedef struct b200_engine_config {
+  const char* model_dir;   /* directory with config.json (+ model.safetensors), or NULL */
+  const char* config_json; /* inline config.json text when model_dir is NULL */
+  int device_id;
+  int max_batch;          /* KV-cache sequence slots (default 64) */
+  int max_context;        /* tokens per slot (default 4096) */
+  int max_prefill_tokens; /* packed tokens per prefill call (default 16384) */
+  int kv_block_size;      /* 64 or 128 (default 128) */
+  uint64_t init_seed;     /* seed of the N(0, init_std) init used when no weights file is given */
+  float init_std;         /* default 0.02 */
+} b200_engine_config;
+
+enum b200_engine_query_key {
+  B200_Q_WEIGHT_BYTES = 0,
+  B200_Q_KV_BYTES = 1,
+  B200_Q_DECODE_LAUNCHES = 2,  /* kernels one b200_engine_decode step launches at max_batch */
+  B200_Q_PREFILL_LAUNCHES = 3, /* kernels one b200_engine_prefill call launches */
+  B200_Q_HIDDEN = 4,
+  B200_Q_LAYERS = 5,
+  B200_Q_VOCAB = 6
+};
+
+/* Model type is resolved from config.json "model_type" through a registry with
+ * exact match first, then priority-ordered compatibility checks
+ * (atb_cpp_llm/src/engine/model_registry.cpp:90-121). */
+B200_API int b200_engine_create(const b200_engine_config* config, b200_engine_t* out);
+B200_API int b200_engine_destroy(b200_engine_t engine);
+
+/* Load one weight by its HF name from host memory (dtype 0 = bf16, 1 = fp16,
+ * 2 = fp32), e.g. "model.layers.3.self_attn.q_proj.weight".  Replaces
+ * LoadQwen3VLWeights / CopyWeightToFp16NPU
+ * (atb_cpp_llm/src/adapters/qwen3vl_embedding/qwen3vl_weights.cpp:79-264,
+ * atb_cpp_llm/src/io/weight_helpers.cpp:16-76) with a direct bf16 upload. */
+B200_API int b200_engine_set_weight(b200_engine_t engine, const char* name, const void* host, int dtype,
+                                    int64_t numel);
+
+/* Prefill fresh sequences packed back to back: ids [sum(seq_lens)] (host or
+ * device), seq_lens / slots [num_seqs] (host), optional position_ids [3, T]
+ * (host, mrope; NULL = 0..len-1 per sequence).  Fills the KV cache of each
+ * slot and writes each sequence's greedy next token to next_tokens (host or
+ * device); logits (device, bf16 [num_seqs, vocab]) when not NULL.
+ * Replaces Qwen3VLModel::ForwardWithTiming's text stage
+ * (atb_cpp_llm/src/adapters/qwen3vl_embedding/qwen3vl_model.cpp:685-768). */
+B200_API int b200_engine_prefill(b200_engine_t engine, const int64_t* ids, int ids_on_device,
+                                 const int32_t* seq_lens, const int32_t* slots, int num_seqs,
+                                 const int64_t* position_ids, int64_t* next_tokens, int next_on_device,
+                                 void* logits);
+
+/* One decode step: one token per listed slot (ids host or device, slots host).
+ * No reference counterpart (the reference has no decode, IsGenerative() is
+ * false for its only model, atb_cpp_llm/include/atb_llm/model.h:47-50). */
+B200_API int b200_engine_decode(b200_engine_t engine, const int64_t* ids, int ids_on_device, const int32_t* slots,
+                                int batch, int64_t* next_tokens, int next_on_device, void* logits);
+
+/* The engine's CUDA stream (device-side results are ordered on it). */
+B200_API int b200_engine_stream(b200_engine_t engine, b200_stream_t* out);
+/* Forget every slot's context (the KV cache contents stay, unreferenced). */
+B200_API int b200_engine_reset(b200_engine_t engine);
+B200_API int b200_engine_query(b200_engine_t engine, int what, int64_t* out);
+B200_API int b200_engine_context_len(b200_engine_t engine, int slot, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif
