@@ -37,6 +37,9 @@ QWEN3_8B = dict(model_type="qwen3", hidden_size=4096, num_hidden_layers=36, num_
                 rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=False)
 METRIC = "Qwen3-8B bf16 decode & prefill tok/s at 1/2/4/8 B200; kernel % of roofline"
 PREFILL_SEQS, PREFILL_LEN, DECODE_BATCH, DECODE_CTX, BLOCK = 8, 2048, 64, 2048, 128
+# DRAM bytes (read + write) of one paged-decode launch at the bench shape, from
+# an ncu capture of `bench.py --profile-kernel decode_attention`.
+DECODE_ATTN_DRAM_BYTES = 537.974784e6 + 5.952256e6
 
 
 def peaks():
@@ -331,6 +334,10 @@ def run_b200(args, rank, world, local_rank):
     # ---- prefill ----
     for i in range(warm):
         prefill(i, True)
+    # clocks are sampled from the first timed prefill step to the last timed
+    # decode step (the decode region alone is shorter than the 200 ms period)
+    clk = ClockSampler(local_rank).__enter__()
+    time.sleep(0.5)  # nvidia-smi start-up
     pf_ms = timed(lambda i: prefill(i, True), steps, warm)
     pf_e2e_ms = timed(lambda i: prefill(i, False), max(1, min(steps, 3)), warm + steps)
     for gi in range(groups):
@@ -362,8 +369,8 @@ def run_b200(args, rank, world, local_rank):
 
     for i in range(warm):
         decode_dev(i)
-    with ClockSampler(local_rank) as clk:
-        dec_ms = timed(decode_dev, steps, 0)
+    dec_ms = timed(decode_dev, steps, 0)
+    clk.__exit__(None, None, None)
     clocks = clk.summary()
     host_ids[:] = ids_d.cpu().numpy()
     dec_e2e_ms = timed(decode_host, steps, 0)
@@ -409,7 +416,9 @@ def run_b200(args, rank, world, local_rank):
         },
         "roofline": {"kernel": "paged_decode_kernel (+combine), B64 ctx2048 32q/8kv", "bound": "hbm",
                      "achieved": att_bytes / (att_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": att_bytes / (att_ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "frac": att_bytes / (att_ms / 1e3) / 1e9 / hbm, "traffic": DECODE_ATTN_DRAM_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch at this "
+                                       "shape (profiles/paged_decode_b64_ctx2048.md)",
                      "peak_source": f"{src} copy bandwidth", "ms": att_ms, "bytes_per_launch": att_bytes},
         "e2e": {"value": world * DECODE_BATCH * steps / (dec_e2e_ms / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": DECODE_BATCH * 8 + DECODE_BATCH * 4, "d2h_bytes_per_step": DECODE_BATCH * 8},
@@ -466,12 +475,25 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm"],
+                    help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile_kernel:
+        import torch
+
+        from atb_llm_study_b200 import capi
+
+        dev = torch.device("cuda", local_rank)
+        fn = kernel_roofline_decode_attention if args.profile_kernel == "decode_attention" \
+            else kernel_roofline_prefill_gemm
+        ms, work = fn(capi.lib(), torch, dev, reps=3)
+        print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
+        return
     if args.impl == "reference":
         run_reference(args, rank)
         return

@@ -106,9 +106,9 @@ def test_engine_prefill_then_decode(block):
         nxt = np.zeros(len(lens), np.int64)
         V = CFG["vocab_size"]
         logits = torch.empty(len(lens), V, dtype=torch.bfloat16, device=G.DEV)
-        G.check(L.b200_engine_prefill(eng, ids.ctypes.data, 0, np.array(lens, np.int32).ctypes.data,
-                                      np.array(slots, np.int32).ctypes.data, len(lens), None, nxt.ctypes.data, 0,
-                                      logits.data_ptr()), "prefill")
+        lens_a, slots_a = np.array(lens, np.int32), np.array(slots, np.int32)  # kept alive across the call
+        G.check(L.b200_engine_prefill(eng, ids.ctypes.data, 0, lens_a.ctypes.data, slots_a.ctypes.data, len(lens),
+                                      None, nxt.ctypes.data, 0, logits.data_ptr()), "prefill")
         torch.cuda.synchronize()
         lg = G.host(logits)
         check_rows(lg, seqs, w)
@@ -146,12 +146,13 @@ def test_engine_rejects_bad_requests():
         INVALID = -1
         # duplicate slot, slot out of range, empty sequence, too long
         for lens, slots in (([4, 4], [1, 1]), ([4, 4], [0, 9]), ([0, 8], [0, 1]), ([200, 1], [0, 1])):
-            rc = L.b200_engine_prefill(eng, ids.ctypes.data, 0, np.array(lens, np.int32).ctypes.data,
-                                       np.array(slots, np.int32).ctypes.data, 2, None, nxt.ctypes.data, 0, None)
+            lens_a, slots_a = np.array(lens, np.int32), np.array(slots, np.int32)
+            rc = L.b200_engine_prefill(eng, ids.ctypes.data, 0, lens_a.ctypes.data, slots_a.ctypes.data, 2, None,
+                                       nxt.ctypes.data, 0, None)
             assert rc == INVALID, (lens, slots, rc)
         # decode on a slot that holds no sequence
-        rc = L.b200_engine_decode(eng, ids.ctypes.data, 0, np.array([3], np.int32).ctypes.data, 1, nxt.ctypes.data, 0,
-                                  None)
+        one = np.array([3], np.int32)
+        rc = L.b200_engine_decode(eng, ids.ctypes.data, 0, one.ctypes.data, 1, nxt.ctypes.data, 0, None)
         assert rc == INVALID
         # unknown model type is refused at create
         cfg = EngineConfig(None, json.dumps(dict(CFG, model_type="mystery", num_local_experts=8)).encode(), 0, 1, 16,
