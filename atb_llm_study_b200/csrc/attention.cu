@@ -598,6 +598,71 @@ extern "C" int b200_flash_prefill(const void* q, int64_t q_stride, const void* k
 #undef B200_PF
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of b200_paged_decode.
+//
+// Its split-KV scratch (per-split partial outputs and log-sum-exps) lives in
+// the file-scope array below instead of a caller-provided workspace.  Every
+// GPU that loads this library holds the array until the process exits.  Host
+// code cannot use the array's name as a device address, so the first call on
+// each device looks the address up with cudaGetSymbolAddress (with that device
+// current) and caches it; all later calls on that device reuse it.
+// ---------------------------------------------------------------------------
+static constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_paged_decode_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_paged_decode_scratch on the current device (nullptr on failure).
+void* noalloc_scratch(cudaError_t* err) {
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_paged_decode_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+
+extern "C" int64_t b200_paged_decode_noalloc_max_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int b200_paged_decode_noalloc(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                         const int32_t* block_tables, int max_blocks_per_seq,
+                                         const int32_t* context_lens, int batch, int nq, int nkv, int head_dim,
+                                         int block_size, int64_t num_blocks, float scale, void* out,
+                                         int64_t out_stride, int max_context, b200_stream_t stream) {
+  // Reject, before any launch, a problem whose split-KV scratch exceeds the
+  // array: the split count b200_paged_decode picks for this shape, times
+  // batch x nq x (head_dim + 1) fp32 values.
+  if (batch < 0 || nq <= 0 || nkv <= 0 || max_context < 0) return B200_ERROR_INVALID_PARAM;
+  if (batch > 0) {
+    const int ctx = std::max(1, max_context);
+    int splits = decode_splits(batch, nkv, ctx);
+    const int tiles_total = (ctx + kDecTile - 1) / kDecTile;
+    const int tiles_per_split = (tiles_total + splits - 1) / splits;
+    splits = (tiles_total + tiles_per_split - 1) / tiles_per_split;
+    const int64_t need =
+        splits > 1 ? (int64_t)batch * nq * splits * (kDecHD + 1) * (int64_t)sizeof(float) : 0;
+    if (need > kNoAllocScratchBytes) return B200_ERROR_INVALID_PARAM;
+  }
+  cudaError_t e = cudaSuccess;
+  void* scratch = noalloc_scratch(&e);
+  if (!scratch) return B200_ERROR_CUDA_BASE - (int)e;
+  return b200_paged_decode(q, q_stride, k_cache, v_cache, block_tables, max_blocks_per_seq, context_lens, batch, nq,
+                           nkv, head_dim, block_size, num_blocks, scale, out, out_stride, scratch,
+                           kNoAllocScratchBytes, max_context, stream);
+}
+
 extern "C" int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head_dim, int max_context) {
   if (batch <= 0 || nq <= 0 || head_dim != kDecHD || max_context <= 0) return 0;
   // splits depend on nkv only through batch*nkv >= batch; size for the largest count

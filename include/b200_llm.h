@@ -156,6 +156,34 @@ B200_API int b200_paged_decode(const void* q, int64_t q_stride, const void* k_ca
 
 B200_API int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head_dim, int max_context);
 
+/* b200_paged_decode for callers that cannot allocate device memory — for
+ * example code running as an operator inside another framework whose memory
+ * pool owns the GPU and forbids raw cudaMalloc, or a serving loop that froze
+ * its memory plan at start-up.  It takes no workspace and allocates nothing:
+ * the split-KV scratch is a fixed 8 MiB array compiled into this library,
+ * held on every GPU that loads it until the process exits
+ * (b200_paged_decode_noalloc_max_scratch_bytes()).  Inputs and outputs are
+ * the caller's, with the same meaning and limits as b200_paged_decode.  The
+ * scratch a call needs is batch x nq x splits x (head_dim + 1) x 4 bytes,
+ * where splits is the KV split count the kernel picks (1 = no scratch; 2 for
+ * batch 64 x 8 kv heads at context 2048, i.e. 2.1 MB); a call that would need
+ * more than 8 MiB is rejected with B200_ERROR_INVALID_PARAM before anything
+ * is launched.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the one array and it keeps the
+ * last call's contents (nothing in it needs to start at zero: each call
+ * writes every scratch entry it reads), so calls whose executions overlap on
+ * the GPU — on different streams, or on several host threads — race and must
+ * be serialised by the caller.
+ * This entry point has no counterpart in the reference. */
+B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                       const int32_t* block_tables, int max_blocks_per_seq,
+                                       const int32_t* context_lens, int batch, int nq, int nkv, int head_dim,
+                                       int block_size, int64_t num_blocks, float scale, void* out,
+                                       int64_t out_stride, int max_context, b200_stream_t stream);
+B200_API int64_t b200_paged_decode_noalloc_max_scratch_bytes(void);
+
 /* slots[t] = block_tables[seq_ids[t], positions[t] / block_size] * block_size
  *            + positions[t] % block_size   (int64, bit-exact).
  * No reference counterpart (the reference has no paged KV cache,

@@ -1,0 +1,79 @@
+"""The allocation-free decode-attention entry point, through the C ABI.
+
+b200_paged_decode_noalloc serves callers that may not call cudaMalloc (an
+operator inside a framework that owns the GPU memory pool, a serving loop
+with a frozen memory plan): its split-KV scratch is a fixed array inside the
+library.  This test checks it against the regular entry point
+(b200_paged_decode with a caller workspace) on two calls in a row — the second
+call reuses the array with the first call's leftovers in it — and that a
+problem needing more scratch than the array holds is refused before launch.
+
+This file is named to be collected last, so a run that stops at the first
+failure has already run every other test.  Tolerance: the per-op bar of the
+other kernel tests (cosine >= 0.9999, max |err| <= 2 % of max |ref|).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    import gpu_util as G
+
+
+def _case(seed, B, ctx):
+    rng = np.random.default_rng(seed)
+    nq, nkv, hd, bs = 32, 8, 128, 128
+    maxb = int((max(ctx) + bs - 1) // bs)
+    nblk = B * maxb
+    kc = G.bf16(rng.standard_normal((nblk, nkv, bs, hd)).astype(np.float32))
+    vc = G.bf16(rng.standard_normal((nblk, nkv, bs, hd)).astype(np.float32))
+    tables = G.i32(rng.permutation(nblk).reshape(B, maxb))
+    q = G.bf16(rng.standard_normal((B, nq * hd)).astype(np.float32))
+    return dict(q=q, kc=kc, vc=vc, tables=tables, ctx=G.i32(ctx), B=B, nq=nq, nkv=nkv, hd=hd, bs=bs, maxb=maxb,
+                nblk=nblk, max_ctx=int(max(ctx)))
+
+
+def _run(c, noalloc):
+    L = G.L()
+    out = torch.empty(c["B"], c["nq"] * c["hd"], dtype=torch.bfloat16, device=G.DEV)
+    args = (c["q"].data_ptr(), c["nq"] * c["hd"], c["kc"].data_ptr(), c["vc"].data_ptr(), c["tables"].data_ptr(),
+            c["maxb"], c["ctx"].data_ptr(), c["B"], c["nq"], c["nkv"], c["hd"], c["bs"], c["nblk"],
+            1.0 / np.sqrt(c["hd"]), out.data_ptr(), c["nq"] * c["hd"])
+    if noalloc:
+        G.check(L.b200_paged_decode_noalloc(*args, c["max_ctx"], G.stream()), "paged_decode_noalloc")
+    else:
+        wsb = L.b200_paged_decode_workspace_bytes(c["B"], c["nq"], c["hd"], c["max_ctx"])
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=G.DEV)
+        G.check(L.b200_paged_decode(*args, ws.data_ptr(), wsb, c["max_ctx"], G.stream()), "paged_decode")
+    torch.cuda.synchronize()
+    return G.host(out)
+
+
+def test_noalloc_decode_matches_workspace_entry_point_twice():
+    L = G.L()
+    assert L.b200_paged_decode_noalloc_max_scratch_bytes() == 8 << 20
+    # two different problems back to back: the second finds the first's data in the scratch
+    for seed, B, ctx in ((11, 64, [2048] * 63 + [5]), (12, 16, [1, 64, 65, 777] * 4)):
+        c = _case(seed, B, np.array(ctx))
+        assert L.b200_paged_decode_workspace_bytes(B, 32, 128, c["max_ctx"]) > 0  # split-KV path in use
+        ref = _run(c, noalloc=False)
+        for _ in range(2):
+            got = _run(c, noalloc=True)
+            for b in range(B):
+                assert G.cosine(got[b], ref[b]) >= 0.9999, b
+                assert G.max_rel_err(got[b], ref[b]) <= 0.02, b
+    assert G.device_errors() == 0
+
+
+def test_noalloc_rejects_problem_larger_than_its_scratch():
+    L = G.L()
+    # 64 sequences x 1 kv head -> 10 KV splits; 64 x 64 heads x 10 x 129 x 4 B = 21 MB > 8 MiB
+    B, nq, nkv, hd, max_ctx = 64, 64, 1, 128, 32768
+    assert L.b200_paged_decode_workspace_bytes(B, nq, hd, max_ctx) > L.b200_paged_decode_noalloc_max_scratch_bytes()
+    dummy = 256  # never dereferenced: the size check fails before any launch
+    rc = L.b200_paged_decode_noalloc(dummy, nq * hd, dummy, dummy, dummy, 256, dummy, B, nq, nkv, hd, 128, 16384, 0.1,
+                                     dummy, nq * hd, max_ctx, G.stream())
+    assert rc == -1  # B200_ERROR_INVALID_PARAM
