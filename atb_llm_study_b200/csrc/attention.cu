@@ -16,6 +16,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -258,7 +259,10 @@ __device__ __forceinline__ uint32_t dec_off(int r, int c) {
   return (uint32_t)((c >> 3) * kDecHalfBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+constexpr int kDecThreads = 160;  // warps 0-3 compute, warp 4 issues the TMA loads
+constexpr int kDecProducerWarp = 4;
+
+__global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV,
                                                            const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     fence_barrier_init();
   }
   // Q rows: heads kh*G .. kh*G+G-1, padded with zeros to 16 rows
-  for (int i = threadIdx.x; i < 16 * 16; i += 128) {
+  for (int i = threadIdx.x; i < 16 * 16; i += blockDim.x) {
     const int r = i >> 4, c = i & 15;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (r < p.G) val = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride + (kh * p.G + r) * kDecHD + c * 8);
@@ -295,6 +299,47 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
   }
   __syncthreads();
 
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+  if (warp == kDecProducerWarp) {
+    // ---- producer warp: tile i of this split covers tokens t_begin + 64 i ... ----
+    // Lane l fetches the block id of tile (32 k + l); lane 0 issues the loads.
+    int myblk = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % kDecStages, round = i / kDecStages;
+      bool ok = true;
+      if (lane == 0 && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, p.err);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if ((i & 31) == 0) {
+        const int ti = i + lane;
+        int blk = 0;
+        if (ti < ntiles) {
+          blk = p.block_tables[(int64_t)b * p.max_blocks + (t_begin + ti * kDecTile) / p.block_size];
+          if (blk < 0 || blk >= p.num_blocks) {
+            raise_error(p.err, DEV_ERR_BAD_INDEX);
+            blk = 0;
+          }
+        }
+        myblk = blk;
+      }
+      const int blk = __shfl_sync(0xffffffffu, myblk, i & 31);
+      if (lane == 0) {
+        const int tok = t_begin + i * kDecTile;
+        const int row = (blk * p.nkv + kh) * p.block_size + tok % p.block_size;
+        uint8_t* dst = smem + s * kDecStageBytes;
+        mbar_arrive_expect_tx(&full[s], kDecStageBytes);
+        tma_load_2d(dst, &tmK, &full[s], 0, row);
+        tma_load_2d(dst + kDecHalfBytes, &tmK, &full[s], 64, row);
+        tma_load_2d(dst + kDecTileBytes, &tmV, &full[s], 0, row);
+        tma_load_2d(dst + kDecTileBytes + kDecHalfBytes, &tmV, &full[s], 64, row);
+      }
+      __syncwarp();
+    }
+  } else {
+  // ---- compute warps 0-3 ----
   uint32_t qf[8][4];
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
@@ -304,47 +349,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     ldmatrix_x4(qf[kk], smem_u32(sQ + r * 256 + ((c ^ (r & 7)) << 4)));
   }
 
-  // producer: tile i of this split covers tokens t_begin + 64 i ...
-  auto issue = [&](int i) {
-    const int tok = t_begin + i * kDecTile;
-    const int bi = tok / p.block_size;
-    int blk = p.block_tables[(int64_t)b * p.max_blocks + bi];
-    if (blk < 0 || blk >= p.num_blocks) {
-      raise_error(p.err, DEV_ERR_BAD_INDEX);
-      blk = 0;
-    }
-    const int row = (blk * p.nkv + kh) * p.block_size + tok % p.block_size;
+  for (int i = 0; i < ntiles; ++i) {
     const int s = i % kDecStages;
-    uint8_t* dst = smem + s * kDecStageBytes;
-    mbar_arrive_expect_tx(&full[s], kDecStageBytes);
-    tma_load_2d(dst, &tmK, &full[s], 0, row);
-    tma_load_2d(dst + kDecHalfBytes, &tmK, &full[s], 64, row);
-    tma_load_2d(dst + kDecTileBytes, &tmV, &full[s], 0, row);
-    tma_load_2d(dst + kDecTileBytes + kDecHalfBytes, &tmV, &full[s], 64, row);
-  };
-  bool alive = true;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < min(ntiles, kDecStages - 1); ++i) issue(i);
-  }
-
-  float o[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-
-  for (int i = 0; i < ntiles && alive; ++i) {
-    if (threadIdx.x == 0 && i + kDecStages - 1 < ntiles) {
-      const int nx = i + kDecStages - 1;
-      const int s = nx % kDecStages;
-      const int round = nx / kDecStages;
-      if (round == 0 || mbar_wait(&empty[s], (round - 1) & 1, p.err)) issue(nx);
-    }
-    __syncwarp();
-    const int s = i % kDecStages;
-    if (!mbar_wait(&full[s], (i / kDecStages) & 1, p.err)) {
-      alive = false;
-      break;
-    }
+    if (!mbar_wait(&full[s], (i / kDecStages) & 1, p.err)) break;
     const uint8_t* sK = smem + s * kDecStageBytes;
     const uint8_t* sV = sK + kDecTileBytes;
     // this warp's 16 keys: rows warp*16 .. +15 of the tile
@@ -418,8 +425,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
+  }  // compute warps
 
-  // ---- merge the 4 warps (each has its own m, l, O over its keys) ----
+  // ---- merge the 4 compute warps (each has its own m, l, O over its keys) ----
   __syncthreads();
   float* sm_m = reinterpret_cast<float*>(smem);          // [4][16]
   float* sm_l = sm_m + 64;                               // [4][16]
@@ -429,13 +437,13 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
     l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
   }
-  if (t4 == 0) {
+  if (t4 == 0 && warp < 4) {
     sm_m[warp * 16 + g] = m_run[0];
     sm_m[warp * 16 + g + 8] = m_run[1];
     sm_l[warp * 16 + g] = l_run[0];
     sm_l[warp * 16 + g + 8] = l_run[1];
   }
-  for (int i = threadIdx.x; i < 16 * kDecHD; i += 128) sm_o[i] = 0.f;
+  for (int i = threadIdx.x; i < 16 * kDecHD; i += blockDim.x) sm_o[i] = 0.f;
   __syncthreads();
   float fac[2];
 #pragma unroll
@@ -458,7 +466,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     __syncthreads();
   }
   // row totals: M (log2 domain) and L = sum_w l_w * 2^(m_w - M)
-  for (int i = threadIdx.x; i < p.G * kDecHD; i += 128) {
+  for (int i = threadIdx.x; i < p.G * kDecHD; i += blockDim.x) {
     const int row = i / kDecHD, d = i % kDecHD;
     float M = -INFINITY;
     for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w * 16 + row]);
@@ -533,12 +541,34 @@ int num_sms() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
+// Most splits a decode may use at this context: >= 4 tiles per split, <= 32.
+int decode_max_splits(int max_context) {
+  return std::max(1, std::min(32, (max_context + 4 * kDecTile - 1) / (4 * kDecTile)));
+}
+
+// KV splits per (sequence, kv head): the count whose CTAs fill the last wave
+// best (two CTAs per SM), with a small charge per extra split for the partial
+// outputs and the combine pass.
 int decode_splits(int batch, int nkv, int max_context) {
-  const int pairs = batch * nkv;
-  const int target = 4 * num_sms();  // two CTAs per SM, two waves
-  int s = (target + pairs - 1) / pairs;
-  const int max_s = std::max(1, (max_context + 4 * kDecTile - 1) / (4 * kDecTile));  // >= 4 tiles per split
-  return std::max(1, std::min(s, std::min(max_s, 32)));
+  static const int forced = [] {  // tuning override: B200_DECODE_SPLITS=<n>
+    const char* v = std::getenv("B200_DECODE_SPLITS");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (forced > 0) return std::min(forced, decode_max_splits(max_context));
+  const int64_t pairs = (int64_t)batch * nkv;
+  const int64_t slots = 2 * (int64_t)num_sms();
+  int best = 1;
+  double best_score = -1.0;
+  for (int s = 1; s <= decode_max_splits(max_context); ++s) {
+    const int64_t ctas = pairs * s;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double score = (double)ctas / (double)(waves * slots) - 0.01 * s;
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
 }
 
 // Opt one kernel (a distinct template argument per kernel) into large dynamic
@@ -665,8 +695,9 @@ extern "C" int b200_paged_decode_noalloc(const void* q, int64_t q_stride, const 
 
 extern "C" int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head_dim, int max_context) {
   if (batch <= 0 || nq <= 0 || head_dim != kDecHD || max_context <= 0) return 0;
-  // splits depend on nkv only through batch*nkv >= batch; size for the largest count
-  const int s = decode_splits(batch, 1, max_context);
+  // the split count depends on nkv, which this query does not take: size for
+  // the most splits any kv-head count can select at this context
+  const int s = decode_max_splits(max_context);
   if (s <= 1) return 0;
   return (int64_t)batch * nq * s * (kDecHD + 1) * (int64_t)sizeof(float) + 256;
 }
@@ -721,7 +752,7 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_
   if (!make_cache_tmap(&tk, k_cache, rows) || !make_cache_tmap(&tv, v_cache, rows)) return B200_ERROR_UNSUPPORTED;
   if (!set_smem<paged_decode_kernel>(kDecSmem)) return B200_ERROR_UNSUPPORTED;
   dim3 grid(batch, nkv, splits);
-  paged_decode_kernel<<<grid, 128, kDecSmem, stream>>>(tk, tv, p);
+  paged_decode_kernel<<<grid, kDecThreads, kDecSmem, stream>>>(tk, tv, p);
   B200_CHECK_LAUNCH();
   if (splits > 1) {
     decode_combine_kernel<<<batch * nq, kDecHD, 0, stream>>>(p.ws_o, p.ws_lse, nq, splits, p.out, out_stride);

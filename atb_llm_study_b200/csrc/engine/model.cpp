@@ -5,6 +5,8 @@
 #include <set>
 
 #include "engine/engine_kernels.h"
+#include "fused.h"
+#include "gemm.h"
 
 namespace b200 {
 unsigned* error_word(int device);
@@ -133,7 +135,11 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   for (int64_t m : {(int64_t)1, (int64_t)opt.max_batch})
     for (auto& s : shapes) ws = std::max(ws, b200_gemm_workspace_bytes(m, s[0], s[1], B200_EPI_NONE_));
   gemm_ws_bytes_ = ws;
-  if (ws > 0) B200_RETURN_IF(A(gemm_ws_, DType::FP32, {(ws + 3) / 4}));
+  if (ws > 0) {
+    B200_RETURN_IF(A(gemm_ws_, DType::FP32, {(ws + 3) / 4}));
+    // split-K accumulator + tile counters start at zero; every GEMM leaves them zero
+    B200_RETURN_IF(FromCuda(cudaMemsetAsync(gemm_ws_.data, 0, gemm_ws_.bytes(), ctx_->GetStream())));
+  }
   attn_ws_bytes_ = b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
   if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
 
@@ -247,44 +253,75 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
   const int64_t AO = (int64_t)cfg_.heads * hd;
   const int nq = cfg_.heads, nkv = cfg_.kv_heads, L = cfg_.layers;
   const float scale = 1.0f / std::sqrt((float)hd);
-  auto gemm = [&](const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
-                  int64_t K, int epi, const void* R, int64_t ldr) {
-    return b200_gemm_bf16(A, lda, B, ldb, C, ldc, M, N, K, epi, nullptr, R, ldr, gemm_ws_.data, gemm_ws_bytes_, st);
+  float* ws = gemm_ws_.as<float>();
+  // Projections may split K (decode-sized M): they then leave fp32 partials in
+  // ws and the next kernel, which reads the result anyway, finishes the sum.
+  auto gemm = [&](const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t N, int64_t K,
+                  int epi, const void* R, int64_t ldr, int* splits) {
+    ++launches_;
+    return b200::gemm_launch(A, lda, B, ldb, C, ldc, T, N, K, epi, nullptr, R, ldr, ws, gemm_ws_bytes_, st, splits);
   };
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
   const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;
+  int s_qkv = 1, s_o = 1, s_gu = 1, s_d = 1;
   for (int l = 0; l < L; ++l) {
-    if (l == 0)
+    if (l == 0) {
+      ++launches_;
       B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, 0), normed_.data, nullptr, T, H, H, cfg_.eps, st));
-    B200_RETURN_IF(gemm(normed_.data, H, bf(wqkv_, (int64_t)l * QKV * H), H, qkv_.data, QKV, T, QKV, H,
-                        B200_EPI_NONE, nullptr, 0));
+    }
+    // attention block
+    B200_RETURN_IF(gemm(normed_.data, H, bf(wqkv_, (int64_t)l * QKV * H), H, qkv_.data, QKV, QKV, H, B200_EPI_NONE,
+                        nullptr, 0, &s_qkv));
     uint16_t* kc = bf(kv_, (int64_t)l * kv_layer);
     uint16_t* vc = kc + kv_layer / 2;
-    B200_RETURN_IF(b200_qk_norm_rope(qkv_.data, T, nq, nkv, (int)hd, QKV, cfg_.qk_norm ? bf(qnorm_, l * hd) : nullptr,
-                                     cfg_.qk_norm ? bf(knorm_, l * hd) : nullptr, cfg_.eps, cos_.as<float>(),
-                                     sin_.as<float>(), slots_.as<int64_t>(), kc, vc, num_blocks_, opt_.block_size,
-                                     st));
+    ++launches_;
+    B200_RETURN_IF(b200::qk_norm_rope_launch(
+        qkv_.data, T, nq, nkv, (int)hd, QKV, cfg_.qk_norm ? bf(qnorm_, l * hd) : nullptr,
+        cfg_.qk_norm ? bf(knorm_, l * hd) : nullptr, cfg_.eps, cos_.as<float>(), sin_.as<float>(),
+        slots_.as<int64_t>(), kc, vc, num_blocks_, opt_.block_size, s_qkv > 1 ? ws : nullptr, s_qkv, st));
     uint16_t* q = static_cast<uint16_t*>(qkv_.data);
     if (!decode) {
+      ++launches_;
       B200_RETURN_IF(b200_flash_prefill(q, QKV, q + nq * hd, q + (nq + nkv) * hd, QKV, attn_.data, AO,
                                         cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, nq, nkv, (int)hd, scale, 1,
                                         st));
     } else {
+      launches_ += attn_ws_bytes_ > 0 ? 2 : 1;
       B200_RETURN_IF(b200_paged_decode(q, QKV, kc, vc, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(),
                                        batch, nq, nkv, (int)hd, opt_.block_size, num_blocks_, scale, attn_.data, AO,
                                        attn_ws_.data, attn_ws_bytes_, opt_.max_context, st));
     }
-    B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, T, H, AO,
-                           B200_EPI_RESIDUAL, hidden_.data, H));
-    B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(pln_, (int64_t)l * H), normed_.data, nullptr, T, H, H,
-                                cfg_.eps, st));
-    B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, (int64_t)l * 2 * I * H), H, act_.data, I, T, 2 * I, H,
-                           B200_EPI_SWIGLU, nullptr, 0));
-    B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, (int64_t)l * H * I), I, hidden_.data, H, T, H, I,
-                           B200_EPI_RESIDUAL, hidden_.data, H));
-    if (l + 1 < L)
-      B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, (int64_t)(l + 1) * H), normed_.data, nullptr, T, H,
-                                  H, cfg_.eps, st));
+    B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, H, AO, B200_EPI_RESIDUAL,
+                        hidden_.data, H, &s_o));
+    ++launches_;
+    if (s_o > 1)  // hidden += sum(partials); normed = rmsnorm(hidden)
+      B200_RETURN_IF(b200::splitk_residual_rmsnorm(ws, s_o, T, H, hidden_.data, bf(pln_, (int64_t)l * H),
+                                                   normed_.data, cfg_.eps, st));
+    else
+      B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(pln_, (int64_t)l * H), normed_.data, nullptr, T, H, H,
+                                  cfg_.eps, st));
+    // MLP block
+    B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, (int64_t)l * 2 * I * H), H, act_.data, I, 2 * I, H,
+                        B200_EPI_SWIGLU, nullptr, 0, &s_gu));
+    if (s_gu > 1) {
+      ++launches_;
+      B200_RETURN_IF(b200::splitk_reduce(ws, s_gu, T, 2 * I, B200_EPI_SWIGLU, nullptr, nullptr, 0, act_.data, I, st));
+    }
+    B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, (int64_t)l * H * I), I, hidden_.data, H, H, I, B200_EPI_RESIDUAL,
+                        hidden_.data, H, &s_d));
+    const void* next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
+    if (s_d > 1) {
+      ++launches_;
+      if (next_norm)
+        B200_RETURN_IF(b200::splitk_residual_rmsnorm(ws, s_d, T, H, hidden_.data, next_norm, normed_.data, cfg_.eps,
+                                                     st));
+      else
+        B200_RETURN_IF(b200::splitk_reduce(ws, s_d, T, H, B200_EPI_RESIDUAL, nullptr, hidden_.data, H, hidden_.data,
+                                           H, st));
+    } else if (next_norm) {
+      ++launches_;
+      B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, next_norm, normed_.data, nullptr, T, H, H, cfg_.eps, st));
+    }
   }
   return STATUS_OK;
 }
@@ -294,12 +331,22 @@ Status DecoderModel::Head(int64_t rows, bool gather, int64_t* next_tokens, bool 
   const int64_t H = cfg_.hidden, V = cfg_.vocab;
   const void* src = hidden_.data;
   if (gather) {
+    ++launches_;
     B200_RETURN_IF(GatherRows(hidden_.data, last_idx_.as<int32_t>(), rows, H, last_hidden_.data, st));
     src = last_hidden_.data;
   }
+  ++launches_;
   B200_RETURN_IF(b200_rmsnorm(src, nullptr, final_norm_.data, normed_.data, nullptr, rows, H, H, cfg_.eps, st));
-  B200_RETURN_IF(b200_gemm_bf16(normed_.data, H, lm_head_.data, H, logits_.data, V, rows, V, H, B200_EPI_NONE, nullptr,
-                                nullptr, 0, gemm_ws_.data, gemm_ws_bytes_, st));
+  int splits = 1;
+  ++launches_;
+  B200_RETURN_IF(b200::gemm_launch(normed_.data, H, lm_head_.data, H, logits_.data, V, rows, V, H, B200_EPI_NONE,
+                                   nullptr, nullptr, 0, gemm_ws_.data, gemm_ws_bytes_, st, &splits));
+  if (splits > 1) {
+    ++launches_;
+    B200_RETURN_IF(b200::splitk_reduce(gemm_ws_.as<float>(), splits, rows, V, B200_EPI_NONE, nullptr, nullptr, 0,
+                                       logits_.data, V, st));
+  }
+  ++launches_;
   B200_RETURN_IF(b200_argmax(logits_.data, rows, V, V, next_.as<int64_t>(), st));
   (void)next_tokens;
   (void)next_on_device;
@@ -364,8 +411,10 @@ Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32
     B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
                                       st));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), T, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  launches_ = 2;  // rope table + embedding
   B200_RETURN_IF(RunLayers(T, false, 0));
   B200_RETURN_IF(Head(num_seqs, true, next_tokens, next_on_device, logits));
+  last_prefill_launches_ = launches_;
   if (logits)
     B200_RETURN_IF(FromCuda(cudaMemcpyAsync(logits, logits_.data, (size_t)num_seqs * cfg_.vocab * 2,
                                             cudaMemcpyDeviceToDevice, st)));
@@ -389,8 +438,11 @@ Status DecoderModel::DecodeDevice(int batch) {
     B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), batch, hd, cfg_.rope_theta, cos_.as<float>(),
                                       sin_.as<float>(), st));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), batch, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  launches_ = 3;  // prepare + rope table + embedding
   B200_RETURN_IF(RunLayers(batch, true, batch));
-  return Head(batch, false, nullptr, true, nullptr);
+  B200_RETURN_IF(Head(batch, false, nullptr, true, nullptr));
+  last_decode_launches_ = launches_;
+  return STATUS_OK;
 }
 
 Status DecoderModel::Decode(const int64_t* ids, bool ids_on_device, const int32_t* slots, int batch,
@@ -451,19 +503,8 @@ Status DecoderModel::Decode(const int64_t* ids, bool ids_on_device, const int32_
   return STATUS_OK;
 }
 
-int DecoderModel::DecodeLaunches() const {
-  // prepare + rope table + embedding; per layer: 2 norms, qk-norm-rope,
-  // attention (+ combine), 4 GEMMs (+ split-K reduces); head: norm, GEMM(s), argmax
-  const int B = opt_.max_batch;
-  const int64_t H = cfg_.hidden, I = cfg_.intermediate, QKV = cfg_.qkv_dim(), AO = (int64_t)cfg_.heads * 128;
-  auto g = [&](int64_t N, int64_t K) { return b200_gemm_workspace_bytes(B, N, K, 0) > 0 ? 2 : 1; };
-  const int attn = b200_paged_decode_workspace_bytes(B, cfg_.heads, 128, opt_.max_context) > 0 ? 2 : 1;
-  const int per_layer = 2 + 1 + attn + g(QKV, H) + g(H, AO) + g(2 * I, H) + g(H, I);
-  return 3 + cfg_.layers * per_layer + 2 + g(cfg_.vocab, H);
-}
+int DecoderModel::DecodeLaunches() const { return last_decode_launches_; }
 
-int DecoderModel::PrefillLaunches() const {
-  return 2 + cfg_.layers * 8 + 4;
-}
+int DecoderModel::PrefillLaunches() const { return last_prefill_launches_; }
 
 }  // namespace b200llm

@@ -94,6 +94,9 @@ class DecoderModel {
   int max_blocks_ = 0;
   int64_t num_blocks_ = 0, max_t_ = 0;
   int cur_num_seqs_ = 0, cur_max_len_ = 0;  // shape of the prefill in flight
+  // kernel launches counted while the last decode step / prefill was enqueued
+  // (a replayed decode graph launches what its capture counted)
+  int launches_ = 0, last_decode_launches_ = 0, last_prefill_launches_ = 0;
 
   // weights (all layers stacked)
   DeviceTensor embed_, lm_head_, final_norm_;

@@ -1,0 +1,21 @@
+// Internal launchers for consumers that finish a split-K projection (the
+// projection stored fp32 partial tiles [splits][rows][cols]; see gemm.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+// b200_qk_norm_rope, optionally reading the qkv projection from split-K
+// partials [splits][T][row_stride] (and writing every head back to qkv).
+int qk_norm_rope_launch(void* qkv, int64_t T, int nq, int nkv, int head_dim, int64_t row_stride, const void* q_norm_w,
+                        const void* k_norm_w, float eps, const float* cos_tab, const float* sin_tab,
+                        const int64_t* slot_mapping, void* k_cache, void* v_cache, int64_t num_blocks, int block_size,
+                        const float* partials, int splits, cudaStream_t stream);
+
+// hidden[rows, dim] += sum_s partials[s]; normed = rmsnorm(hidden) * weight.
+int splitk_residual_rmsnorm(const float* partials, int splits, int64_t rows, int64_t dim, void* hidden,
+                            const void* weight, void* normed, float eps, cudaStream_t stream);
+
+}  // namespace b200

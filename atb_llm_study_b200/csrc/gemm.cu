@@ -15,8 +15,10 @@
 // Skinny problems (few token rows, the decode case) run "swapped": the weight
 // matrix feeds the 128-row MMA side and the tokens the N side, and the
 // epilogue writes the transpose.  When there are too few output tiles to
-// cover the SMs the K loop is split and fp32 partials go to a workspace that
-// a second kernel reduces while applying the epilogue.
+// cover the SMs the K loop is split: each split stores its fp32 partial tile
+// in a workspace slice with plain coalesced stores, and the reduction (with
+// the epilogue) runs in the consumer — splitk_reduce for the C ABI call, or a
+// kernel that reads the result anyway (residual + RMSNorm, QK-norm + rope).
 //
 // No TMA multicast is used (the library also runs in multi-GPU jobs).
 #include <math.h>
@@ -57,7 +59,7 @@ struct Params {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* R;
   int64_t ldr;
-  float* ws;  // split-K partials [splits][tokens][features]
+  float* ws;  // split-K fp32 partial tiles [splits][tokens][features]
   unsigned* err;
 };
 
@@ -93,6 +95,55 @@ __device__ __forceinline__ float epi1(float v, int64_t tok, int64_t f, const Par
   if (EPI == B200_EPI_BIAS_GELU) v = gelu_tanh_f(v);
   if (EPI == B200_EPI_RESIDUAL || EPI == B200_EPI_BIAS_RESIDUAL) v += bf2f(p.R[tok * p.ldr + f]);
   return v;
+}
+
+// Store one 32-column chunk of accumulator values for MMA row `row`, columns
+// [col0, col0+32), applying the epilogue.  Normal orientation: row = token,
+// columns = features (vector stores).  Swapped: row = feature (consecutive
+// features in consecutive lanes), columns = tokens.
+template <int EPI, bool SWAP>
+__device__ __forceinline__ void emit_chunk(float v[32], int64_t row, int64_t col0, int lane, const Params& p) {
+  if (!SWAP) {
+    if (row >= p.rows) return;
+    if (EPI == B200_EPI_SWIGLU) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int64_t c = col0 + g * 8;
+        if (c < p.cols) {
+          uint2 o;
+          o.x = pack2(silu_f(v[8 * g]) * v[8 * g + 1], silu_f(v[8 * g + 2]) * v[8 * g + 3]);
+          o.y = pack2(silu_f(v[8 * g + 4]) * v[8 * g + 5], silu_f(v[8 * g + 6]) * v[8 * g + 7]);
+          *reinterpret_cast<uint2*>(p.C + row * p.ldc + c / 2) = o;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int64_t c = col0 + g * 8;
+        if (c < p.cols) {
+          float* vv = v + 8 * g;
+          epi8<EPI>(vv, row, c, p);
+          *reinterpret_cast<uint4*>(p.C + row * p.ldc + c) = pack8(vv);
+        }
+      }
+    }
+  } else if (EPI == B200_EPI_SWIGLU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+      if (!(lane & 1) && row < p.rows && col0 + i < p.cols) p.C[(col0 + i) * p.ldc + row / 2] = f2bf(silu_f(v[i]) * up);
+    }
+  } else if (row < p.rows) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < p.cols) p.C[(col0 + i) * p.ldc + row] = f2bf(epi1<EPI>(v[i], col0 + i, row, p));
+  }
+}
+
+// Index of (MMA row, MMA column) in the split-K accumulator ws[token][feature].
+template <bool SWAP>
+__device__ __forceinline__ int64_t ws_index(int64_t row, int64_t col, const Params& p) {
+  return SWAP ? col * p.rows + row : row * p.cols + col;
 }
 
 __device__ __forceinline__ void decode_unit(int w, const Params& p, int& tm, int& tn, int& kb0, int& kb1) {
@@ -246,61 +297,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         const int64_t col0 = (int64_t)tn * BN + ch * 32;
-        if (!SWAP) {
-          // row = token, columns = features
+        if (PARTIAL) {
+          // this K slice's partial tile -> ws[split][token][feature] (plain coalesced stores)
           if (row < p.rows) {
-            if (PARTIAL) {
-              float* dst = p.ws + ((int64_t)split * p.rows + row) * p.cols;
+            float* base = p.ws + (int64_t)split * p.rows * p.cols;
+            if (!SWAP && col0 + 32 <= p.cols) {
 #pragma unroll
               for (int g = 0; g < 8; ++g)
-                if (col0 + g * 4 < p.cols)
-                  *reinterpret_cast<float4*>(dst + col0 + g * 4) =
-                      make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-            } else if (EPI == B200_EPI_SWIGLU) {
-#pragma unroll
-              for (int g = 0; g < 4; ++g) {
-                const int64_t c = col0 + g * 8;
-                if (c < p.cols) {
-                  uint2 o;
-                  o.x = pack2(silu_f(v[8 * g]) * v[8 * g + 1], silu_f(v[8 * g + 2]) * v[8 * g + 3]);
-                  o.y = pack2(silu_f(v[8 * g + 4]) * v[8 * g + 5], silu_f(v[8 * g + 6]) * v[8 * g + 7]);
-                  *reinterpret_cast<uint2*>(p.C + row * p.ldc + c / 2) = o;
-                }
-              }
+                __stcg(reinterpret_cast<float4*>(base + ws_index<SWAP>(row, col0 + 4 * g, p)),
+                       make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
             } else {
 #pragma unroll
-              for (int g = 0; g < 4; ++g) {
-                const int64_t c = col0 + g * 8;
-                if (c < p.cols) {
-                  float* vv = v + 8 * g;
-                  epi8<EPI>(vv, row, c, p);
-                  *reinterpret_cast<uint4*>(p.C + row * p.ldc + c) = pack8(vv);
-                }
-              }
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.cols) __stcg(base + ws_index<SWAP>(row, col0 + i, p), v[i]);
             }
           }
         } else {
-          // row = feature (lanes hold consecutive features), columns = tokens
-          if (PARTIAL) {
-            if (row < p.rows) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < p.cols) p.ws[((int64_t)split * p.cols + col0 + i) * p.rows + row] = v[i];
-            }
-          } else if (EPI == B200_EPI_SWIGLU) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
-              if (!(lane & 1) && row < p.rows && col0 + i < p.cols)
-                p.C[(col0 + i) * p.ldc + row / 2] = f2bf(silu_f(v[i]) * up);
-            }
-          } else {
-            if (row < p.rows) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < p.cols) p.C[(col0 + i) * p.ldc + row] = f2bf(epi1<EPI>(v[i], col0 + i, row, p));
-            }
-          }
+          emit_chunk<EPI, SWAP>(v, row, col0, lane, p);
         }
       }
       tc_fence_before();
@@ -313,33 +326,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
-  }
-}
-
-// Sum split-K partials ws[s][tok][feat] and apply the epilogue.
-// One thread per 8 features (SwiGLU: per 8 interleaved features -> 4 outputs).
-template <int EPI>
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t tokens, int64_t feats,
-                                     Params p) {
-  const int64_t nv = feats / 8;
-  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (gid >= tokens * nv) return;
-  const int64_t tok = gid / nv, f0 = (gid % nv) * 8;
-  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int s = 0; s < splits; ++s) {
-    const float4* src = reinterpret_cast<const float4*>(ws + ((int64_t)s * tokens + tok) * feats + f0);
-    const float4 a = src[0], b = src[1];
-    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
-  }
-  if (EPI == B200_EPI_SWIGLU) {
-    uint2 o;
-    o.x = pack2(silu_f(v[0]) * v[1], silu_f(v[2]) * v[3]);
-    o.y = pack2(silu_f(v[4]) * v[5], silu_f(v[6]) * v[7]);
-    *reinterpret_cast<uint2*>(p.C + tok * p.ldc + f0 / 2) = o;
-  } else {
-    epi8<EPI>(v, tok, f0, p);
-    *reinterpret_cast<uint4*>(p.C + tok * p.ldc + f0) = pack8(v);
   }
 }
 
@@ -402,8 +388,36 @@ int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int gr
   return B200_OK;
 }
 
+// Sum split-K partials ws[s][tok][feat] and apply the epilogue.  One thread per
+// 8 features (SwiGLU: 8 interleaved gate/up features -> 4 outputs).
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t tokens, int64_t feats,
+                                     Params p) {
+  const int64_t nv = feats / 8;
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (gid >= tokens * nv) return;
+  const int64_t tok = gid / nv, f0 = (gid % nv) * 8;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < splits; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(ws + ((int64_t)s * tokens + tok) * feats + f0);
+    const float4 a = src[0], b = src[1];
+    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  }
+  if (EPI == B200_EPI_SWIGLU) {
+    uint2 o;
+    o.x = pack2(silu_f(v[0]) * v[1], silu_f(v[2]) * v[3]);
+    o.y = pack2(silu_f(v[4]) * v[5], silu_f(v[6]) * v[7]);
+    *reinterpret_cast<uint2*>(p.C + tok * p.ldc + f0 / 2) = o;
+  } else {
+    epi8<EPI>(v, tok, f0, p);
+    *reinterpret_cast<uint4*>(p.C + tok * p.ldc + f0) = pack8(v);
+  }
+}
+
 template <int BN, bool SWAP, bool PARTIAL>
 int launch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const Params& p, int grid, cudaStream_t st) {
+  // split-K units only store partials: the epilogue runs where they are reduced
   if (PARTIAL) return launch_t<BN, B200_EPI_NONE, SWAP, true>(a, b, p, grid, st);
   switch (epi) {
     case B200_EPI_NONE: return launch_t<BN, B200_EPI_NONE, SWAP, false>(a, b, p, grid, st);
@@ -416,20 +430,27 @@ int launch_epi(int epi, const CUtensorMap& a, const CUtensorMap& b, const Params
   return B200_ERROR_INVALID_PARAM;
 }
 
-int launch_reduce(int epi, const Params& p, int64_t tokens, int64_t feats, cudaStream_t st) {
-  const int64_t n = tokens * (feats / 8);
-  const unsigned g = (unsigned)((n + 255) / 256);
-  switch (epi) {
-    case B200_EPI_NONE: splitk_reduce_kernel<B200_EPI_NONE><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    case B200_EPI_BIAS: splitk_reduce_kernel<B200_EPI_BIAS><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    case B200_EPI_RESIDUAL: splitk_reduce_kernel<B200_EPI_RESIDUAL><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    case B200_EPI_SWIGLU: splitk_reduce_kernel<B200_EPI_SWIGLU><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    case B200_EPI_BIAS_GELU: splitk_reduce_kernel<B200_EPI_BIAS_GELU><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    case B200_EPI_BIAS_RESIDUAL: splitk_reduce_kernel<B200_EPI_BIAS_RESIDUAL><<<g, 256, 0, st>>>(p.ws, p.splits, tokens, feats, p); break;
-    default: return B200_ERROR_INVALID_PARAM;
-  }
-  B200_CHECK_LAUNCH();
-  return B200_OK;
+Params make_params(const b200::GemmPlan& g, int64_t M, int64_t N, int64_t K, void* Cp, int64_t ldc, const void* bias,
+                   const void* R, int64_t ldr, void* ws) {
+  Params p;
+  p.rows = g.swap ? N : M;
+  p.cols = g.swap ? M : N;
+  p.K = K;
+  p.tiles_m = g.tiles_m;
+  p.tiles_n = g.tiles_n;
+  p.splits = g.splits;
+  p.kb_total = g.kb_total;
+  p.kb_per_split = g.kb_per_split;
+  p.C = static_cast<__nv_bfloat16*>(Cp);
+  p.ldc = ldc;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.R = static_cast<const __nv_bfloat16*>(R);
+  p.ldr = ldr;
+  p.ws = g.splits > 1 ? static_cast<float*>(ws) : nullptr;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  p.err = b200::error_word(dev);
+  return p;
 }
 
 }  // namespace
@@ -442,27 +463,27 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
   const int64_t mma_rows = g.swap ? N : M;
   const int64_t mma_cols = g.swap ? M : N;
   if (g.swap) g.bn = mma_cols <= 64 ? 64 : 128;
-  else g.bn = (mma_cols >= 2048 || mma_cols > 128) ? 256 : 128;
+  else g.bn = mma_cols > 128 ? 256 : 128;
   g.tiles_m = (int)((mma_rows + BM - 1) / BM);
   g.tiles_n = (int)((mma_cols + g.bn - 1) / g.bn);
   g.kb_total = (int)((K + BK - 1) / BK);
   const int tiles = g.tiles_m * g.tiles_n;
-  // Split K only when the output tiles leave SMs idle: pick the split count
-  // (<= 16, >= 4 k-blocks per split) with the best wave efficiency.
+  // Split K only when the output tiles leave SMs idle.  Each split keeps
+  // >= 16 k-blocks (its pipeline fill stays small next to its weight stream)
+  // and every extra split is charged 3 % for its partial-tile traffic.
   int best = 1;
-  double best_eff = (double)tiles / ((double)sms * ((tiles + sms - 1) / sms));
   if (tiles < 2 * sms) {
+    double best_score = (double)tiles / ((double)sms * ((tiles + sms - 1) / sms)) - 0.03;
     for (int s = 2; s <= 16; ++s) {
-      if (g.kb_total / s < 4) break;
+      if (g.kb_total / s < 16) break;
       const int u = tiles * s;
-      const double eff = (double)u / ((double)sms * ((u + sms - 1) / sms));
-      if (eff > best_eff + 0.05) {
-        best_eff = eff;
+      const double score = (double)u / ((double)sms * ((u + sms - 1) / sms)) - 0.03 * s;
+      if (score > best_score + 0.02) {
+        best_score = score;
         best = s;
       }
     }
   }
-  g.splits = best;
   g.kb_per_split = (g.kb_total + best - 1) / best;
   g.splits = (g.kb_total + g.kb_per_split - 1) / g.kb_per_split;
   g.ws_bytes = g.splits > 1 ? (int64_t)g.splits * M * N * (int64_t)sizeof(float) : 0;
@@ -470,9 +491,10 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
   return g;
 }
 
-int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
-             int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
-             cudaStream_t st) {
+int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
+                int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
+                cudaStream_t st, int* splits_out) {
+  if (splits_out) *splits_out = 1;
   if (!A || !B || !Cp || M < 0 || N < 0 || K <= 0) return B200_ERROR_INVALID_PARAM;
   if (epi < B200_EPI_NONE || epi > B200_EPI_BIAS_RESIDUAL) return B200_ERROR_INVALID_PARAM;
   if (K % 8 || lda % 8 || ldb % 8 || ldc % 8 || lda < K || ldb < K || N % 8) return B200_ERROR_INVALID_PARAM;
@@ -490,29 +512,11 @@ int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, i
 
   const int sms = num_sms();
   GemmPlan g = plan_gemm(M, N, K, epi, sms);
-  if (g.splits > 1 && (!ws || ws_bytes < g.ws_bytes)) {
+  if (g.splits > 1 && (!splits_out || !ws || ws_bytes < g.ws_bytes)) {
     g.splits = 1;
     g.kb_per_split = g.kb_total;
   }
-  Params p;
-  p.rows = g.swap ? N : M;
-  p.cols = g.swap ? M : N;
-  p.K = K;
-  p.tiles_m = g.tiles_m;
-  p.tiles_n = g.tiles_n;
-  p.splits = g.splits;
-  p.kb_total = g.kb_total;
-  p.kb_per_split = g.kb_per_split;
-  p.C = static_cast<__nv_bfloat16*>(Cp);
-  p.ldc = ldc;
-  p.bias = static_cast<const __nv_bfloat16*>(bias);
-  p.R = static_cast<const __nv_bfloat16*>(R);
-  p.ldr = ldr;
-  p.ws = static_cast<float*>(ws);
-  int dev = 0;
-  cudaGetDevice(&dev);
-  p.err = error_word(dev);
-
+  const Params p = make_params(g, M, N, K, Cp, ldc, bias, R, ldr, ws);
   CUtensorMap ta, tb;
   const void* mA = g.swap ? B : A;  // operand on the 128-row MMA side
   const void* mB = g.swap ? A : B;
@@ -533,8 +537,37 @@ int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, i
   } else {
     rc = partial ? launch_epi<64, true, true>(epi, ta, tb, p, grid, st) : launch_epi<64, true, false>(epi, ta, tb, p, grid, st);
   }
-  if (rc != B200_OK || !partial) return rc;
-  return launch_reduce(epi, p, M, N, st);
+  if (rc == B200_OK && splits_out) *splits_out = g.splits;
+  return rc;
+}
+
+int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epi, const void* bias, const void* R,
+                  int64_t ldr, void* Cp, int64_t ldc, cudaStream_t st) {
+  GemmPlan g;
+  g.splits = splits;
+  Params p = make_params(g, M, N, 0, Cp, ldc, bias, R, ldr, nullptr);
+  const int64_t n = M * (N / 8);
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  switch (epi) {
+    case B200_EPI_NONE: splitk_reduce_kernel<B200_EPI_NONE><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_BIAS: splitk_reduce_kernel<B200_EPI_BIAS><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_RESIDUAL: splitk_reduce_kernel<B200_EPI_RESIDUAL><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_SWIGLU: splitk_reduce_kernel<B200_EPI_SWIGLU><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_BIAS_GELU: splitk_reduce_kernel<B200_EPI_BIAS_GELU><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_BIAS_RESIDUAL: splitk_reduce_kernel<B200_EPI_BIAS_RESIDUAL><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    default: return B200_ERROR_INVALID_PARAM;
+  }
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
+             int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
+             cudaStream_t st) {
+  int splits = 1;
+  int rc = gemm_launch(A, lda, B, ldb, Cp, ldc, M, N, K, epi, bias, R, ldr, ws, ws_bytes, st, &splits);
+  if (rc != B200_OK || splits <= 1) return rc;
+  return splitk_reduce(static_cast<const float*>(ws), splits, M, N, epi, bias, R, ldr, Cp, ldc, st);
 }
 
 }  // namespace b200
@@ -550,3 +583,4 @@ extern "C" int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, in
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   return b200::plan_gemm(M, N, K, epilogue, num_sms()).ws_bytes;
 }
+

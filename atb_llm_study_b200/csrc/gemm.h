@@ -16,6 +16,20 @@ struct GemmPlan {
 
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms);
 
+// Launch the GEMM.  When the plan splits K, `ws` holds ws_bytes of the plan and
+// splits_out is not null, the kernel only stores fp32 partial tiles
+// ws[split][M][N] and *splits_out returns the split count: the caller reduces
+// them (splitk_reduce, or a consumer kernel that fuses the reduction).
+// Otherwise the epilogue is applied and *splits_out = 1.
+int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
+                int64_t K, int epilogue, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
+                cudaStream_t stream, int* splits_out);
+
+// C[M, N'] = epilogue(sum_s ws[s][M][N]).
+int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epilogue, const void* bias, const void* R,
+                  int64_t ldr, void* C, int64_t ldc, cudaStream_t stream);
+
+// gemm_launch followed by splitk_reduce when K was split (the C ABI call).
 int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
              int64_t K, int epilogue, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
              cudaStream_t stream);

@@ -73,6 +73,52 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
   }
 }
 
+// One CTA per row: h = hidden + sum_s partials[s][row] (a split-K projection
+// finished here), hidden = bf16(h), out = rmsnorm(bf16(h)) * w.
+template <int CH>
+__global__ void __launch_bounds__(kNormThreads) splitk_residual_rmsnorm_kernel(const float* __restrict__ partials,
+                                                                               int splits, int64_t rows,
+                                                                               __nv_bfloat16* hidden,
+                                                                               const __nv_bfloat16* __restrict__ w,
+                                                                               __nv_bfloat16* __restrict__ out,
+                                                                               int64_t dim, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int64_t nchunk = dim / 8;
+  float v[CH][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) {
+      unpack8(*reinterpret_cast<const uint4*>(hidden + row * dim + idx * 8), v[c]);
+      for (int s = 0; s < splits; ++s) {
+        const float4* src = reinterpret_cast<const float4*>(partials + ((int64_t)s * rows + row) * dim + idx * 8);
+        const float4 a = src[0], b = src[1];
+        v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
+        v[c][4] += b.x; v[c][5] += b.y; v[c][6] += b.z; v[c][7] += b.w;
+      }
+      const uint4 hb = pack8(v[c]);
+      *reinterpret_cast<uint4*>(hidden + row * dim + idx * 8) = hb;
+      unpack8(hb, v[c]);  // normalise the stored (bf16) residual stream
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
+    }
+  }
+  const float inv = rsqrtf(block_sum<kNormThreads>(ss, red) / (float)dim + eps);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) {
+      float g[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(w + idx * 8), g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * inv * g[i];
+      *reinterpret_cast<uint4*>(out + row * dim + idx * 8) = pack8(o);
+    }
+  }
+}
+
 template <int CH>
 __global__ void __launch_bounds__(kNormThreads) layernorm_kernel(const __nv_bfloat16* __restrict__ x,
                                                                  const __nv_bfloat16* __restrict__ g,
@@ -163,7 +209,12 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
                                                            const float* __restrict__ sin_tab,
                                                            const int64_t* __restrict__ slots,
                                                            __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                                                           int64_t num_blocks, int block_size, unsigned* err) {
+                                                           int64_t num_blocks, int block_size, unsigned* err,
+                                                           const float* __restrict__ partials, int splits,
+                                                           int64_t p_ld, int64_t p_slice) {
+  // partials != null: the projection was split along K and qkv holds nothing
+  // yet; every head is summed from the fp32 partial tiles
+  // partials[s][t][p_ld] and written to qkv (v too, for prefill attention).
   constexpr int E = HD / 32;
   const int64_t t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -187,9 +238,26 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
   for (int h = warp; h < nheads; h += blockDim.x / 32) {
     __nv_bfloat16* hp = row + (int64_t)h * HD + lane * E;
     float x[E];
+    if (partials) {
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = bf2f(hp[e]);
+      for (int e = 0; e < E; ++e) x[e] = 0.f;
+      const float* src = partials + t * p_ld + (int64_t)h * HD + lane * E;
+      for (int s = 0; s < splits; ++s) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] += src[(int64_t)s * p_slice + e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] = bf2f(hp[e]);
+    }
     const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
+    if (partials && !is_q && !is_k) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        hp[e] = f2bf(x[e]);
+        x[e] = bf2f(hp[e]);  // the cache holds the same bf16 value as qkv
+      }
+    }
     if (is_q || is_k) {
       const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
       if (nw) {
@@ -266,19 +334,40 @@ __global__ void scatter_add_kernel(__nv_bfloat16* hidden, int64_t rows, int64_t 
   }
 }
 
-__global__ void __launch_bounds__(256) argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab,
-                                                     int64_t ld, int64_t* __restrict__ out) {
-  __shared__ float sv[8];
-  __shared__ int64_t si[8];
+constexpr int kArgmaxThreads = 512;
+
+// One CTA per row.  With 16-byte aligned rows each thread reads 8 logits per
+// load; indices a thread visits only increase, so `>` keeps the lowest index
+// on ties, and the reductions below break ties toward the lower index.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                                int64_t vocab, int64_t ld, int64_t* __restrict__ out) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int64_t si[kArgmaxThreads / 32];
   const int64_t r = blockIdx.x;
   const __nv_bfloat16* row = logits + r * ld;
   float best = -INFINITY;
   int64_t bi = INT64_MAX;
-  for (int64_t j = threadIdx.x; j < vocab; j += blockDim.x) {
-    const float v = bf2f(row[j]);
-    if (v > best) {  // j increases per thread, so ties keep the lowest index
-      best = v;
-      bi = j;
+  const bool vec = (vocab % 8 == 0) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  if (vec) {
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+    for (int64_t c = threadIdx.x; c < vocab / 8; c += blockDim.x) {
+      float f[8];
+      unpack8(__ldg(rv + c), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (f[i] > best) {
+          best = f[i];
+          bi = c * 8 + i;
+        }
+    }
+  } else {
+    for (int64_t j = threadIdx.x; j < vocab; j += blockDim.x) {
+      const float v = bf2f(row[j]);
+      if (v > best) {
+        best = v;
+        bi = j;
+      }
     }
   }
 #pragma unroll
@@ -297,7 +386,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const __nv_bfloat16* __rest
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int i = 1; i < 8; ++i)
+    for (int i = 1; i < kArgmaxThreads / 32; ++i)
       if (sv[i] > best || (sv[i] == best && si[i] < bi)) {
         best = sv[i];
         bi = si[i];
@@ -426,15 +515,18 @@ extern "C" int b200_rope_table_1d(const int64_t* positions, int64_t T, int head_
   return rope_table(positions, T, head_dim, theta, 0, 0, 0, cos_out, sin_out, stream);
 }
 
-extern "C" int b200_qk_norm_rope(void* qkv, int64_t T, int nq, int nkv, int head_dim, int64_t row_stride,
-                                 const void* q_norm_w, const void* k_norm_w, float eps, const float* cos_tab,
-                                 const float* sin_tab, const int64_t* slot_mapping, void* k_cache, void* v_cache,
-                                 int64_t num_blocks, int block_size, b200_stream_t stream) {
+namespace b200 {
+
+int qk_norm_rope_launch(void* qkv, int64_t T, int nq, int nkv, int head_dim, int64_t row_stride, const void* q_norm_w,
+                        const void* k_norm_w, float eps, const float* cos_tab, const float* sin_tab,
+                        const int64_t* slot_mapping, void* k_cache, void* v_cache, int64_t num_blocks, int block_size,
+                        const float* partials, int splits, cudaStream_t stream) {
   if (!qkv || !cos_tab || !sin_tab || T < 0 || nq <= 0 || nkv <= 0 || nq % nkv ||
       row_stride < (int64_t)(nq + 2 * nkv) * head_dim)
     return B200_ERROR_INVALID_PARAM;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return B200_ERROR_INVALID_PARAM;
   if (slot_mapping && (!k_cache || !v_cache || block_size <= 0 || num_blocks <= 0)) return B200_ERROR_INVALID_PARAM;
+  if (partials && splits <= 0) return B200_ERROR_INVALID_PARAM;
   if (T == 0) return B200_OK;
   auto q = static_cast<__nv_bfloat16*>(qkv);
   auto qn = static_cast<const __nv_bfloat16*>(q_norm_w);
@@ -442,15 +534,49 @@ extern "C" int b200_qk_norm_rope(void* qkv, int64_t T, int nq, int nkv, int head
   auto kc = static_cast<__nv_bfloat16*>(k_cache);
   auto vc = static_cast<__nv_bfloat16*>(v_cache);
   unsigned* err = current_error_word();
+  const int64_t p_ld = row_stride, p_slice = T * row_stride;  // partials [splits][T][row_stride]
   dim3 g((unsigned)T);
   switch (head_dim) {
-    case 32: qk_norm_rope_kernel<32><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err); break;
-    case 64: qk_norm_rope_kernel<64><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err); break;
-    case 128: qk_norm_rope_kernel<128><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err); break;
+    case 32: qk_norm_rope_kernel<32><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
+    case 64: qk_norm_rope_kernel<64><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
+    case 128: qk_norm_rope_kernel<128><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
   return B200_OK;
+}
+
+int splitk_residual_rmsnorm(const float* partials, int splits, int64_t rows, int64_t dim, void* hidden,
+                            const void* weight, void* normed, float eps, cudaStream_t stream) {
+  if (!partials || splits <= 0 || !hidden || !weight || !normed || rows < 0 || dim <= 0 || dim % 8)
+    return B200_ERROR_INVALID_PARAM;
+  if (rows == 0) return B200_OK;
+  const int64_t per = (dim / 8 + kNormThreads - 1) / kNormThreads;
+  auto h = static_cast<__nv_bfloat16*>(hidden);
+  auto w = static_cast<const __nv_bfloat16*>(weight);
+  auto o = static_cast<__nv_bfloat16*>(normed);
+  dim3 g((unsigned)rows);
+  switch (per) {
+    case 1: splitk_residual_rmsnorm_kernel<1><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    case 2: splitk_residual_rmsnorm_kernel<2><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    case 3:
+    case 4: splitk_residual_rmsnorm_kernel<4><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    case 5: case 6: case 7:
+    case 8: splitk_residual_rmsnorm_kernel<8><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    default: return B200_ERROR_UNSUPPORTED;
+  }
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+}  // namespace b200
+
+extern "C" int b200_qk_norm_rope(void* qkv, int64_t T, int nq, int nkv, int head_dim, int64_t row_stride,
+                                 const void* q_norm_w, const void* k_norm_w, float eps, const float* cos_tab,
+                                 const float* sin_tab, const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                 int64_t num_blocks, int block_size, b200_stream_t stream) {
+  return b200::qk_norm_rope_launch(qkv, T, nq, nkv, head_dim, row_stride, q_norm_w, k_norm_w, eps, cos_tab, sin_tab,
+                                   slot_mapping, k_cache, v_cache, num_blocks, block_size, nullptr, 0, stream);
 }
 
 extern "C" int b200_slot_mapping(const int32_t* block_tables, int max_blocks_per_seq, const int32_t* seq_ids,
@@ -493,7 +619,8 @@ extern "C" int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int6
                            b200_stream_t stream) {
   if (!logits || !out || rows < 0 || vocab <= 0 || ld < vocab) return B200_ERROR_INVALID_PARAM;
   if (rows == 0) return B200_OK;
-  argmax_kernel<<<(unsigned)rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), vocab, ld, out);
+  argmax_kernel<<<(unsigned)rows, kArgmaxThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), vocab, ld,
+                                                               out);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }

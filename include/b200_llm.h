@@ -116,6 +116,9 @@ enum b200_epilogue {
  * Row strides lda/ldb/ldc/ldr in elements; K, lda, ldb, ldc, ldr multiples of 8;
  * 16-byte aligned base pointers.  `workspace` (may be NULL) enables split-K
  * for skinny problems; b200_gemm_workspace_bytes() gives the size it can use.
+ * With split-K each K slice stores its fp32 partial tile in the workspace and
+ * a second kernel sums them and applies the epilogue; calls that overlap on
+ * the GPU must not share a workspace.
  * Replaces LinearOp::Create(transB=true) (atb_cpp_llm/src/ops/linear_op.cpp:7-20)
  * and the SiLU/Mul/Add ops fused into its consumers
  * (atb_cpp_llm/src/components/common/mlp_builder.cpp:12-56). */

@@ -90,14 +90,18 @@ def max_rel_err(out, ref):
 
 
 def gemm(A, B, epi=0, bias=None, R=None, out=None, ws=True):
-    """C = epi(A @ B^T) through b200_gemm_bf16 (torch bf16 device tensors)."""
+    """C = epi(A @ B^T) through b200_gemm_bf16 (torch bf16 device tensors).
+    ws: True = a fresh zeroed split-K workspace, False = none, or a tensor to reuse."""
     M, K = A.shape
     N = B.shape[0]
     outN = N // 2 if epi == 3 else N
     if out is None:
         out = torch.empty(M, outN, dtype=torch.bfloat16, device=DEV)
-    wsb = L().b200_gemm_workspace_bytes(M, N, K, epi) if ws else 0
-    wst = torch.empty(max(wsb, 16), dtype=torch.uint8, device=DEV) if wsb else None
+    if isinstance(ws, torch.Tensor):
+        wst, wsb = ws, ws.numel()
+    else:
+        wsb = L().b200_gemm_workspace_bytes(M, N, K, epi) if ws else 0
+        wst = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=DEV) if wsb else None
     check(L().b200_gemm_bf16(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), out.data_ptr(), out.stride(0),
                              M, N, K, epi, ptr(bias), ptr(R), 0 if R is None else R.stride(0), ptr(wst), wsb,
                              stream()), "gemm")

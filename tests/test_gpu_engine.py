@@ -2,6 +2,11 @@
 several packed sequences into the paged KV cache, then greedy decode steps
 (eager first, CUDA-graph replays after), against the numpy whole-model oracle.
 
+Two configurations: "narrow" (every projection runs unsplit) and "wide"
+(decode-sized projections split K, so the fused consumers — QK-norm/rope over
+split-K partials, residual + RMSNorm over split-K partials, SwiGLU reduce —
+are on the path).
+
 Bar: cosine >= 0.999 of every last-token logit row; the greedy token must
 match the oracle's wherever the oracle's top-2 margin exceeds the bf16 noise.
 """
@@ -19,7 +24,6 @@ pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
     import gpu_util as G
-    from atb_llm_study_b200 import capi
 
 
 class EngineConfig(ctypes.Structure):
@@ -28,25 +32,28 @@ class EngineConfig(ctypes.Structure):
                 ("kv_block_size", ctypes.c_int), ("init_seed", ctypes.c_uint64), ("init_std", ctypes.c_float)]
 
 
-CFG = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
-           head_dim=128, intermediate_size=1024, vocab_size=1200, rms_norm_eps=1e-6, rope_theta=1e6,
-           tie_word_embeddings=False)
+NARROW = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
+              head_dim=128, intermediate_size=1024, vocab_size=1200, rms_norm_eps=1e-6, rope_theta=1e6,
+              tie_word_embeddings=False)
+WIDE = dict(NARROW, hidden_size=2048, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+            intermediate_size=4096)
 
 
-def make_weights(seed=0):
+def make_weights(C, seed=0):
     rng = np.random.default_rng(seed)
-    H, I, V, hd = CFG["hidden_size"], CFG["intermediate_size"], CFG["vocab_size"], CFG["head_dim"]
-    nq, nkv = CFG["num_attention_heads"], CFG["num_key_value_heads"]
+    H, I, V, hd = C["hidden_size"], C["intermediate_size"], C["vocab_size"], C["head_dim"]
+    nq, nkv = C["num_attention_heads"], C["num_key_value_heads"]
 
     def n(*s, std=0.05):
         return G.rounded(rng.standard_normal(s).astype(np.float32) * std)
 
-    w = {"embed": n(V, H, std=1.0), "lm_head": n(V, H), "norm": G.rounded(1 + n(H, std=0.1)), "layers": []}
-    for _ in range(CFG["num_hidden_layers"]):
+    std = 0.05 if H <= 512 else 0.02
+    w = {"embed": n(V, H, std=1.0), "lm_head": n(V, H, std=std), "norm": G.rounded(1 + n(H, std=0.1)), "layers": []}
+    for _ in range(C["num_hidden_layers"]):
         w["layers"].append({
-            "q_w": n(nq * hd, H), "k_w": n(nkv * hd, H), "v_w": n(nkv * hd, H), "o_w": n(H, nq * hd),
-            "qn_w": G.rounded(1 + n(hd, std=0.1)), "kn_w": G.rounded(1 + n(hd, std=0.1)),
-            "gate_w": n(I, H), "up_w": n(I, H), "down_w": n(H, I),
+            "q_w": n(nq * hd, H, std=std), "k_w": n(nkv * hd, H, std=std), "v_w": n(nkv * hd, H, std=std),
+            "o_w": n(H, nq * hd, std=std), "qn_w": G.rounded(1 + n(hd, std=0.1)), "kn_w": G.rounded(1 + n(hd, std=0.1)),
+            "gate_w": n(I, H, std=std), "up_w": n(I, H, std=std), "down_w": n(H, I, std=std),
             "iln_w": G.rounded(1 + n(H, std=0.1)), "pln_w": G.rounded(1 + n(H, std=0.1)),
         })
     return w
@@ -58,9 +65,9 @@ HF_NAMES = {"q_w": "self_attn.q_proj", "k_w": "self_attn.k_proj", "v_w": "self_a
             "iln_w": "input_layernorm", "pln_w": "post_attention_layernorm"}
 
 
-def create_engine(w, max_batch=8, max_context=512, block=128):
+def create_engine(C, w, max_batch=8, max_context=512, block=128):
     L = G.L()
-    cfg = EngineConfig(None, json.dumps(CFG).encode(), 0, max_batch, max_context, 1024, block, 7, 0.02)
+    cfg = EngineConfig(None, json.dumps(C).encode(), 0, max_batch, max_context, 1024, block, 7, 0.02)
     eng = ctypes.c_void_p()
     G.check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create")
 
@@ -77,14 +84,14 @@ def create_engine(w, max_batch=8, max_context=512, block=128):
     return eng
 
 
-def oracle_cfg():
-    return dict(heads=CFG["num_attention_heads"], kv_heads=CFG["num_key_value_heads"], head_dim=CFG["head_dim"],
-                eps=CFG["rms_norm_eps"], theta=CFG["rope_theta"])
+def oracle_cfg(C):
+    return dict(heads=C["num_attention_heads"], kv_heads=C["num_key_value_heads"], head_dim=C["head_dim"],
+                eps=C["rms_norm_eps"], theta=C["rope_theta"])
 
 
-def check_rows(logits, seqs, w):
+def check_rows(C, logits, seqs, w):
     for i, s in enumerate(seqs):
-        ref = forward_last_logits(s, w, oracle_cfg())
+        ref = forward_last_logits(s, w, oracle_cfg(C))
         got = logits[i]
         assert G.cosine(got, ref) >= 0.999, (i, G.cosine(got, ref))
         top2 = np.sort(ref)[-2:]
@@ -92,26 +99,28 @@ def check_rows(logits, seqs, w):
             assert int(np.argmax(got)) == int(np.argmax(ref)), i
 
 
-@pytest.mark.parametrize("block", [128, 64])
-def test_engine_prefill_then_decode(block):
-    w = make_weights()
-    eng = create_engine(w, block=block)
+@pytest.mark.parametrize("C,block", [(NARROW, 128), (NARROW, 64), (WIDE, 128)], ids=["narrow-128", "narrow-64", "wide"])
+def test_engine_prefill_then_decode(C, block):
+    w = make_weights(C)
+    eng = create_engine(C, w, block=block)
     L = G.L()
     try:
+        if C is WIDE:  # the decode projections really split K in this configuration
+            assert L.b200_gemm_workspace_bytes(4, 2 * C["intermediate_size"], C["hidden_size"], 3) > 0
         rng = np.random.default_rng(3)
         lens = [5, 17, 130, 64]
         slots = [2, 0, 5, 7]
-        seqs = [rng.integers(0, CFG["vocab_size"], n) for n in lens]
+        seqs = [rng.integers(0, C["vocab_size"], n) for n in lens]
         ids = np.concatenate(seqs).astype(np.int64)
         nxt = np.zeros(len(lens), np.int64)
-        V = CFG["vocab_size"]
+        V = C["vocab_size"]
         logits = torch.empty(len(lens), V, dtype=torch.bfloat16, device=G.DEV)
         lens_a, slots_a = np.array(lens, np.int32), np.array(slots, np.int32)  # kept alive across the call
         G.check(L.b200_engine_prefill(eng, ids.ctypes.data, 0, lens_a.ctypes.data, slots_a.ctypes.data, len(lens),
                                       None, nxt.ctypes.data, 0, logits.data_ptr()), "prefill")
         torch.cuda.synchronize()
         lg = G.host(logits)
-        check_rows(lg, seqs, w)
+        check_rows(C, lg, seqs, w)
         np.testing.assert_array_equal(nxt, np.argmax(lg, 1))
         # decode 4 steps, feeding back the greedy tokens; slot order shuffled
         order = [3, 0, 2, 1]
@@ -125,7 +134,7 @@ def test_engine_prefill_then_decode(block):
             torch.cuda.synchronize()
             for j, i in enumerate(order):
                 seqs[i] = np.append(seqs[i], nxt[i])
-            check_rows(G.host(lgd), [seqs[i] for i in order], w)
+            check_rows(C, G.host(lgd), [seqs[i] for i in order], w)
             for j, i in enumerate(order):
                 nxt[i] = out[j]
                 n = ctypes.c_int64()
@@ -137,8 +146,8 @@ def test_engine_prefill_then_decode(block):
 
 
 def test_engine_rejects_bad_requests():
-    w = make_weights(1)
-    eng = create_engine(w, max_batch=4, max_context=128)
+    w = make_weights(NARROW, 1)
+    eng = create_engine(NARROW, w, max_batch=4, max_context=128)
     L = G.L()
     try:
         ids = np.zeros(8, np.int64)
@@ -155,8 +164,8 @@ def test_engine_rejects_bad_requests():
         rc = L.b200_engine_decode(eng, ids.ctypes.data, 0, one.ctypes.data, 1, nxt.ctypes.data, 0, None)
         assert rc == INVALID
         # unknown model type is refused at create
-        cfg = EngineConfig(None, json.dumps(dict(CFG, model_type="mystery", num_local_experts=8)).encode(), 0, 1, 16,
-                           16, 128, 0, 0.02)
+        cfg = EngineConfig(None, json.dumps(dict(NARROW, model_type="mystery", num_local_experts=8)).encode(), 0, 1,
+                           16, 16, 128, 0, 0.02)
         e2 = ctypes.c_void_p()
         assert L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(e2)) == -7
     finally:

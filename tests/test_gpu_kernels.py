@@ -84,6 +84,29 @@ def test_gemm_shapes(M, N, K):
     assert G.device_errors() == 0
 
 
+def test_gemm_splitk_workspace_reuse():
+    """One workspace, zeroed once, serves a sequence of split-K calls of
+    different shapes and epilogues: each call must leave its tile counters at
+    zero for the next (a stale counter would make a wrong split finish a tile)."""
+    torch.manual_seed(0)
+    shapes = [(64, 4096, 4096, 0), (64, 2048, 4096, 3), (7, 4096, 1024, 2), (64, 1024, 8192, 0)]
+    L = G.L()
+    wsb = max(L.b200_gemm_workspace_bytes(M, N, K, e) for M, N, K, e in shapes)
+    assert wsb > 0
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=G.DEV)
+    for rep in range(2):
+        for M, N, K, epi in shapes:
+            A = (torch.randn(M, K, device=G.DEV) * 0.5).to(torch.bfloat16)
+            B = (torch.randn(N, K, device=G.DEV) * 0.1).to(torch.bfloat16)
+            R = torch.randn(M, N, device=G.DEV).to(torch.bfloat16)
+            acc = A.float() @ B.float().T
+            ref = {0: acc, 2: acc + R.float(), 3: torch.nn.functional.silu(acc[:, 0::2]) * acc[:, 1::2]}[epi]
+            got = G.host(G.gemm(A, B, epi=epi, R=R, ws=ws))
+            assert G.cosine(got, ref.cpu().numpy()) > 0.9999, (rep, M, N, K, epi)
+            assert G.max_rel_err(got, ref.cpu().numpy()) < 0.01, (rep, M, N, K, epi)
+    assert G.device_errors() == 0
+
+
 @pytest.mark.parametrize("M", [8, 96, 640])
 def test_gemm_epilogues(M):
     torch.manual_seed(M)
