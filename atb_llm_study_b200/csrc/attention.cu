@@ -546,9 +546,11 @@ int decode_max_splits(int max_context) {
   return std::max(1, std::min(32, (max_context + 4 * kDecTile - 1) / (4 * kDecTile)));
 }
 
-// KV splits per (sequence, kv head): the count whose CTAs fill the last wave
-// best (two CTAs per SM), with a small charge per extra split for the partial
-// outputs and the combine pass.
+// KV splits per (sequence, kv head).  Splitting costs a CTA prologue per split,
+// partial outputs and the combine pass, which measured more than the tail of
+// a partly filled last wave (batch 64 x 8 kv heads at context 2048: 95 us
+// unsplit, 114 us with 2 splits, 125 us with 4).  So split only when the
+// (sequence, kv head) pairs cannot occupy every SM: aim for two CTAs per SM.
 int decode_splits(int batch, int nkv, int max_context) {
   static const int forced = [] {  // tuning override: B200_DECODE_SPLITS=<n>
     const char* v = std::getenv("B200_DECODE_SPLITS");
@@ -556,19 +558,10 @@ int decode_splits(int batch, int nkv, int max_context) {
   }();
   if (forced > 0) return std::min(forced, decode_max_splits(max_context));
   const int64_t pairs = (int64_t)batch * nkv;
-  const int64_t slots = 2 * (int64_t)num_sms();
-  int best = 1;
-  double best_score = -1.0;
-  for (int s = 1; s <= decode_max_splits(max_context); ++s) {
-    const int64_t ctas = pairs * s;
-    const int64_t waves = (ctas + slots - 1) / slots;
-    const double score = (double)ctas / (double)(waves * slots) - 0.01 * s;
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  const int64_t sms = num_sms();
+  if (pairs >= sms) return 1;
+  const int64_t want = (2 * sms + pairs - 1) / pairs;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(want, decode_max_splits(max_context)));
 }
 
 // Opt one kernel (a distinct template argument per kernel) into large dynamic

@@ -168,10 +168,10 @@ B200_API int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head_d
  * (b200_paged_decode_noalloc_max_scratch_bytes()).  Inputs and outputs are
  * the caller's, with the same meaning and limits as b200_paged_decode.  The
  * scratch a call needs is batch x nq x splits x (head_dim + 1) x 4 bytes,
- * where splits is the KV split count the kernel picks (1 = no scratch; 2 for
- * batch 64 x 8 kv heads at context 2048, i.e. 2.1 MB); a call that would need
- * more than 8 MiB is rejected with B200_ERROR_INVALID_PARAM before anything
- * is launched.
+ * where splits is the KV split count the kernel picks (1 = no scratch, e.g.
+ * batch 64 x 8 kv heads; 5 for batch 8 x 8 kv heads at context 2048, i.e.
+ * 660 KB); a call that would need more than 8 MiB is rejected with
+ * B200_ERROR_INVALID_PARAM before anything is launched.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  All calls share the one array and it keeps the

@@ -55,10 +55,12 @@ def _run(c, noalloc):
 def test_noalloc_decode_matches_workspace_entry_point_twice():
     L = G.L()
     assert L.b200_paged_decode_noalloc_max_scratch_bytes() == 8 << 20
-    # two different problems back to back: the second finds the first's data in the scratch
-    for seed, B, ctx in ((11, 64, [2048] * 63 + [5]), (12, 16, [1, 64, 65, 777] * 4)):
+    # two different problems back to back: the second finds the first's data in
+    # the scratch.  Small batches (8 and 16 sequences x 8 kv heads leave SMs
+    # idle) so the kernel splits the KV range and really uses the scratch.
+    for seed, B, ctx in ((11, 8, [2048] * 7 + [5]), (12, 16, [1, 64, 65, 777] * 4)):
         c = _case(seed, B, np.array(ctx))
-        assert L.b200_paged_decode_workspace_bytes(B, 32, 128, c["max_ctx"]) > 0  # split-KV path in use
+        assert L.b200_paged_decode_workspace_bytes(B, 32, 128, c["max_ctx"]) > 0
         ref = _run(c, noalloc=False)
         for _ in range(2):
             got = _run(c, noalloc=True)
@@ -70,7 +72,7 @@ def test_noalloc_decode_matches_workspace_entry_point_twice():
 
 def test_noalloc_rejects_problem_larger_than_its_scratch():
     L = G.L()
-    # 64 sequences x 1 kv head -> 10 KV splits; 64 x 64 heads x 10 x 129 x 4 B = 21 MB > 8 MiB
+    # 64 sequences x 1 kv head -> 5 KV splits; 64 x 64 heads x 5 x 129 x 4 B = 10.6 MB > 8 MiB
     B, nq, nkv, hd, max_ctx = 64, 64, 1, 128, 32768
     assert L.b200_paged_decode_workspace_bytes(B, nq, hd, max_ctx) > L.b200_paged_decode_noalloc_max_scratch_bytes()
     dummy = 256  # never dereferenced: the size check fails before any launch
