@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
   uint8_t* sK[2] = {smem + Cf::BM * HD * 2, smem + Cf::BM * HD * 2 + Cf::TILE_BYTES};
   uint8_t* sV[2] = {smem + Cf::BM * HD * 2 + 2 * Cf::TILE_BYTES, smem + Cf::BM * HD * 2 + 3 * Cf::TILE_BYTES};
 
+  pdl_trigger();
+  pdl_wait();
   const int seq = blockIdx.z, h = blockIdx.y;
   const int mb = m_blocks - 1 - blockIdx.x;  // heaviest (latest) query blocks first
   const int s0 = cu_seqlens[seq], len = cu_seqlens[seq + 1] - s0;
@@ -271,6 +273,8 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const __grid_
   uint64_t* full = reinterpret_cast<uint64_t*>(sQ + 16 * kDecHD * 2);
   uint64_t* empty = full + kDecStages;
 
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
@@ -488,6 +492,8 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const __grid_
 // out[b, h] = sum_s w_s O_s with w_s = 2^(lse_s - max) / sum (lse in log2 units)
 __global__ void decode_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, int nq,
                                       int splits, __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  pdl_trigger();
+  pdl_wait();
   const int bh = blockIdx.x;  // b * nq + h
   const int b = bh / nq, h = bh % nq;
   const float* lse = ws_lse + (int64_t)bh * splits;
@@ -583,10 +589,9 @@ int launch_prefill(const void* q, int64_t qs, const void* k, const void* v, int6
   if (!set_smem<flash_prefill_kernel<HD, CAUSAL>>(PrefillCfg<HD>::SMEM)) return B200_ERROR_UNSUPPORTED;
   const int mblocks = (max_seqlen + 63) / 64;
   dim3 grid(mblocks, nq, num_seqs);
-  kern<<<grid, 128, PrefillCfg<HD>::SMEM, st>>>(
-      static_cast<const __nv_bfloat16*>(q), qs, static_cast<const __nv_bfloat16*>(k),
-      static_cast<const __nv_bfloat16*>(v), kvs, static_cast<__nv_bfloat16*>(out), os, cu, nq, nkv,
-      scale * kLog2e, mblocks);
+  launch_kernel(kern, grid, 128, PrefillCfg<HD>::SMEM, st, static_cast<const __nv_bfloat16*>(q), qs,
+                static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), kvs,
+                static_cast<__nv_bfloat16*>(out), os, cu, nq, nkv, scale * kLog2e, mblocks);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -745,10 +750,11 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_
   if (!make_cache_tmap(&tk, k_cache, rows) || !make_cache_tmap(&tv, v_cache, rows)) return B200_ERROR_UNSUPPORTED;
   if (!set_smem<paged_decode_kernel>(kDecSmem)) return B200_ERROR_UNSUPPORTED;
   dim3 grid(batch, nkv, splits);
-  paged_decode_kernel<<<grid, kDecThreads, kDecSmem, stream>>>(tk, tv, p);
+  launch_kernel(paged_decode_kernel, grid, kDecThreads, kDecSmem, stream, tk, tv, p);
   B200_CHECK_LAUNCH();
   if (splits > 1) {
-    decode_combine_kernel<<<batch * nq, kDecHD, 0, stream>>>(p.ws_o, p.ws_lse, nq, splits, p.out, out_stride);
+    launch_kernel(decode_combine_kernel, dim3(batch * nq), kDecHD, 0, stream, p.ws_o, p.ws_lse, nq, splits, p.out,
+                  out_stride);
     B200_CHECK_LAUNCH();
   }
   return B200_OK;

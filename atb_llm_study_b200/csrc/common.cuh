@@ -259,6 +259,35 @@ B200_DEV void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialisation: it may start while its predecessor
+// on the stream is still finishing, runs its prologue (and anything that only
+// reads constant data, such as weights), then pdl_wait() blocks until the
+// predecessor has completed and its writes are visible.  pdl_trigger() lets
+// the successor launch early.  Launched without the attribute both are no-ops.
+// ---------------------------------------------------------------------------
+B200_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+B200_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();  // B200_PDL=0 in the environment turns it off
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace b200
 
 // Host helpers shared by the launchers.

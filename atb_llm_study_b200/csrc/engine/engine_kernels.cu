@@ -33,6 +33,8 @@ __global__ void fill_const_kernel(__nv_bfloat16* x, int64_t n, float v) {
 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const int32_t* __restrict__ idx,
                                    int64_t dim, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(src + (int64_t)idx[r] * dim);
   uint4* d = reinterpret_cast<uint4*>(out + r * dim);
@@ -44,6 +46,8 @@ __global__ void decode_prepare_kernel(const int32_t* __restrict__ seq_slots, int
                                       int64_t* __restrict__ positions, int64_t* __restrict__ slots,
                                       int32_t* __restrict__ ctx_batch, int32_t* __restrict__ bt_batch,
                                       unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   const int s = seq_slots[b];
   const int p = ctx_lens[s];
@@ -84,8 +88,8 @@ int FillConstBf16(void* x, int64_t n, float value, cudaStream_t st) {
 
 int GatherRows(const void* src, const int32_t* idx, int64_t n, int64_t dim, void* out, cudaStream_t st) {
   if (n <= 0) return 0;
-  gather_rows_kernel<<<(unsigned)n, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(src), idx, dim,
-                                                  static_cast<__nv_bfloat16*>(out));
+  launch_kernel(gather_rows_kernel, dim3((unsigned)n), 128, 0, st, static_cast<const __nv_bfloat16*>(src), idx, dim,
+                static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
 }
 
@@ -93,8 +97,8 @@ int DecodePrepare(const int32_t* seq_slots, int B, int32_t* ctx_lens, const int3
                   int block_size, int64_t* positions, int64_t* slots, int32_t* ctx_batch, int32_t* bt_batch,
                   unsigned* err, cudaStream_t st) {
   if (B <= 0) return 0;
-  decode_prepare_kernel<<<B, 64, 0, st>>>(seq_slots, B, ctx_lens, block_tables, max_blocks, block_size, positions,
-                                          slots, ctx_batch, bt_batch, err);
+  launch_kernel(decode_prepare_kernel, dim3(B), 64, 0, st, seq_slots, B, ctx_lens, block_tables, max_blocks,
+                block_size, positions, slots, ctx_batch, bt_batch, err);
   return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
 }
 

@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = p.tiles_m * p.tiles_n * p.splits;
+  pdl_trigger();
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -206,24 +207,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // The weight operand (A when swapped, B otherwise) is constant: its
+      // tiles for the first stages are requested before waiting for the
+      // previous kernel on the stream, so the weight stream starts while that
+      // kernel drains.  Activation tiles are only loaded after the wait.
+      int pre = 0;
+      if ((int)blockIdx.x < units) {
+        int tm0, tn0, kb00, kb10;
+        decode_unit(blockIdx.x, p, tm0, tn0, kb00, kb10);
+        pre = min(C::STAGES, kb10 - kb00);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          if (SWAP) tma_load_2d(sA + i * C::A_BYTES, &tmA, &full[i], (kb00 + i) * BK, tm0 * BM);
+          else tma_load_2d(sB + i * C::B_BYTES, &tmB, &full[i], (kb00 + i) * BK, tn0 * BN);
+        }
+      }
+      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
+      bool first = true;
       for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x) {
         int tm, tn, kb0, kb1;
         decode_unit(w, p, tm, tn, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
-            *abort_flag = 1;
-            break;
+          if (first && kb - kb0 < pre) {
+            // stage == kb - kb0 already expects both halves; add the activation half
+            if (SWAP) tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
+            else tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        first = false;
       }
     }
     __syncwarp();
@@ -273,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // reads the residual / writes outputs the previous kernel may still use
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int rit = q * 32 + lane;
     int local = 0;
@@ -383,7 +409,7 @@ int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int gr
       return B200_ERROR_UNSUPPORTED;
     attr_set[dev] = true;
   }
-  k<<<grid, kThreads, Cfg<BN>::SMEM, st>>>(a, b, p);
+  launch_kernel(k, dim3(grid), kThreads, Cfg<BN>::SMEM, st, a, b, p);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -393,6 +419,8 @@ int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int gr
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t tokens, int64_t feats,
                                      Params p) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t nv = feats / 8;
   const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (gid >= tokens * nv) return;
@@ -549,12 +577,12 @@ int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epi, co
   const int64_t n = M * (N / 8);
   const unsigned grid = (unsigned)((n + 255) / 256);
   switch (epi) {
-    case B200_EPI_NONE: splitk_reduce_kernel<B200_EPI_NONE><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
-    case B200_EPI_BIAS: splitk_reduce_kernel<B200_EPI_BIAS><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
-    case B200_EPI_RESIDUAL: splitk_reduce_kernel<B200_EPI_RESIDUAL><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
-    case B200_EPI_SWIGLU: splitk_reduce_kernel<B200_EPI_SWIGLU><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
-    case B200_EPI_BIAS_GELU: splitk_reduce_kernel<B200_EPI_BIAS_GELU><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
-    case B200_EPI_BIAS_RESIDUAL: splitk_reduce_kernel<B200_EPI_BIAS_RESIDUAL><<<grid, 256, 0, st>>>(ws, splits, M, N, p); break;
+    case B200_EPI_NONE: launch_kernel(splitk_reduce_kernel<B200_EPI_NONE>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
+    case B200_EPI_BIAS: launch_kernel(splitk_reduce_kernel<B200_EPI_BIAS>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
+    case B200_EPI_RESIDUAL: launch_kernel(splitk_reduce_kernel<B200_EPI_RESIDUAL>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
+    case B200_EPI_SWIGLU: launch_kernel(splitk_reduce_kernel<B200_EPI_SWIGLU>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
+    case B200_EPI_BIAS_GELU: launch_kernel(splitk_reduce_kernel<B200_EPI_BIAS_GELU>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
+    case B200_EPI_BIAS_RESIDUAL: launch_kernel(splitk_reduce_kernel<B200_EPI_BIAS_RESIDUAL>, dim3(grid), 256, 0, st, ws, splits, M, N, p); break;
     default: return B200_ERROR_INVALID_PARAM;
   }
   B200_CHECK_LAUNCH();

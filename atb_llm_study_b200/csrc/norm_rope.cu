@@ -7,6 +7,8 @@
 // shuffles plus one shared-memory hop.
 #include <math.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 using namespace b200;
@@ -37,6 +39,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
                                                                __nv_bfloat16* out, __nv_bfloat16* residual_out,
                                                                int64_t dim, int64_t stride, float eps) {
   __shared__ float red[kNormThreads / 32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int64_t nchunk = dim / 8;
   const __nv_bfloat16* xr = x + row * stride;
@@ -73,16 +77,23 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
   }
 }
 
-// One CTA per row: h = hidden + sum_s partials[s][row] (a split-K projection
-// finished here), hidden = bf16(h), out = rmsnorm(bf16(h)) * w.
+// One CTA of 512 threads per row (decode has few rows, so each thread owns
+// one to four 16-byte chunks and issues all its loads up front):
+// h = hidden + sum_s partials[s][row] (a split-K projection finished here),
+// hidden = bf16(h), out = rmsnorm(bf16(h)) * w.
+constexpr int kRowThreads = 512;
+
 template <int CH>
-__global__ void __launch_bounds__(kNormThreads) splitk_residual_rmsnorm_kernel(const float* __restrict__ partials,
-                                                                               int splits, int64_t rows,
-                                                                               __nv_bfloat16* hidden,
-                                                                               const __nv_bfloat16* __restrict__ w,
-                                                                               __nv_bfloat16* __restrict__ out,
-                                                                               int64_t dim, float eps) {
+__global__ void __launch_bounds__(kRowThreads) splitk_residual_rmsnorm_kernel(const float* __restrict__ partials,
+                                                                              int splits, int64_t rows,
+                                                                              __nv_bfloat16* hidden,
+                                                                              const __nv_bfloat16* __restrict__ w,
+                                                                              __nv_bfloat16* __restrict__ out,
+                                                                              int64_t dim, float eps) {
+  constexpr int kNormThreads = kRowThreads;
   __shared__ float red[kNormThreads / 32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int64_t nchunk = dim / 8;
   float v[CH][8];
@@ -126,6 +137,8 @@ __global__ void __launch_bounds__(kNormThreads) layernorm_kernel(const __nv_bflo
                                                                  __nv_bfloat16* __restrict__ out, int64_t dim,
                                                                  float eps) {
   __shared__ float red[kNormThreads / 32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int64_t nchunk = dim / 8;
   float v[CH][8];
@@ -177,6 +190,8 @@ struct InvFreq {
 __global__ void rope_table_kernel(const int64_t* __restrict__ pos, int64_t T, int half, const InvFreq inv_freq,
                                   int mrope, int sec_h, int sec_w, float* __restrict__ cos_out,
                                   float* __restrict__ sin_out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (gid >= T * half) return;
   const int64_t t = gid / half;
@@ -198,7 +213,7 @@ __global__ void rope_table_kernel(const int64_t* __restrict__ pos, int64_t T, in
 }
 
 // Per-head RMSNorm (q, k) + half-rotation rope (q, k) + paged-KV write (k, v).
-// One CTA per token; each warp walks heads.  Lane l holds elements
+// Grid (token, head group); each warp handles one head.  Lane l holds elements
 // [l*E, l*E+E) of a head (E = head_dim/32); the rotation partner of element
 // i (i +- head_dim/2) sits in lane l^16.
 template <int HD>
@@ -216,6 +231,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
   // yet; every head is summed from the fp32 partial tiles
   // partials[s][t][p_ld] and written to qkv (v too, for prefill attention).
   constexpr int E = HD / 32;
+  pdl_trigger();
+  pdl_wait();
   const int64_t t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nheads = nq + 2 * nkv;
@@ -235,7 +252,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
     }
   }
   const float sign = lane < 16 ? -1.f : 1.f;
-  for (int h = warp; h < nheads; h += blockDim.x / 32) {
+  const int wpc = blockDim.x / 32;  // heads of a token are spread over gridDim.y CTAs
+  for (int h = blockIdx.y * wpc + warp; h < nheads; h += gridDim.y * wpc) {
     __nv_bfloat16* hp = row + (int64_t)h * HD + lane * E;
     float x[E];
     if (partials) {
@@ -294,6 +312,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
 __global__ void slot_mapping_kernel(const int32_t* __restrict__ bt, int max_blocks, const int32_t* __restrict__ seq,
                                     const int64_t* __restrict__ pos, int64_t T, int bs, int64_t* __restrict__ slots,
                                     unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (t >= T) return;
   const int64_t p = pos[t];
@@ -308,6 +328,8 @@ __global__ void slot_mapping_kernel(const int32_t* __restrict__ bt, int max_bloc
 
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  int64_t vocab, int64_t dim, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t t = blockIdx.x;
   const int64_t id = ids[t];
   const bool ok = id >= 0 && id < vocab;
@@ -318,6 +340,8 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfl
 
 __global__ void scatter_add_kernel(__nv_bfloat16* hidden, int64_t rows, int64_t dim, const int32_t* __restrict__ idx,
                                    const __nv_bfloat16* __restrict__ feat, float alpha, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = blockIdx.x;
   const int64_t r = idx[i];
   if (r < 0 || r >= rows) {
@@ -343,6 +367,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const __nv_bfloa
                                                                 int64_t vocab, int64_t ld, int64_t* __restrict__ out) {
   __shared__ float sv[kArgmaxThreads / 32];
   __shared__ int64_t si[kArgmaxThreads / 32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   const __nv_bfloat16* row = logits + r * ld;
   float best = -INFINITY;
@@ -403,6 +429,14 @@ __device__ unsigned g_device_error_word;
 }  // namespace
 
 namespace b200 {
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 unsigned* error_word(int device) {
   static unsigned* ptrs[64] = {nullptr};
   if (device < 0 || device >= 64) return nullptr;
@@ -450,12 +484,12 @@ extern "C" int b200_rmsnorm(const void* x, const void* residual, const void* wei
   auto rob = static_cast<__nv_bfloat16*>(residual_out);
   dim3 g((unsigned)rows);
   switch (per) {
-    case 1: rmsnorm_kernel<1><<<g, kNormThreads, 0, stream>>>(xb, rb, wb, ob, rob, dim, stride, eps); break;
-    case 2: rmsnorm_kernel<2><<<g, kNormThreads, 0, stream>>>(xb, rb, wb, ob, rob, dim, stride, eps); break;
+    case 1: launch_kernel(rmsnorm_kernel<1>, g, kNormThreads, 0, stream, xb, rb, wb, ob, rob, dim, stride, eps); break;
+    case 2: launch_kernel(rmsnorm_kernel<2>, g, kNormThreads, 0, stream, xb, rb, wb, ob, rob, dim, stride, eps); break;
     case 3:
-    case 4: rmsnorm_kernel<4><<<g, kNormThreads, 0, stream>>>(xb, rb, wb, ob, rob, dim, stride, eps); break;
+    case 4: launch_kernel(rmsnorm_kernel<4>, g, kNormThreads, 0, stream, xb, rb, wb, ob, rob, dim, stride, eps); break;
     case 5: case 6: case 7:
-    case 8: rmsnorm_kernel<8><<<g, kNormThreads, 0, stream>>>(xb, rb, wb, ob, rob, dim, stride, eps); break;
+    case 8: launch_kernel(rmsnorm_kernel<8>, g, kNormThreads, 0, stream, xb, rb, wb, ob, rob, dim, stride, eps); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
@@ -474,12 +508,12 @@ extern "C" int b200_layernorm(const void* x, const void* gamma, const void* beta
   auto ob = static_cast<__nv_bfloat16*>(out);
   dim3 g((unsigned)rows);
   switch (per) {
-    case 1: layernorm_kernel<1><<<g, kNormThreads, 0, stream>>>(xb, gb, bb, ob, dim, eps); break;
-    case 2: layernorm_kernel<2><<<g, kNormThreads, 0, stream>>>(xb, gb, bb, ob, dim, eps); break;
+    case 1: launch_kernel(layernorm_kernel<1>, g, kNormThreads, 0, stream, xb, gb, bb, ob, dim, eps); break;
+    case 2: launch_kernel(layernorm_kernel<2>, g, kNormThreads, 0, stream, xb, gb, bb, ob, dim, eps); break;
     case 3:
-    case 4: layernorm_kernel<4><<<g, kNormThreads, 0, stream>>>(xb, gb, bb, ob, dim, eps); break;
+    case 4: launch_kernel(layernorm_kernel<4>, g, kNormThreads, 0, stream, xb, gb, bb, ob, dim, eps); break;
     case 5: case 6: case 7:
-    case 8: layernorm_kernel<8><<<g, kNormThreads, 0, stream>>>(xb, gb, bb, ob, dim, eps); break;
+    case 8: launch_kernel(layernorm_kernel<8>, g, kNormThreads, 0, stream, xb, gb, bb, ob, dim, eps); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
@@ -498,7 +532,8 @@ static int rope_table(const int64_t* pos, int64_t T, int head_dim, float theta, 
   for (int i = 0; i < head_dim / 2; ++i) inv.v[i] = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
   const int half = head_dim / 2;
   const int64_t n = T * half;
-  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(pos, T, half, inv, mrope, sh, sw, c, s);
+  launch_kernel(rope_table_kernel, dim3((unsigned)((n + 255) / 256)), 256, 0, stream, pos, T, half, inv, mrope, sh, sw,
+                c, s);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -535,11 +570,11 @@ int qk_norm_rope_launch(void* qkv, int64_t T, int nq, int nkv, int head_dim, int
   auto vc = static_cast<__nv_bfloat16*>(v_cache);
   unsigned* err = current_error_word();
   const int64_t p_ld = row_stride, p_slice = T * row_stride;  // partials [splits][T][row_stride]
-  dim3 g((unsigned)T);
+  dim3 g((unsigned)T, (unsigned)((nq + 2 * nkv + 3) / 4));  // one warp per (token, head)
   switch (head_dim) {
-    case 32: qk_norm_rope_kernel<32><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
-    case 64: qk_norm_rope_kernel<64><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
-    case 128: qk_norm_rope_kernel<128><<<g, 128, 0, stream>>>(q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
+    case 32: launch_kernel(qk_norm_rope_kernel<32>, g, 128, 0, stream, q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
+    case 64: launch_kernel(qk_norm_rope_kernel<64>, g, 128, 0, stream, q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
+    case 128: launch_kernel(qk_norm_rope_kernel<128>, g, 128, 0, stream, q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
@@ -551,18 +586,16 @@ int splitk_residual_rmsnorm(const float* partials, int splits, int64_t rows, int
   if (!partials || splits <= 0 || !hidden || !weight || !normed || rows < 0 || dim <= 0 || dim % 8)
     return B200_ERROR_INVALID_PARAM;
   if (rows == 0) return B200_OK;
-  const int64_t per = (dim / 8 + kNormThreads - 1) / kNormThreads;
+  const int64_t per = (dim / 8 + kRowThreads - 1) / kRowThreads;
   auto h = static_cast<__nv_bfloat16*>(hidden);
   auto w = static_cast<const __nv_bfloat16*>(weight);
   auto o = static_cast<__nv_bfloat16*>(normed);
   dim3 g((unsigned)rows);
   switch (per) {
-    case 1: splitk_residual_rmsnorm_kernel<1><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
-    case 2: splitk_residual_rmsnorm_kernel<2><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    case 1: launch_kernel(splitk_residual_rmsnorm_kernel<1>, g, kRowThreads, 0, stream, partials, splits, rows, h, w, o, dim, eps); break;
+    case 2: launch_kernel(splitk_residual_rmsnorm_kernel<2>, g, kRowThreads, 0, stream, partials, splits, rows, h, w, o, dim, eps); break;
     case 3:
-    case 4: splitk_residual_rmsnorm_kernel<4><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
-    case 5: case 6: case 7:
-    case 8: splitk_residual_rmsnorm_kernel<8><<<g, kNormThreads, 0, stream>>>(partials, splits, rows, h, w, o, dim, eps); break;
+    case 4: launch_kernel(splitk_residual_rmsnorm_kernel<4>, g, kRowThreads, 0, stream, partials, splits, rows, h, w, o, dim, eps); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
@@ -585,9 +618,8 @@ extern "C" int b200_slot_mapping(const int32_t* block_tables, int max_blocks_per
   if (!block_tables || !seq_ids || !positions || !slots || T < 0 || block_size <= 0 || max_blocks_per_seq <= 0)
     return B200_ERROR_INVALID_PARAM;
   if (T == 0) return B200_OK;
-  slot_mapping_kernel<<<(unsigned)((T + 255) / 256), 256, 0, stream>>>(block_tables, max_blocks_per_seq, seq_ids,
-                                                                        positions, T, block_size, slots,
-                                                                        current_error_word());
+  launch_kernel(slot_mapping_kernel, dim3((unsigned)((T + 255) / 256)), 256, 0, stream, block_tables,
+                max_blocks_per_seq, seq_ids, positions, T, block_size, slots, current_error_word());
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -597,8 +629,8 @@ extern "C" int b200_embedding(const int64_t* ids, int64_t T, const void* table, 
   if (!ids || !table || !out || T < 0 || vocab <= 0 || dim <= 0 || dim % 8) return B200_ERROR_INVALID_PARAM;
   if (!aligned16(table) || !aligned16(out)) return B200_ERROR_INVALID_PARAM;
   if (T == 0) return B200_OK;
-  embedding_kernel<<<(unsigned)T, 128, 0, stream>>>(ids, static_cast<const __nv_bfloat16*>(table), vocab, dim,
-                                                    static_cast<__nv_bfloat16*>(out));
+  launch_kernel(embedding_kernel, dim3((unsigned)T), 128, 0, stream, ids, static_cast<const __nv_bfloat16*>(table),
+                vocab, dim, static_cast<__nv_bfloat16*>(out));
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -608,9 +640,8 @@ extern "C" int b200_scatter_add_rows(void* hidden, int64_t rows, int64_t dim, co
   if (!hidden || !idx || !feat || rows < 0 || n < 0 || dim <= 0 || dim % 8) return B200_ERROR_INVALID_PARAM;
   if (!aligned16(hidden) || !aligned16(feat)) return B200_ERROR_INVALID_PARAM;
   if (n == 0) return B200_OK;
-  scatter_add_kernel<<<(unsigned)n, 128, 0, stream>>>(static_cast<__nv_bfloat16*>(hidden), rows, dim, idx,
-                                                      static_cast<const __nv_bfloat16*>(feat), alpha,
-                                                      current_error_word());
+  launch_kernel(scatter_add_kernel, dim3((unsigned)n), 128, 0, stream, static_cast<__nv_bfloat16*>(hidden), rows, dim,
+                idx, static_cast<const __nv_bfloat16*>(feat), alpha, current_error_word());
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -619,8 +650,8 @@ extern "C" int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int6
                            b200_stream_t stream) {
   if (!logits || !out || rows < 0 || vocab <= 0 || ld < vocab) return B200_ERROR_INVALID_PARAM;
   if (rows == 0) return B200_OK;
-  argmax_kernel<<<(unsigned)rows, kArgmaxThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), vocab, ld,
-                                                               out);
+  launch_kernel(argmax_kernel, dim3((unsigned)rows), kArgmaxThreads, 0, stream,
+                static_cast<const __nv_bfloat16*>(logits), vocab, ld, out);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
