@@ -270,7 +270,12 @@ B200_DEV void cp_async_wait() {
 B200_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 B200_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-bool pdl_enabled();  // B200_PDL=0 in the environment turns it off
+// Whether launches from this host thread use programmatic dependent launch:
+// on by default; B200_PDL=0 in the environment turns it off everywhere, and
+// set_pdl(false) turns it off for the calling thread (the engine does so for
+// prefill, whose large grids gain nothing from early launch).
+bool pdl_enabled();
+void set_pdl(bool on);
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

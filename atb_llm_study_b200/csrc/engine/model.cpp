@@ -10,7 +10,17 @@
 
 namespace b200 {
 unsigned* error_word(int device);
+void set_pdl(bool on);
 }
+
+namespace {
+// Prefill launches without programmatic dependent launch: its grids fill the
+// GPU on their own, and early-launched successors measured slower there.
+struct NoPdlScope {
+  NoPdlScope() { b200::set_pdl(false); }
+  ~NoPdlScope() { b200::set_pdl(true); }
+};
+}  // namespace
 
 namespace b200llm {
 
@@ -369,6 +379,7 @@ Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32
     max_len = std::max(max_len, seq_lens[i]);
   }
   if (T > max_t_) return ERROR_INVALID_PARAM;
+  NoPdlScope no_pdl;
   cudaStream_t st = ctx_->GetStream();
   // host-side metadata staged in pinned memory
   uint8_t* pin = static_cast<uint8_t*>(pinned_);

@@ -429,13 +429,17 @@ __device__ unsigned g_device_error_word;
 }  // namespace
 
 namespace b200 {
+static thread_local bool t_pdl_on = true;
+
 bool pdl_enabled() {
-  static const bool on = [] {
+  static const bool env_on = [] {
     const char* v = std::getenv("B200_PDL");
     return !(v && v[0] == '0');
   }();
-  return on;
+  return env_on && t_pdl_on;
 }
+
+void set_pdl(bool on) { t_pdl_on = on; }
 
 unsigned* error_word(int device) {
   static unsigned* ptrs[64] = {nullptr};
