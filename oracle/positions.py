@@ -138,6 +138,61 @@ def causal_mask_fp16(S):
     return m
 
 
+def merge_order(t, h, w, merge_size=2):
+    """Row-major patch index (row * w + col) of every token in the vision
+    tower's order: merge blocks row-major, the merge_size x merge_size patches
+    of a block row-major, the whole grid repeated t times
+    (pos_embed_interp.cpp:62-90, engine_utils.py:398-405)."""
+    m = merge_size
+    order = []
+    for br in range(h // m):
+        for bc in range(w // m):
+            for ir in range(m):
+                for ic in range(m):
+                    order.append((br * m + ir) * w + bc * m + ic)
+    return np.tile(np.asarray(order, np.int64), t)
+
+
+def pos_embed_interp(table, grid_thw, num_grid=48, merge_size=2):
+    """Bilinear interpolation of the learned ``[num_grid^2, H]`` position table
+    to each image's ``h x w`` patch grid, in merge order, repeated over t.
+
+    Restates the reference's CPU ``ComputePosEmbedInterp``
+    (atb_cpp_llm/src/components/vision/pos_embed_interp.cpp:10-90) in fp32 with
+    its exact evaluation order: ``fy = float(i) * (G-1) / (h-1)``, truncating
+    floor, ``min(floor+1, G-1)``, and
+    ``v00*(1-dy)*(1-dx) + v01*(1-dy)*dx + v10*dy*(1-dx) + v11*dy*dx``.
+    The result is fp32 (the reference rounds it to fp16 afterwards).
+    """
+    table = np.asarray(table, np.float32)
+    G = np.float32(num_grid - 1)
+    outs = []
+    for t, h, w in np.asarray(grid_thw, np.int64):
+        def axis(n):
+            if n <= 1:
+                f = np.zeros(n, np.float32)
+            else:
+                f = (np.arange(n).astype(np.float32) * G) / np.float32(n - 1)
+            lo = f.astype(np.int64)
+            hi = np.minimum(lo + 1, num_grid - 1)
+            return lo, hi, (f - lo.astype(np.float32)).astype(np.float32)
+
+        y0, y1, dy = axis(int(h))
+        x0, x1, dx = axis(int(w))
+        one = np.float32(1.0)
+        Y0, X0 = np.meshgrid(y0, x0, indexing="ij")
+        Y1, X1 = np.meshgrid(y1, x1, indexing="ij")
+        DY, DX = np.meshgrid(dy, dx, indexing="ij")
+        DY, DX = DY.reshape(-1, 1), DX.reshape(-1, 1)
+        v00 = table[(Y0 * num_grid + X0).reshape(-1)]
+        v01 = table[(Y0 * num_grid + X1).reshape(-1)]
+        v10 = table[(Y1 * num_grid + X0).reshape(-1)]
+        v11 = table[(Y1 * num_grid + X1).reshape(-1)]
+        interp = (v00 * (one - DY) * (one - DX) + v01 * (one - DY) * DX) + v10 * DY * (one - DX) + v11 * DY * DX
+        outs.append(interp[merge_order(int(t), int(h), int(w), merge_size)])
+    return np.concatenate(outs).astype(np.float32)
+
+
 def vision_rope_cos_sin(grid_thw, head_dim=64, merge_size=2, theta=10000.0):
     """2-D vision rope cos/sin ``[T, head_dim]``.
 

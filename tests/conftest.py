@@ -66,6 +66,23 @@ def decoder_case(name):
                 out_ref=fx[f"{name}_out_ref"])
 
 
+def checked_inputs(fixture, prefix, rebuilt):
+    """Rebuilt (seed-replayed) inputs of one golden case, each checked against
+    the committed array or, for arrays too large to commit, the sha256 the
+    reference run recorded.  ``prefix`` is the case's key prefix ('' or 'x_')."""
+    import regen
+
+    fx = load_fixture(fixture)
+    man = manifest()
+    for k, v in rebuilt.items():
+        key = f"{prefix}{k}"
+        if key in fx:
+            np.testing.assert_array_equal(fx[key], v, err_msg=key)
+        else:
+            assert regen.sha256(v) == man[f"{fixture}/{key}"]["sha256"], key
+    return fx
+
+
 def cosine(a, b):
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()

@@ -34,11 +34,15 @@ STAGES = [
     "op_self_attention", "swiglu_mlp", "mrope_cos_sin", "mrope_pid_simple",
     "mrope_pid_no_img", "mrope_pid_image_text", "mrope_pid_multi_img",
     "mrope_pid_chat_template", "mrope_pid_boundary", "op_activation",
-    "vision_rope",
+    "vision_rope", "vision_attention", "vision_mlp", "vision_block", "patch_embed",
+    "vision_merger",
 ]
 
 
 def main():
+    # the generator seeds its activation cases with hash(name): pin str hashing
+    if os.environ.get("PYTHONHASHSEED") != "0":
+        os.execve(sys.executable, [sys.executable] + sys.argv, dict(os.environ, PYTHONHASHSEED="0"))
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--max-bytes", type=int, default=600_000)
@@ -84,22 +88,30 @@ def pack(tmp, files, calls, max_bytes, read_bin, read_i32s):
         "linear": "cpu_op_linear_", "rope": "cpu_op_rope_",
         "self_attention": "cpu_op_sa_", "swiglu": "cpu_swiglu_mlp_",
         "activation": "cpu_op_activation_", "mrope": "cpu_mrope_",
-        "vision_rope": "cpu_vision_",
+        "vision_rope": ("cpu_vision_rope_", "cpu_vision_freq_table"),
+        "vision_attn": "cpu_vision_attn_", "vision_mlp": "cpu_vision_mlp",
+        "vision_block": "cpu_vision_block", "patch_embed": "cpu_patch_embed",
+        "vision_merger": "cpu_vision_merger_",
     }
+    fp16_fixtures = ("decoder_layer", "rope", "self_attention", "swiglu", "vision_attn", "vision_mlp",
+                     "vision_block", "patch_embed", "vision_merger")
     manifest = {}
-    for fixture, prefix in groups.items():
+    for fixture, prefixes in groups.items():
+        prefixes = prefixes if isinstance(prefixes, tuple) else (prefixes,)
         arrays = {}
         for f in files:
-            if not f.startswith(prefix) or not f.endswith(".bin"):
+            prefix = next((p for p in prefixes if f.startswith(p)), None)
+            if prefix is None or not f.endswith(".bin"):
                 continue
-            key = f[len(prefix):-4]
+            key = f[len("cpu_vision_"):-4] if fixture == "vision_rope" else f[len(prefix):-4]
+            key = key.lstrip("_")
             path = os.path.join(tmp, f)
             if fixture == "activation" and "fast_gelu" in key:
                 continue
-            if key.endswith("_meta"):
+            if key == "meta" or key.endswith("_meta"):
                 arrays[key] = read_i32s(path)
                 continue
-            if fixture in ("decoder_layer", "rope", "self_attention", "swiglu"):
+            if fixture in fp16_fixtures:
                 a = read_bin(path, "fp16")
             elif fixture == "mrope" and key.startswith("pid"):
                 a = read_bin(path, "i64")

@@ -56,6 +56,54 @@ def swiglu_inputs(S, H, I, seed):
     return {k: _f16(v) for k, v in d.items()}
 
 
+def vision_block_inputs(N, nh, hd, inter, seed):
+    """Draw order of ``gen_vision_block._build_case`` (gen_cpu_reference.py:1969-1983)."""
+    rng = np.random.default_rng(seed)
+    hidden = nh * hd
+    f32 = np.float32
+    d = {}
+    d["x"] = rng.standard_normal((N, hidden)).astype(f32) * 0.2
+    d["qkv_w"] = rng.standard_normal((3 * hidden, hidden)).astype(f32) * 0.1
+    d["qkv_b"] = rng.standard_normal((3 * hidden,)).astype(f32) * 0.05
+    d["proj_w"] = rng.standard_normal((hidden, hidden)).astype(f32) * 0.1
+    d["proj_b"] = rng.standard_normal((hidden,)).astype(f32) * 0.05
+    d["fc1_w"] = rng.standard_normal((inter, hidden)).astype(f32) * 0.1
+    d["fc1_b"] = rng.standard_normal((inter,)).astype(f32) * 0.05
+    d["fc2_w"] = rng.standard_normal((hidden, inter)).astype(f32) * 0.1
+    d["fc2_b"] = rng.standard_normal((hidden,)).astype(f32) * 0.05
+    d["n1_w"] = rng.standard_normal((hidden,)).astype(f32) * 0.1 + 1.0
+    d["n1_b"] = rng.standard_normal((hidden,)).astype(f32) * 0.05
+    d["n2_w"] = rng.standard_normal((hidden,)).astype(f32) * 0.1 + 1.0
+    d["n2_b"] = rng.standard_normal((hidden,)).astype(f32) * 0.05
+    return {k: _f16(v) for k, v in d.items()}
+
+
+def vision_mlp_inputs(N, hidden, inter, seed, zero_bias=False):
+    """Draw order of ``gen_vision_mlp._make`` (gen_cpu_reference.py:1909-1918)."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    d = {"x": rng.standard_normal((N, hidden)).astype(f32) * 0.2,
+         "fc1_w": rng.standard_normal((inter, hidden)).astype(f32) * 0.1,
+         "fc2_w": rng.standard_normal((hidden, inter)).astype(f32) * 0.1}
+    if zero_bias:
+        d["fc1_b"] = np.zeros((inter,), f32)
+        d["fc2_b"] = np.zeros((hidden,), f32)
+    else:
+        d["fc1_b"] = rng.standard_normal((inter,)).astype(f32) * 0.05
+        d["fc2_b"] = rng.standard_normal((hidden,)).astype(f32) * 0.05
+    return {k: _f16(v) for k, v in d.items()}
+
+
+def patch_embed_inputs(N, K, embed_dim, seed):
+    """Draw order of ``gen_patch_embed._make`` (gen_cpu_reference.py:2104-2107)."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    d = {"pixels": rng.standard_normal((N, K)).astype(f32) * 0.2,
+         "w": rng.standard_normal((embed_dim, K)).astype(f32) * 0.05,
+         "b": rng.standard_normal((embed_dim,)).astype(f32) * 0.05}
+    return {k: _f16(v) for k, v in d.items()}
+
+
 def linear_inputs(S, K, N):
     """Draw order of ``gen_linear._make_tb`` (gen_cpu_reference.py:898-902)."""
     import torch
