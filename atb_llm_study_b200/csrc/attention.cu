@@ -618,6 +618,7 @@ extern "C" int b200_flash_prefill(const void* q, int64_t q_stride, const void* k
                 : launch_prefill<HD, false>(q, q_stride, k, v, kv_stride, out, out_stride, cu_seqlens, num_seqs, \
                                             max_seqlen, nq, nkv, scale, stream)
   switch (head_dim) {
+    case 16: B200_PF(16);
     case 32: B200_PF(32);
     case 64: B200_PF(64);
     case 128: B200_PF(128);

@@ -85,6 +85,32 @@ B200_API int b200_rope_table_mrope(const int64_t* position_ids, int64_t T, int h
 B200_API int b200_rope_table_1d(const int64_t* positions, int64_t T, int head_dim, float theta, float* cos_out,
                        float* sin_out, b200_stream_t stream);
 
+/* cos/sin tables [T, head_dim] (fp32) of the 2-D vision rope for num_images
+ * grids grid_thw [num_images, 3] (host, t/h/w in patches; h, w multiples of
+ * merge_size; at most 64 images), tokens in merge-block order:
+ * freq = cat(row * inv_freq, col * inv_freq), inv_freq over head_dim/2 with
+ * step 2, emb = cat(freq, freq).  Replaces ComputeVisionRotPosEmb
+ * (atb_cpp_llm/src/components/common/mrope.cpp:155-228) and VisRopeGraph
+ * (atb_cpp_llm/src/components/vision/vis_rope_npu_graph.cpp:18-139). */
+B200_API int b200_rope_table_vision(const int64_t* grid_thw, int num_images, int merge_size, int head_dim,
+                                    float theta, float* cos_out, float* sin_out, b200_stream_t stream);
+
+/* In place half rotation x*cos + cat(-x2, x1)*sin on `nheads` consecutive
+ * heads of each row of x [T, stride] (any even head_dim), cos/sin [T, head_dim].
+ * Replaces RopeOp::Create(rotaryCoeff=2) where no per-head norm precedes it
+ * (atb_cpp_llm/src/components/vision/vision_attention_graph.cpp:71). */
+B200_API int b200_rope_apply(void* x, int64_t T, int nheads, int head_dim, int64_t stride, const float* cos_tab,
+                             const float* sin_tab, b200_stream_t stream);
+
+/* out[t] (+)= bilinear interpolation of the learned [num_grid^2, dim] position
+ * table at token t's patch position (tokens of grid_thw in merge-block order;
+ * accumulate != 0 adds onto out, e.g. the patch embeddings).  Replaces
+ * ComputePosEmbedInterp / PosEmbedInterpGraph
+ * (atb_cpp_llm/src/components/vision/pos_embed_interp.cpp:10-90,
+ * atb_cpp_llm/src/components/vision/pos_embed_npu_graph.cpp:19-211). */
+B200_API int b200_pos_embed_interp(const void* table, int num_grid, int64_t dim, const int64_t* grid_thw,
+                                   int num_images, int merge_size, void* out, int accumulate, b200_stream_t stream);
+
 /* In place on the fused projection output qkv [T, row_stride] laid out as
  * [q heads | k heads | v heads] x head_dim: per-head RMSNorm of q and k
  * (skipped when the norm weight is NULL), then the half rotation
@@ -134,7 +160,7 @@ B200_API int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int 
 /* Prefill attention over packed sequences: softmax(q k^T * scale [+ causal]) v,
  * GQA with nq % nkv == 0.  Sequence i owns rows cu_seqlens[i]..cu_seqlens[i+1]
  * of q [T, q_stride], k/v [T, kv_stride] (head h at column h*head_dim) and of
- * out [T, out_stride].  head_dim in {32, 64, 128}.  The causal rule (key j
+ * out [T, out_stride].  head_dim in {16, 32, 64, 128}.  The causal rule (key j
  * masked for query i when j > i) is applied in-kernel; no S x S mask exists.
  * Replaces SelfAttentionOp::Create (PA_ENCODER, BSND, MASK_TYPE_NORM)
  * (atb_cpp_llm/src/ops/self_attention_op.cpp:8-30) fed by
