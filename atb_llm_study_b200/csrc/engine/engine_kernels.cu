@@ -41,6 +41,39 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const 
   for (int64_t c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = s[c];
 }
 
+__global__ void scatter_rows_kernel(__nv_bfloat16* __restrict__ dst, const int32_t* __restrict__ idx, int64_t dim,
+                                    const __nv_bfloat16* __restrict__ src) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t r = blockIdx.x;
+  const uint4* s = reinterpret_cast<const uint4*>(src + r * dim);
+  uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)idx[r] * dim);
+  for (int64_t c = threadIdx.x; c < dim / 8; c += blockDim.x) d[c] = s[c];
+}
+
+// out = x / sqrt(sum(x^2) + 1e-12) (fp32 math), or a plain widening copy.
+__global__ void pool_l2_kernel(const __nv_bfloat16* __restrict__ x, int64_t dim, int normalize, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) {
+    const float v = bf2f(x[c]);
+    ss += v * v;
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = normalize ? 1.0f / sqrtf(red[0] + 1e-12f) : 1.0f;
+  for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) out[c] = bf2f(x[c]) * inv;
+}
+
 __global__ void decode_prepare_kernel(const int32_t* __restrict__ seq_slots, int B, int32_t* ctx_lens,
                                       const int32_t* __restrict__ bt, int max_blocks, int bs,
                                       int64_t* __restrict__ positions, int64_t* __restrict__ slots,
@@ -90,6 +123,19 @@ int GatherRows(const void* src, const int32_t* idx, int64_t n, int64_t dim, void
   if (n <= 0) return 0;
   launch_kernel(gather_rows_kernel, dim3((unsigned)n), 128, 0, st, static_cast<const __nv_bfloat16*>(src), idx, dim,
                 static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
+}
+
+int ScatterRows(void* dst, const int32_t* idx, int64_t n, int64_t dim, const void* src, cudaStream_t st) {
+  if (n <= 0) return 0;
+  launch_kernel(scatter_rows_kernel, dim3((unsigned)n), 128, 0, st, static_cast<__nv_bfloat16*>(dst), idx, dim,
+                static_cast<const __nv_bfloat16*>(src));
+  return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
+}
+
+int PoolL2(const void* x, int64_t dim, int normalize, float* out, cudaStream_t st) {
+  if (dim <= 0) return 0;
+  launch_kernel(pool_l2_kernel, dim3(1), 512, 0, st, static_cast<const __nv_bfloat16*>(x), dim, normalize, out);
   return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
 }
 

@@ -12,6 +12,10 @@ int FillNormalBf16(void* x, int64_t n, float mean, float std, uint64_t seed, cud
 int FillConstBf16(void* x, int64_t n, float value, cudaStream_t st);
 // out[i, :] = src[idx[i], :]; bf16 rows of width dim (dim % 8 == 0).
 int GatherRows(const void* src, const int32_t* idx, int64_t n, int64_t dim, void* out, cudaStream_t st);
+// dst[idx[i], :] = src[i, :]; bf16 rows of width dim (dim % 8 == 0), unique idx.
+int ScatterRows(void* dst, const int32_t* idx, int64_t n, int64_t dim, const void* src, cudaStream_t st);
+// out[:dim] (fp32) = x / sqrt(sum(x^2) + 1e-12) when normalize, else x; one bf16 row.
+int PoolL2(const void* x, int64_t dim, int normalize, float* out, cudaStream_t st);
 
 // Per decode row b with cache slot s = seq_slots[b] and p = ctx_lens[s]:
 //   positions[plane*B + b] = p (three planes), slots[b] = paged slot of p,

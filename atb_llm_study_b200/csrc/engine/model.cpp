@@ -138,6 +138,8 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(seq_slots_, DType::INT32, {opt.max_batch}));
   B200_RETURN_IF(A(ctx_batch_, DType::INT32, {opt.max_batch}));
   B200_RETURN_IF(A(bt_batch_, DType::INT32, {opt.max_batch, max_blocks_}));
+  B200_RETURN_IF(A(inject_idx_, DType::INT32, {max_t_}));
+  B200_RETURN_IF(A(pooled_, DType::FP32, {H}));
 
   // split-K workspace: the largest any decode-sized projection asks for
   int64_t ws = 0;
@@ -153,7 +155,7 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   attn_ws_bytes_ = b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
   if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
 
-  pinned_bytes_ = (size_t)max_t_ * 8 * 5 + (size_t)(opt.max_batch + 1) * 16 + 4096;
+  pinned_bytes_ = (size_t)max_t_ * 8 * 5 + (size_t)(opt.max_batch + 1) * 16 + (size_t)H * 4 + 4096;
   B200_RETURN_IF(FromCuda(cudaMallocHost(&pinned_, pinned_bytes_)));
   return ctx_->Synchronize();
 }
@@ -288,7 +290,8 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     B200_RETURN_IF(b200::qk_norm_rope_launch(
         qkv_.data, T, nq, nkv, (int)hd, QKV, cfg_.qk_norm ? bf(qnorm_, l * hd) : nullptr,
         cfg_.qk_norm ? bf(knorm_, l * hd) : nullptr, cfg_.eps, cos_.as<float>(), sin_.as<float>(),
-        slots_.as<int64_t>(), kc, vc, num_blocks_, opt_.block_size, s_qkv > 1 ? ws : nullptr, s_qkv, st));
+        write_kv_ ? slots_.as<int64_t>() : nullptr, kc, vc, num_blocks_, opt_.block_size, s_qkv > 1 ? ws : nullptr,
+        s_qkv, st));
     uint16_t* q = static_cast<uint16_t*>(qkv_.data);
     if (!decode) {
       ++launches_;
@@ -320,7 +323,21 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, (int64_t)l * H * I), I, hidden_.data, H, H, I, B200_EPI_RESIDUAL,
                         hidden_.data, H, &s_d));
     const void* next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
-    if (s_d > 1) {
+    if (l < (int)inject_feats_.size() && inject_n_ > 0) {
+      // deepstack: hidden[rows] += feature[l] between this layer and the next norm
+      if (s_d > 1) {
+        ++launches_;
+        B200_RETURN_IF(b200::splitk_reduce(ws, s_d, T, H, B200_EPI_RESIDUAL, nullptr, hidden_.data, H, hidden_.data,
+                                           H, st));
+      }
+      ++launches_;
+      B200_RETURN_IF(b200_scatter_add_rows(hidden_.data, T, H, inject_idx_.as<int32_t>(), inject_feats_[l],
+                                           inject_n_, 1.0f, st));
+      if (next_norm) {
+        ++launches_;
+        B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, next_norm, normed_.data, nullptr, T, H, H, cfg_.eps, st));
+      }
+    } else if (s_d > 1) {
       ++launches_;
       if (next_norm)
         B200_RETURN_IF(b200::splitk_residual_rmsnorm(ws, s_d, T, H, hidden_.data, next_norm, normed_.data, cfg_.eps,
@@ -512,6 +529,89 @@ Status DecoderModel::Decode(const int64_t* ids, bool ids_on_device, const int32_
   B200_RETURN_IF(ctx_->Synchronize());
   std::memcpy(next_tokens, h_next, (size_t)batch * 8);
   return STATUS_OK;
+}
+
+Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* position_ids, const int32_t* vis_rows,
+                            int64_t n_vis, const void* vis_embeds, const void* const* deepstack, int n_ds,
+                            int64_t pool_row, bool normalize, float* out, void* hidden_out) {
+  if (!ids || !out || S <= 0 || S > max_t_ || S > INT32_MAX || pool_row < 0 || pool_row >= S || n_vis < 0 ||
+      n_vis > S || n_ds < 0 || n_ds > cfg_.layers)
+    return ERROR_INVALID_PARAM;
+  if (n_vis > 0 && (!vis_rows || !vis_embeds)) return ERROR_INVALID_PARAM;
+  if (n_ds > 0 && (n_vis == 0 || !deepstack)) return ERROR_INVALID_PARAM;
+  for (int i = 0; i < n_ds; ++i)
+    if (!deepstack[i]) return ERROR_INVALID_PARAM;
+  {
+    std::vector<char> seen((size_t)S, 0);
+    for (int64_t i = 0; i < n_vis; ++i) {
+      if (vis_rows[i] < 0 || vis_rows[i] >= S || seen[vis_rows[i]]) return ERROR_INVALID_PARAM;
+      seen[vis_rows[i]] = 1;
+    }
+  }
+  NoPdlScope no_pdl;
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden;
+  uint8_t* pin = static_cast<uint8_t*>(pinned_);
+  int64_t* h_pos = reinterpret_cast<int64_t*>(pin);
+  int64_t* h_ids = h_pos + 3 * S;
+  int32_t* h_rows = reinterpret_cast<int32_t*>(h_ids + S);
+  int32_t* h_cu = h_rows + n_vis;
+  for (int64_t t = 0; t < S; ++t)
+    for (int p = 0; p < 3; ++p) h_pos[p * S + t] = position_ids ? position_ids[p * S + t] : t;
+  std::memcpy(h_ids, ids, (size_t)S * 8);
+  if (n_vis) std::memcpy(h_rows, vis_rows, (size_t)n_vis * 4);
+  h_cu[0] = 0;
+  h_cu[1] = (int32_t)S;
+  h_cu[2] = (int32_t)pool_row;
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(pos_.data, h_pos, (size_t)3 * S * 8, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(ids_.data, h_ids, (size_t)S * 8, cudaMemcpyHostToDevice, st)));
+  if (n_vis)
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(inject_idx_.data, h_rows, (size_t)n_vis * 4, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(cu_.data, h_cu, 8, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(last_idx_.data, h_cu + 2, 4, cudaMemcpyHostToDevice, st)));
+  B200_RETURN_IF(ctx_->Synchronize());  // pinned staging is reused by the next call
+  cur_num_seqs_ = 1;
+  cur_max_len_ = (int)S;
+
+  const int hd = cfg_.head_dim;
+  if (cfg_.mrope)
+    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), S, hd, cfg_.rope_theta, cfg_.mrope_section[0],
+                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
+                                         sin_.as<float>(), st));
+  else
+    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), S, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
+                                      st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), S, embed_.data, cfg_.vocab, H, hidden_.data, st));
+  launches_ = 2;
+  if (n_vis) {
+    ++launches_;
+    B200_RETURN_IF(ScatterRows(hidden_.data, inject_idx_.as<int32_t>(), n_vis, H, vis_embeds, st));
+  }
+  write_kv_ = false;
+  inject_feats_.assign(deepstack, deepstack + n_ds);
+  inject_n_ = n_vis;
+  Status s = RunLayers(S, false, 0);
+  write_kv_ = true;
+  inject_feats_.clear();
+  inject_n_ = 0;
+  B200_RETURN_IF(s);
+  // final RMSNorm of the pooled row, then L2 pooling (BaseModel::RunPooling,
+  // atb_cpp_llm/src/families/base_model.cpp:137-199)
+  launches_ += 3;
+  B200_RETURN_IF(GatherRows(hidden_.data, last_idx_.as<int32_t>(), 1, H, last_hidden_.data, st));
+  B200_RETURN_IF(b200_rmsnorm(last_hidden_.data, nullptr, final_norm_.data, normed_.data, nullptr, 1, H, H, cfg_.eps,
+                              st));
+  B200_RETURN_IF(PoolL2(normed_.data, H, normalize ? 1 : 0, pooled_.as<float>(), st));
+  if (hidden_out) {
+    ++launches_;
+    B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, final_norm_.data, hidden_out, nullptr, S, H, H, cfg_.eps, st));
+  }
+  last_encode_launches_ = launches_;
+  float* h_out = reinterpret_cast<float*>(pin);
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(h_out, pooled_.data, (size_t)H * 4, cudaMemcpyDeviceToHost, st)));
+  B200_RETURN_IF(ctx_->Synchronize());
+  std::memcpy(out, h_out, (size_t)H * 4);
+  return FromCuda(cudaGetLastError());
 }
 
 int DecoderModel::DecodeLaunches() const { return last_decode_launches_; }

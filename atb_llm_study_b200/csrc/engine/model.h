@@ -68,7 +68,22 @@ class DecoderModel {
   Status Decode(const int64_t* ids, bool ids_on_device, const int32_t* slots, int batch, int64_t* next_tokens,
                 bool next_on_device, void* logits);
 
+  // Encoder forward of one sequence for a pooled embedding (the text stage of
+  // the Qwen3-VL embedding model): causal attention, no KV cache.  Rows
+  // vis_rows (host, n_vis) of the input embeddings are replaced by vis_embeds
+  // (device bf16 [n_vis, hidden]); deepstack[i] (device bf16 [n_vis, hidden])
+  // is added to the same rows after layer i.  position_ids: [3, S] host (null:
+  // 0..S-1).  Writes the final-normed row pool_row (L2-normalised when
+  // `normalize`) to out (host fp32 [hidden]); hidden_out (device bf16 [S,
+  // hidden], optional) receives every final-normed row.
+  Status Encode(const int64_t* ids, int64_t S, const int64_t* position_ids, const int32_t* vis_rows, int64_t n_vis,
+                const void* vis_embeds, const void* const* deepstack, int n_ds, int64_t pool_row, bool normalize,
+                float* out, void* hidden_out);
+  int EncodeLaunches() const { return last_encode_launches_; }
+
   cudaStream_t stream() const { return ctx_ ? ctx_->GetStream() : nullptr; }
+  ContextManager* context() const { return ctx_.get(); }
+  TensorAllocator* allocator() const { return alloc_.get(); }
   const ModelConfig& config() const { return cfg_; }
   size_t WeightBytes() const { return weight_bytes_; }
   size_t KvBytes() const { return kv_bytes_; }
@@ -96,7 +111,12 @@ class DecoderModel {
   int cur_num_seqs_ = 0, cur_max_len_ = 0;  // shape of the prefill in flight
   // kernel launches counted while the last decode step / prefill was enqueued
   // (a replayed decode graph launches what its capture counted)
-  int launches_ = 0, last_decode_launches_ = 0, last_prefill_launches_ = 0;
+  int launches_ = 0, last_decode_launches_ = 0, last_prefill_launches_ = 0, last_encode_launches_ = 0;
+  // set by Encode for the duration of one RunLayers: KV writes off, and the
+  // deepstack features added after layers 0..size-1 at rows inject_idx_[:inject_n_]
+  bool write_kv_ = true;
+  std::vector<const void*> inject_feats_;
+  int64_t inject_n_ = 0;
 
   // weights (all layers stacked)
   DeviceTensor embed_, lm_head_, final_norm_;
@@ -106,7 +126,7 @@ class DecoderModel {
   DeviceTensor block_tables_, ctx_lens_;
   // activations / scratch
   DeviceTensor ids_, hidden_, normed_, qkv_, attn_, act_, cos_, sin_, pos_, slots_, cu_, last_idx_, last_hidden_,
-      logits_, next_, seq_slots_, ctx_batch_, bt_batch_, gemm_ws_, attn_ws_;
+      logits_, next_, seq_slots_, ctx_batch_, bt_batch_, gemm_ws_, attn_ws_, inject_idx_, pooled_;
   int64_t gemm_ws_bytes_ = 0, attn_ws_bytes_ = 0;
   std::vector<int32_t> host_ctx_;
   // pinned staging for host <-> device copies

@@ -80,6 +80,18 @@ B200_API int b200_layernorm(const void* x, const void* gamma, const void* beta, 
 B200_API int b200_rope_table_mrope(const int64_t* position_ids, int64_t T, int head_dim, float theta, int section_t,
                           int section_h, int section_w, float* cos_out, float* sin_out, b200_stream_t stream);
 
+/* Host function (no GPU): 3-D position ids [3, batch, seq_len] (int64,
+ * bit-exact) of text + image sequences.  Text runs are consecutive; the image
+ * tokens after a vision-start token take their merged (t, h, w) grid offsets
+ * from the running position, and the next run starts max(t, h/merge, w/merge)
+ * later.  Images are taken from image_grid_thw [num_images, 3] in order;
+ * tokens outside attention_mask (optional [batch, seq_len]) get 1.
+ * Replaces GetRopeIndex (atb_cpp_llm/src/components/common/mrope.cpp:234-348). */
+B200_API int b200_get_rope_index(const int64_t* input_ids, int64_t batch, int64_t seq_len,
+                                 const int64_t* attention_mask, const int64_t* image_grid_thw, int64_t num_images,
+                                 int64_t image_token_id, int64_t vision_start_token_id, int64_t spatial_merge_size,
+                                 int64_t* position_ids);
+
 /* cos/sin tables [T, head_dim] (fp32) for standard 1-D rope from positions [T].
  * Replaces Rope1D::Compute (atb_cpp_llm/src/components/common/rope_1d.h:23-167). */
 B200_API int b200_rope_table_1d(const int64_t* positions, int64_t T, int head_dim, float theta, float* cos_out,
@@ -269,7 +281,11 @@ enum b200_engine_query_key {
   B200_Q_PREFILL_LAUNCHES = 3, /* kernels one b200_engine_prefill call launches */
   B200_Q_HIDDEN = 4,
   B200_Q_LAYERS = 5,
-  B200_Q_VOCAB = 6
+  B200_Q_VOCAB = 6,
+  B200_Q_HAS_VISION = 7,           /* 1 when the config carried a vision tower */
+  B200_Q_VISION_WEIGHT_BYTES = 8,
+  B200_Q_VISION_LAUNCHES = 9,      /* kernels the last b200_engine_vision / embed vision stage launched */
+  B200_Q_ENCODE_LAUNCHES = 10      /* kernels the last b200_engine_embed text stage launched */
 };
 
 /* Model type is resolved from config.json "model_type" through a registry with
@@ -303,6 +319,36 @@ B200_API int b200_engine_prefill(b200_engine_t engine, const int64_t* ids, int i
  * false for its only model, atb_cpp_llm/include/atb_llm/model.h:47-50). */
 B200_API int b200_engine_decode(b200_engine_t engine, const int64_t* ids, int ids_on_device, const int32_t* slots,
                                 int batch, int64_t* next_tokens, int next_on_device, void* logits);
+
+/* Vision tower of a Qwen3-VL engine: pixels [num_patches, C*tp*p*p] in the
+ * image processor's merge-block order (host bf16/fp16/fp32 by pixel_dtype
+ * 0/1/2, or device bf16), grid_thw [num_images, 3] (host).  Writes the merged
+ * embeddings [num_patches / merge^2, out_hidden] (device bf16) to merged_out
+ * and the deepstack features [num_deepstack, num_patches / merge^2,
+ * out_hidden] to deepstack_out when not NULL; *merged_tokens when not NULL.
+ * Replaces the vision stage of Qwen3VLModel::ForwardWithTiming
+ * (atb_cpp_llm/src/adapters/qwen3vl_embedding/qwen3vl_model.cpp:384-575) and
+ * VisionRunner (atb_cpp_llm/src/runners/vision_runner.cpp:57-113). */
+B200_API int b200_engine_vision(b200_engine_t engine, const void* pixels, int pixel_dtype, int pixels_on_device,
+                                int64_t num_patches, const int64_t* grid_thw, int num_images, void* merged_out,
+                                void* deepstack_out, int64_t* merged_tokens);
+
+/* Qwen3-VL embedding forward of one request: input_ids [seq_len] (host),
+ * optional attention_mask [seq_len] (host; pools the last unmasked token),
+ * optional image (pixels as for b200_engine_vision; NULL = text only).  The
+ * merged vision embeddings replace the rows of the image tokens, deepstack
+ * feature i is added to them after text layer i, position ids follow
+ * b200_get_rope_index, attention is causal.  Writes the final-normed pooled
+ * token, L2-normalised when `normalize`, to embedding (host fp32 [hidden]);
+ * hidden_out (device bf16 [seq_len, hidden]) receives every final-normed row
+ * when not NULL.  An image-token count that differs from the merged vision
+ * token count is ERROR_INVALID_PARAM.  Replaces Qwen3VLModel::Forward /
+ * ForwardWithTiming (atb_cpp_llm/src/adapters/qwen3vl_embedding/qwen3vl_model.cpp:262-802)
+ * with BaseModel::RunPooling (atb_cpp_llm/src/families/base_model.cpp:137-199). */
+B200_API int b200_engine_embed(b200_engine_t engine, const int64_t* input_ids, int64_t seq_len,
+                               const int64_t* attention_mask, const void* pixels, int pixel_dtype,
+                               int pixels_on_device, int64_t num_patches, const int64_t* grid_thw, int num_images,
+                               int normalize, float* embedding, void* hidden_out);
 
 /* The engine's CUDA stream (device-side results are ordered on it). */
 B200_API int b200_engine_stream(b200_engine_t engine, b200_stream_t* out);

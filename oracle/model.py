@@ -29,3 +29,41 @@ def forward_last_logits(ids, w, cfg):
         x = decoder_layer(x, lw, cos, sin, cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"], causal=True)
     h = rms_norm(x[-1:], w["norm"], cfg["eps"])
     return linear(h, w["lm_head"])[0]
+
+
+def embed_forward(ids, w, cfg, position_ids=None, vis_rows=None, vis_embeds=None, deepstack=(), pool_row=None,
+                  normalize=True):
+    """Pooled embedding of one sequence: the Qwen3-VL embedding text stage.
+
+    Token embedding, the rows ``vis_rows`` replaced by ``vis_embeds``, the
+    decoder layers with mrope (``position_ids [3, S]``; ``cfg["mrope"]``
+    sections) or 1-D rope, ``deepstack[i]`` added to the same rows after layer
+    i, final RMSNorm, the row ``pool_row`` (default last), L2-normalised with
+    ``sqrt(sum(x^2) + 1e-12)``.  Mirrors Qwen3VLModel::ForwardWithTiming's text
+    stage and pooling (qwen3vl_model.cpp:576-800; DeepstackFusion::InjectFeatures,
+    deepstack_fusion.cpp:143-201; BaseModel::RunPooling, base_model.cpp:137-199).
+    Returns ``(embedding [H], final-normed hidden [S, H])``.
+    """
+    from .positions import mrope_cos_sin
+
+    ids = np.asarray(ids, np.int64)
+    S = len(ids)
+    V = w["embed"].shape[0]
+    x = np.where(((ids >= 0) & (ids < V))[:, None], w["embed"][np.clip(ids, 0, V - 1)], 0).astype(np.float32)
+    if vis_rows is not None and len(vis_rows):
+        x[np.asarray(vis_rows)] = vis_embeds
+    if cfg.get("mrope"):
+        pid = np.arange(S)[None].repeat(3, 0) if position_ids is None else np.asarray(position_ids, np.int64)
+        cos, sin = mrope_cos_sin(pid[:, None, :], cfg["head_dim"], cfg["theta"], tuple(cfg["mrope"]))
+        cos, sin = cos[0], sin[0]
+    else:
+        cos, sin = rope1d_cos_sin(np.arange(S), cfg["head_dim"], cfg["theta"])
+    for i, lw in enumerate(w["layers"]):
+        x = decoder_layer(x, lw, cos, sin, cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"], causal=True)
+        if i < len(deepstack):
+            x[np.asarray(vis_rows)] += deepstack[i]
+    h = rms_norm(x, w["norm"], cfg["eps"])
+    p = h[S - 1 if pool_row is None else pool_row]
+    if normalize:
+        p = p / np.sqrt(np.sum(p * p) + np.float32(1e-12))
+    return p.astype(np.float32), h

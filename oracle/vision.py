@@ -58,3 +58,44 @@ def vision_merger(x, n_w, n_b, f1_w, f1_b, f2_w, f2_b, merge=2, deepstack=False,
     else:
         h = layer_norm(x, n_w, n_b, eps).reshape(N // g, H * g)
     return linear(gelu_tanh(linear(h, f1_w, f1_b)), f2_w, f2_b)
+
+
+def vision_tower(pixels, grid_thw, w, cfg):
+    """Whole vision tower: patch embed + interpolated position embedding, the
+    blocks (attention within each temporal frame of each image), a deepstack
+    merger after each block listed in ``cfg["deepstack"]``, the main merger.
+    Returns ``(merged [N/m^2, out], [deepstack_i [N/m^2, out], ...])``.
+
+    Composes the pinned pieces above the way Qwen3VLModel::ForwardWithTiming's
+    vision stage runs them (atb_cpp_llm/src/adapters/qwen3vl_embedding/
+    qwen3vl_model.cpp:384-575; first layer = patch embed + pos embed + block 0,
+    vision_runner.cpp:57-113; deepstack taps deepstack_fusion.cpp:55-105).
+    ``w``: patch_w patch_b pos_table, ``blocks`` (list of vision_block dicts),
+    ``merger`` and ``deepstack_mergers`` (dicts n_w n_b f1_w f1_b f2_w f2_b).
+    ``cfg``: heads, merge, eps, deepstack (block indexes), num_grid.
+    """
+    from .positions import pos_embed_interp, vision_rope_cos_sin
+
+    grid = np.asarray(grid_thw, np.int64)
+    hidden = w["patch_w"].shape[0]
+    nh = cfg["heads"]
+    hd = hidden // nh
+    m = cfg["merge"]
+    eps = cfg.get("eps", 1e-6)
+    x = patch_embed(np.asarray(pixels, np.float32), w["patch_w"], w["patch_b"])
+    x = x + pos_embed_interp(w["pos_table"], grid, cfg["num_grid"], m)
+    cos, sin = vision_rope_cos_sin(grid, hd, m)
+    cu = [0]
+    for t, h, ww in grid:
+        for _ in range(int(t)):
+            cu.append(cu[-1] + int(h * ww))
+    ds = []
+    for i, bw in enumerate(w["blocks"]):
+        x = vision_block(x, bw, cos, sin, nh, hd, eps, cu_seqlens=cu)
+        if i in cfg["deepstack"]:
+            mw = w["deepstack_mergers"][cfg["deepstack"].index(i)]
+            ds.append(vision_merger(x, *(mw[k] for k in ("n_w", "n_b", "f1_w", "f1_b", "f2_w", "f2_b")), merge=m,
+                                    deepstack=True, eps=eps))
+    mw = w["merger"]
+    merged = vision_merger(x, *(mw[k] for k in ("n_w", "n_b", "f1_w", "f1_b", "f2_w", "f2_b")), merge=m, eps=eps)
+    return merged, ds
