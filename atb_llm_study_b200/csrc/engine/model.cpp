@@ -141,10 +141,14 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(inject_idx_, DType::INT32, {max_t_}));
   B200_RETURN_IF(A(pooled_, DType::FP32, {H}));
 
-  // split-K workspace: the largest any decode-sized projection asks for
+  // split-K workspace: the largest any projection asks for at any token count
+  // this engine runs (K is split only while the output tiles leave SMs idle,
+  // so the need stops growing after a few thousand tokens)
   int64_t ws = 0;
   const int64_t shapes[5][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}};
-  for (int64_t m : {(int64_t)1, (int64_t)opt.max_batch})
+  std::vector<int64_t> ms = {1, (int64_t)opt.max_batch};
+  for (int64_t m = 64; m <= std::min<int64_t>(max_t_, 65536); m += 64) ms.push_back(m);
+  for (int64_t m : ms)
     for (auto& s : shapes) ws = std::max(ws, b200_gemm_workspace_bytes(m, s[0], s[1], B200_EPI_NONE_));
   gemm_ws_bytes_ = ws;
   if (ws > 0) {

@@ -49,6 +49,14 @@ Status VisionConfig::FromJson(const JsonConfig& root, VisionConfig& c) {
 
 // ---------------------------------------------------------------- setup
 
+VisionModel::~VisionModel() { DropGraphs(); }
+
+void VisionModel::DropGraphs() {
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.second.exec);
+  graphs_.clear();
+  calls_.clear();
+}
+
 Status VisionModel::Init(const VisionConfig& cfg, ContextManager* ctx, TensorAllocator* alloc) {
   if (!ctx || !alloc) return ERROR_INVALID_PARAM;
   cfg_ = cfg;
@@ -186,6 +194,7 @@ int VisionModel::DeepstackSlot(int block) const {
 Status VisionModel::Reserve(int64_t N, int64_t frames) {
   if (N <= cap_patches_ && frames <= cap_frames_) return STATUS_OK;
   B200_RETURN_IF(ctx_->Synchronize());
+  DropGraphs();  // captured passes point at the buffers freed below
   N = std::max(N, cap_patches_);
   frames = std::max(frames, cap_frames_);
   for (DeviceTensor* t : {&pix_, &h_, &normed_, &qkv_, &attn_, &act_, &cos_, &sin_, &cu_, &merged_, &ds_, &ws_})
@@ -271,8 +280,7 @@ Status VisionModel::Forward(const void* pixels, DType dtype, bool on_device, int
   if (on_device && dtype != DType::BF16) return ERROR_UNSUPPORTED;
   B200_RETURN_IF(Reserve(N, frames));
   cudaStream_t st = ctx_->GetStream();
-  const int64_t H = cfg_.hidden, I = cfg_.intermediate, P = cfg_.patch_dim(), hd = cfg_.head_dim();
-  const int nh = cfg_.heads;
+  const int64_t P = cfg_.patch_dim();
   const void* pix = pixels;
   if (!on_device) {
     std::vector<uint16_t> b16;
@@ -285,12 +293,48 @@ Status VisionModel::Forward(const void* pixels, DType dtype, bool on_device, int
     return ERROR_INVALID_PARAM;
   }
   B200_RETURN_IF(FromCuda(cudaMemcpyAsync(cu_.data, cu.data(), cu.size() * 4, cudaMemcpyHostToDevice, st)));
+  if (pix != pix_.data)  // the tower always reads pix_, so a captured graph serves any caller buffer
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(pix_.data, pix, (size_t)(N * P) * 2, cudaMemcpyDeviceToDevice, st)));
   B200_RETURN_IF(FromCuda(cudaStreamSynchronize(st)));
   merged_tokens_ = N / ((int64_t)m * m);
+
+  // The kernel sequence depends only on the image grids: it is captured in a
+  // CUDA graph the second time a grid list is seen and replayed afterwards.
+  static const bool no_graph = EnvInt("B200_DISABLE_GRAPHS", 0) != 0;
+  std::vector<int64_t> key(grid_thw, grid_thw + 3 * num_images);
+  auto it = graphs_.find(key);
+  if (it != graphs_.end()) {
+    launches_ = it->second.launches;
+    return FromCuda(cudaGraphLaunch(it->second.exec, st));
+  }
+  if (no_graph || ++calls_[key] < 2) return RunTower(N, grid_thw, num_images, (int)frames, max_len);
+  B200_RETURN_IF(FromCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed)));
+  Status s = RunTower(N, grid_thw, num_images, (int)frames, max_len);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (s != STATUS_OK || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return s != STATUS_OK ? s : FromCuda(e);
+  }
+  cudaGraphExec_t ex = nullptr;
+  e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  B200_RETURN_IF(FromCuda(e));
+  graphs_[key] = {ex, launches_};
+  return FromCuda(cudaGraphLaunch(ex, st));
+}
+
+// Patch embed + position embedding, the blocks with their deepstack taps, the
+// main merger: every kernel of one tower pass, enqueued on the stream.
+Status VisionModel::RunTower(int64_t N, const int64_t* grid_thw, int num_images, int frames, int max_len) {
+  cudaStream_t st = ctx_->GetStream();
+  const int m = cfg_.merge;
+  const int64_t H = cfg_.hidden, I = cfg_.intermediate, P = cfg_.patch_dim(), hd = cfg_.head_dim();
+  const int nh = cfg_.heads;
   launches_ = 0;
 
   // patch embedding (Conv3d with stride = kernel is a linear map of the flattened patch)
-  B200_RETURN_IF(Gemm(pix, P, patch_w_.data, h_.data, H, N, H, P, B200_EPI_BIAS, patch_b_.data, nullptr, 0));
+  B200_RETURN_IF(Gemm(pix_.data, P, patch_w_.data, h_.data, H, N, H, P, B200_EPI_BIAS, patch_b_.data, nullptr, 0));
   launches_ += 2;
   B200_RETURN_IF(b200_pos_embed_interp(pos_table_.data, cfg_.grid(), H, grid_thw, num_images, m, h_.data, 1, st));
   B200_RETURN_IF(b200_rope_table_vision(grid_thw, num_images, m, (int)hd, cfg_.rope_theta, cos_.as<float>(),

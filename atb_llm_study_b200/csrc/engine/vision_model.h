@@ -15,6 +15,7 @@
 // bidirectional within each temporal frame of each image.
 #pragma once
 
+#include <map>
 #include <string>
 #include <vector>
 
@@ -42,7 +43,9 @@ struct VisionConfig {
 class VisionModel {
  public:
   VisionModel() = default;
-  ~VisionModel() = default;
+  ~VisionModel();
+  VisionModel(const VisionModel&) = delete;
+  VisionModel& operator=(const VisionModel&) = delete;
 
   // Weights are allocated from `alloc` (shared with the text decoder); all work
   // runs on `ctx`'s stream.
@@ -68,6 +71,8 @@ class VisionModel {
 
  private:
   Status Reserve(int64_t patches, int64_t frames);
+  Status RunTower(int64_t N, const int64_t* grid_thw, int num_images, int frames, int max_len);
+  void DropGraphs();
   Status Gemm(const void* A, int64_t lda, const void* W, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi,
               const void* bias, const void* R, int64_t ldr);
   Status Merger(const void* x, int64_t N, int which, void* out);
@@ -93,6 +98,14 @@ class VisionModel {
   // activations, grown on demand
   DeviceTensor pix_, h_, normed_, qkv_, attn_, act_, cos_, sin_, cu_, merged_, ds_, ws_;
   int64_t ws_bytes_ = 0;
+
+  // tower passes captured per grid list (flattened grid_thw) on its second call
+  struct Captured {
+    cudaGraphExec_t exec;
+    int launches;
+  };
+  std::map<std::vector<int64_t>, Captured> graphs_;
+  std::map<std::vector<int64_t>, int> calls_;
 };
 
 }  // namespace b200llm

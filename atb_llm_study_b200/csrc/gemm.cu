@@ -493,17 +493,23 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
   if (g.swap) g.bn = mma_cols <= 64 ? 64 : 128;
   else g.bn = mma_cols > 128 ? 256 : 128;
   g.tiles_m = (int)((mma_rows + BM - 1) / BM);
+  // Few 256-wide tiles over a short K (the few-hundred-token GEMMs of the
+  // vision tower and of short prompts): 128-wide tiles put twice as many CTAs
+  // to work; with long K the wider tile's lower bytes per flop wins instead.
+  if (!g.swap && g.bn == 256 && 2 * g.tiles_m * ((mma_cols + 255) / 256) < sms && K <= 2048) g.bn = 128;
   g.tiles_n = (int)((mma_cols + g.bn - 1) / g.bn);
   g.kb_total = (int)((K + BK - 1) / BK);
   const int tiles = g.tiles_m * g.tiles_n;
   // Split K only when the output tiles leave SMs idle.  Each split keeps
-  // >= 16 k-blocks (its pipeline fill stays small next to its weight stream)
-  // and every extra split is charged 3 % for its partial-tile traffic.
+  // >= 16 k-blocks (its pipeline fill stays small next to its weight stream;
+  // 8 when token-major tiles cover under half the SMs) and every extra split
+  // is charged 3 % for its partial-tile traffic.
+  const int min_kb = (!g.swap && 2 * tiles < sms) ? 8 : 16;
   int best = 1;
   if (tiles < 2 * sms) {
     double best_score = (double)tiles / ((double)sms * ((tiles + sms - 1) / sms)) - 0.03;
     for (int s = 2; s <= 16; ++s) {
-      if (g.kb_total / s < 16) break;
+      if (g.kb_total / s < min_kb) break;
       const int u = tiles * s;
       const double score = (double)u / ((double)sms * ((u + sms - 1) / sms)) - 0.03 * s;
       if (score > best_score + 0.02) {

@@ -258,6 +258,98 @@ def kernel_roofline_prefill_gemm(L, torch, dev, reps=10):
     return ms, 2.0 * M * N * K
 
 
+QWEN3VL_2B = dict(
+    model_type="qwen3_vl", image_token_id=151655, vision_start_token_id=151652, tie_word_embeddings=True,
+    text_config=dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                     head_dim=128, intermediate_size=6144, vocab_size=151936, rms_norm_eps=1e-6, rope_theta=5e6,
+                     rope_scaling=dict(mrope_section=[24, 20, 20], mrope_interleaved=True)),
+    vision_config=dict(depth=24, hidden_size=1024, num_heads=16, intermediate_size=4096, patch_size=16,
+                       temporal_patch_size=2, in_channels=3, spatial_merge_size=2, out_hidden_size=2048,
+                       num_position_embeddings=2304, deepstack_visual_indexes=[5, 11, 17]))
+VL_GRID, VL_SEQ = (1, 28, 28), 256
+# algorithmic work of one request (2*params*tokens per linear + 2*2*S^2*hidden per attention):
+# vision: 24 blocks (qkv, proj, fc1, fc2 over 784 tokens + bidirectional attention over 784) +
+# patch embed + main merger + 3 deepstack mergers over 196 merged tokens;
+# text: 28 layers over 256 tokens with causal attention counted as half of S^2.
+VL_VISION_FLOP = (24 * (2 * 784 * (3 * 1024 * 1024 + 1024 * 1024 + 2 * 4096 * 1024) + 4 * 784 * 784 * 1024)
+                  + 2 * 784 * 1536 * 1024 + 4 * 2 * 196 * (4096 * 4096 + 2048 * 4096))
+VL_TEXT_FLOP = 28 * (2 * 256 * (2048 * (2048 + 2 * 1024) + 2048 * 2048 + 3 * 2048 * 6144) + 2 * 256 * 256 * 2048)
+
+
+def bench_qwen3vl(L, torch, dev, steps, warm, stream_of):
+    """Qwen3-VL-2B embedding request: 448x448 image (grid 1x28x28 = 784 patches,
+    196 merged tokens) inside a 256-token prompt; vision tower alone, then the
+    whole embedding forward (vision -> deepstack -> 28 text layers -> pooling)."""
+    import numpy as np
+
+    cfg = EngineConfig(None, json.dumps(QWEN3VL_2B).encode(), dev.index, 1, 1024, 1024, BLOCK, 99, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create qwen3vl")
+    est = stream_of(eng)
+    try:
+        t, h, w = VL_GRID
+        N = t * h * w
+        rng = np.random.default_rng(5)
+        px_host = rng.uniform(-1, 1, (N, 1536)).astype(np.float32)
+        px_dev = torch.from_numpy(px_host).to(dev).to(torch.bfloat16)
+        grid = np.array([VL_GRID], np.int64)
+        n_img = N // 4
+        tail = VL_SEQ - n_img - 31
+        ids = np.concatenate([rng.integers(0, 151000, 30), [151652], np.full(n_img, 151655),
+                              rng.integers(0, 151000, tail)]).astype(np.int64)
+        emb = np.zeros(2048, np.float32)
+
+        def q(k):
+            v = ctypes.c_int64()
+            check(L.b200_engine_query(eng, k, ctypes.byref(v)), "query")
+            return v.value
+
+        def vision(_):
+            check(L.b200_engine_vision(eng, px_dev.data_ptr(), 0, 1, N, grid.ctypes.data, 1, None, None, None),
+                  "vision")
+
+        def embed_dev(_):
+            check(L.b200_engine_embed(eng, ids.ctypes.data, VL_SEQ, None, px_dev.data_ptr(), 0, 1, N,
+                                      grid.ctypes.data, 1, 1, emb.ctypes.data, None), "embed")
+
+        def embed_host(_):
+            check(L.b200_engine_embed(eng, ids.ctypes.data, VL_SEQ, None, px_host.ctypes.data, 2, 0, N,
+                                      grid.ctypes.data, 1, 1, emb.ctypes.data, None), "embed")
+
+        def timed(fn, n):
+            for i in range(warm):
+                fn(i)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(est)
+            for i in range(n):
+                fn(i)
+            e1.record(est)
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1) / n
+
+        vis_ms = timed(vision, steps)
+        vis_launches = q(9)
+        emb_ms = timed(embed_dev, steps)
+        enc_launches = q(10)
+        e2e_ms = timed(embed_host, steps)
+        assert abs(float(np.linalg.norm(emb)) - 1.0) < 1e-2
+        _, tf_burst, _, src = peaks()
+        flop = VL_VISION_FLOP + VL_TEXT_FLOP
+        return {
+            "workload": "Qwen3-VL-2B embedding: 448x448 image (784 patches -> 196 tokens) in a 256-token prompt",
+            "vision_ms": vis_ms, "vision_tflops": VL_VISION_FLOP / (vis_ms / 1e3) / 1e12,
+            "vision_frac": VL_VISION_FLOP / (vis_ms / 1e3) / 1e12 / tf_burst,
+            "embed_ms": emb_ms, "embed_tflops": flop / (emb_ms / 1e3) / 1e12,
+            "embed_frac": flop / (emb_ms / 1e3) / 1e12 / tf_burst,
+            "requests_per_s": 1e3 / emb_ms, "e2e_ms": e2e_ms, "e2e_requests_per_s": 1e3 / e2e_ms,
+            "flop_per_request": flop, "peak_source": f"{src} bf16 burst",
+            "launches": {"vision": vis_launches, "text": enc_launches},
+        }
+    finally:
+        L.b200_engine_destroy(eng)
+
+
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -383,6 +475,13 @@ def run_b200(args, rank, world, local_rank):
     gemm_ms, gemm_flops = kernel_roofline_prefill_gemm(L, torch, dev)
     L.b200_engine_destroy(eng)
 
+    def stream_of(e):
+        s = ctypes.c_void_p()
+        check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
+        return torch.cuda.ExternalStream(s.value, device=dev)
+
+    vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
     pf_tok_s = world * T * steps / (pf_ms / 1e3)
     result = {
@@ -427,6 +526,8 @@ def run_b200(args, rank, world, local_rank):
                              f"{prefill_launches}",
         "clocks": clocks,
     }
+    if vl:
+        result["qwen3vl_embedding"] = vl
     if dist:
         dist.barrier()
     if rank == 0:
@@ -475,6 +576,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-vl", action="store_true", help="skip the Qwen3-VL-2B embedding section")
+    ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm"],
                     help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
@@ -496,6 +599,22 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.vl_only:
+        import torch
+
+        from atb_llm_study_b200 import capi
+
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        L = capi.lib()
+
+        def stream_of(e):
+            s = ctypes.c_void_p()
+            check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
+            return torch.cuda.ExternalStream(s.value, device=dev)
+
+        print(json.dumps(bench_qwen3vl(L, torch, dev, args.steps, args.warmup, stream_of)), flush=True)
         return
     run_b200(args, rank, world, local_rank)
 

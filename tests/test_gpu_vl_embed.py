@@ -141,14 +141,24 @@ def test_vision_tower(engine, grid):
     merged = torch.empty(Nm, 512, dtype=torch.bfloat16, device=G.DEV)
     ds = torch.empty(2, Nm, 512, dtype=torch.bfloat16, device=G.DEV)
     nm = ctypes.c_int64()
-    G.check(L.b200_engine_vision(eng, px.ctypes.data, 2, 0, len(px), g.ctypes.data, len(g), merged.data_ptr(),
-                                 ds.data_ptr(), ctypes.byref(nm)), "engine_vision")
-    torch.cuda.synchronize()
-    assert nm.value == Nm
     ref_m, ref_ds = vision_tower(G.rounded(px), g, vis, VCFG)
-    close(G.host(merged), ref_m)
-    for i in range(2):
-        close(G.host(ds[i]), ref_ds[i])
+    # eager pass, captured pass, replayed graph (device pixels on the last one)
+    px_dev = G.bf16(px)
+    for rep in range(3):
+        merged.zero_()
+        ds.zero_()
+        torch.cuda.synchronize()  # the engine runs on its own stream
+        if rep < 2:
+            G.check(L.b200_engine_vision(eng, px.ctypes.data, 2, 0, len(px), g.ctypes.data, len(g),
+                                         merged.data_ptr(), ds.data_ptr(), ctypes.byref(nm)), "engine_vision")
+        else:
+            G.check(L.b200_engine_vision(eng, px_dev.data_ptr(), 0, 1, len(px), g.ctypes.data, len(g),
+                                         merged.data_ptr(), ds.data_ptr(), ctypes.byref(nm)), "engine_vision")
+        torch.cuda.synchronize()
+        assert nm.value == Nm
+        close(G.host(merged), ref_m)
+        for i in range(2):
+            close(G.host(ds[i]), ref_ds[i])
     assert G.device_errors() == 0
 
 
