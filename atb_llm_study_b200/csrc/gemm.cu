@@ -37,6 +37,8 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
+constexpr int kMaxGroups = 256;                            // experts of one grouped GEMM
+constexpr int kGroupTabBytes = 2 * (kMaxGroups + 2) * 4;  // row offsets + unit prefix in shared memory
 
 template <int BN>
 struct Cfg {
@@ -46,6 +48,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_GROUPED = SMEM + kGroupTabBytes;
   static constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
 };
 
@@ -61,6 +64,22 @@ struct Params {
   int64_t ldr;
   float* ws;  // split-K fp32 partial tiles [splits][tokens][features]
   unsigned* err;
+  // Grouped (per-expert) GEMM: the tokens of group g are rows [goff[g],
+  // goff[g+1]) of the token operand and its weights are rows [g*gN, (g+1)*gN)
+  // of the weight operand; the output row of a token is its token row.
+  const int32_t* goff;
+  int groups;
+  int64_t gN;
+  int gF;          // feature tiles per group
+  int64_t gRows;   // rows of the token operand (goff is clamped to it)
+};
+
+// One output tile: its MMA tile coordinates, K range, the TMA row coordinates
+// of both operands and the epilogue's row / column origin and limits.
+struct Unit {
+  int tm, tn, kb0, kb1;
+  int a_row, b_row;
+  int64_t row0, col0, row_lim, col_lim;
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -161,7 +180,61 @@ __device__ __forceinline__ void decode_unit(int w, const Params& p, int& tm, int
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
 
-template <int BN, int EPI, bool SWAP, bool PARTIAL>
+// Unit w of the launch.  Plain GEMM: decode_unit's raster.  Grouped: gtab[0..G]
+// holds the groups' token row offsets and gtab[G+1..2G+1] the prefix of their
+// unit counts; within a group the token tiles of one feature tile are
+// consecutive (they share that weight tile).
+template <int BN, bool SWAP, bool GROUPED>
+__device__ __forceinline__ Unit get_unit(int w, const Params& p, const int* gtab) {
+  Unit u;
+  if (!GROUPED) {
+    decode_unit(w, p, u.tm, u.tn, u.kb0, u.kb1);
+    u.a_row = u.tm * BM;
+    u.b_row = u.tn * BN;
+    u.row0 = (int64_t)u.tm * BM;
+    u.col0 = (int64_t)u.tn * BN;
+    u.row_lim = p.rows;
+    u.col_lim = p.cols;
+    return u;
+  }
+  const int* up = gtab + p.groups + 1;
+  int lo = 0, hi = p.groups;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (up[mid] <= w) lo = mid;
+    else hi = mid;
+  }
+  const int g = lo;
+  constexpr int TOKT = SWAP ? BN : BM;
+  const int t0 = gtab[g], t1 = gtab[g + 1];
+  const int tt = (t1 - t0 + TOKT - 1) / TOKT;
+  const int r = w - up[g];
+  const int tok = r % tt, feat = r / tt;
+  u.kb0 = 0;
+  u.kb1 = p.kb_total;
+  if (SWAP) {
+    u.tm = feat;
+    u.tn = tok;
+    u.a_row = (int)(g * p.gN) + feat * BM;
+    u.b_row = t0 + tok * BN;
+    u.row0 = (int64_t)feat * BM;
+    u.row_lim = p.gN;
+    u.col0 = (int64_t)t0 + (int64_t)tok * BN;
+    u.col_lim = t1;
+  } else {
+    u.tm = tok;
+    u.tn = feat;
+    u.a_row = t0 + tok * BM;
+    u.b_row = (int)(g * p.gN) + feat * BN;
+    u.row0 = (int64_t)t0 + (int64_t)tok * BM;
+    u.row_lim = t1;
+    u.col0 = (int64_t)feat * BN;
+    u.col_lim = p.gN;
+  }
+  return u;
+}
+
+template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const Params p) {
@@ -177,8 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  int* gtab = reinterpret_cast<int*>(smem + C::STAGES * C::STAGE_BYTES + 256);  // grouped launches only
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = p.tiles_m * p.tiles_n * p.splits;
+  int units = p.tiles_m * p.tiles_n * p.splits;
   pdl_trigger();
 
   if (warp == 0 && lane == 0) {
@@ -203,6 +278,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (GROUPED) {
+    // the group row offsets come from the previous kernel (the expert permutation)
+    pdl_wait();
+    if (threadIdx.x == 0) {
+      int prev = 0, run = 0;
+      for (int g = 0; g <= p.groups; ++g) {
+        int v = p.goff[g];
+        if (v < prev || v > p.gRows || (g == 0 && v != 0)) {
+          raise_error(p.err, DEV_ERR_BAD_INDEX);
+          v = min(max(v, prev), (int)p.gRows);
+          if (g == 0) v = 0;
+        }
+        gtab[g] = prev = v;
+      }
+      constexpr int TOKT = SWAP ? BN : BM;
+      for (int g = 0; g < p.groups; ++g) {
+        gtab[p.groups + 1 + g] = run;
+        run += ((gtab[g + 1] - gtab[g] + TOKT - 1) / TOKT) * p.gF;
+      }
+      gtab[2 * p.groups + 1] = run;
+    }
+    __syncthreads();
+    units = gtab[2 * p.groups + 1];
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -211,15 +310,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // tiles for the first stages are requested before waiting for the
       // previous kernel on the stream, so the weight stream starts while that
       // kernel drains.  Activation tiles are only loaded after the wait.
+      // (Grouped launches already waited: their tiles depend on the offsets.)
       int pre = 0;
-      if ((int)blockIdx.x < units) {
-        int tm0, tn0, kb00, kb10;
-        decode_unit(blockIdx.x, p, tm0, tn0, kb00, kb10);
-        pre = min(C::STAGES, kb10 - kb00);
+      if (!GROUPED && (int)blockIdx.x < units) {
+        const Unit u0 = get_unit<BN, SWAP, GROUPED>(blockIdx.x, p, gtab);
+        pre = min(C::STAGES, u0.kb1 - u0.kb0);
         for (int i = 0; i < pre; ++i) {
           mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          if (SWAP) tma_load_2d(sA + i * C::A_BYTES, &tmA, &full[i], (kb00 + i) * BK, tm0 * BM);
-          else tma_load_2d(sB + i * C::B_BYTES, &tmB, &full[i], (kb00 + i) * BK, tn0 * BN);
+          if (SWAP) tma_load_2d(sA + i * C::A_BYTES, &tmA, &full[i], (u0.kb0 + i) * BK, u0.a_row);
+          else tma_load_2d(sB + i * C::B_BYTES, &tmB, &full[i], (u0.kb0 + i) * BK, u0.b_row);
         }
       }
       pdl_wait();
@@ -227,21 +326,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool first = true;
       for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x) {
-        int tm, tn, kb0, kb1;
-        decode_unit(w, p, tm, tn, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (first && kb - kb0 < pre) {
+        const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+          if (first && kb - u.kb0 < pre) {
             // stage == kb - kb0 already expects both halves; add the activation half
-            if (SWAP) tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
-            else tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
+            if (SWAP) tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, u.b_row);
+            else tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, u.a_row);
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
               *abort_flag = 1;
               break;
             }
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, tm * BM);
-            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, tn * BN);
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, u.a_row);
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, u.b_row);
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -259,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
-        int tm, tn, kb0, kb1;
-        decode_unit(w, p, tm, tn, kb0, kb1);
+        const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
+        const int kb0 = u.kb0, kb1 = u.kb1;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) {
@@ -303,8 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rit = q * 32 + lane;
     int local = 0;
     for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
-      int tm, tn, kb0, kb1;
-      decode_unit(w, p, tm, tn, kb0, kb1);
+      const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
       const int split = w / (p.tiles_m * p.tiles_n);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -313,7 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = (int64_t)tm * BM + rit;
+      const int64_t row = u.row0 + rit;
+      Params pe = p;  // bounds of this tile's output (a group's rows in grouped launches)
+      pe.rows = u.row_lim;
+      pe.cols = u.col_lim;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         uint32_t r[32];
@@ -322,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        const int64_t col0 = (int64_t)tn * BN + ch * 32;
+        const int64_t col0 = u.col0 + ch * 32;
         if (PARTIAL) {
           // this K slice's partial tile -> ws[split][token][feature] (plain coalesced stores)
           if (row < p.rows) {
@@ -339,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         } else {
-          emit_chunk<EPI, SWAP>(v, row, col0, lane, p);
+          emit_chunk<EPI, SWAP>(v, row, col0, lane, pe);
         }
       }
       tc_fence_before();
@@ -398,18 +498,19 @@ int num_sms() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
-template <int BN, int EPI, bool SWAP, bool PARTIAL>
+template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false>
 int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int grid, cudaStream_t st) {
-  auto k = gemm_tcgen05_kernel<BN, EPI, SWAP, PARTIAL>;
+  auto k = gemm_tcgen05_kernel<BN, EPI, SWAP, PARTIAL, GROUPED>;
+  constexpr int smem = GROUPED ? Cfg<BN>::SMEM_GROUPED : Cfg<BN>::SMEM;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return B200_ERROR_UNSUPPORTED;
     attr_set[dev] = true;
   }
-  launch_kernel(k, dim3(grid), kThreads, Cfg<BN>::SMEM, st, a, b, p);
+  launch_kernel(k, dim3(grid), kThreads, smem, st, a, b, p);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -475,6 +576,11 @@ Params make_params(const b200::GemmPlan& g, int64_t M, int64_t N, int64_t K, voi
   p.R = static_cast<const __nv_bfloat16*>(R);
   p.ldr = ldr;
   p.ws = g.splits > 1 ? static_cast<float*>(ws) : nullptr;
+  p.goff = nullptr;
+  p.groups = 0;
+  p.gN = 0;
+  p.gF = 0;
+  p.gRows = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   p.err = b200::error_word(dev);
@@ -595,6 +701,55 @@ int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epi, co
   return B200_OK;
 }
 
+int grouped_gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc,
+                        const int32_t* goff, int groups, int64_t rows, int64_t N, int64_t K, int epi,
+                        cudaStream_t st) {
+  if (!A || !B || !Cp || !goff || groups <= 0 || groups > kMaxGroups || rows < 0 || N <= 0 || K <= 0)
+    return B200_ERROR_INVALID_PARAM;
+  if (epi != B200_EPI_NONE && epi != B200_EPI_SWIGLU) return B200_ERROR_INVALID_PARAM;
+  if (K % 8 || lda % 8 || ldb % 8 || ldc % 8 || lda < K || ldb < K || N % 8) return B200_ERROR_INVALID_PARAM;
+  if (epi == B200_EPI_SWIGLU && N % 16) return B200_ERROR_INVALID_PARAM;
+  if (ldc < (epi == B200_EPI_SWIGLU ? N / 2 : N)) return B200_ERROR_INVALID_PARAM;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(A) || !al(B) || !al(Cp)) return B200_ERROR_INVALID_PARAM;
+  if (rows == 0) return B200_OK;
+  if (rows > INT32_MAX / 2 || (int64_t)groups * N > INT32_MAX / 2 || K > INT32_MAX) return B200_ERROR_UNSUPPORTED;
+  // Few tokens per group (decode): weights on the 128-row MMA side, up to 64
+  // tokens of a group on the N side.  Otherwise tokens on the 128-row side.
+  const bool swap = rows <= 96LL * groups;
+  GemmPlan g;
+  g.swap = swap;
+  g.bn = swap ? 64 : (N > 128 ? 256 : 128);
+  g.kb_total = (int)((K + BK - 1) / BK);
+  g.kb_per_split = g.kb_total;
+  g.splits = 1;
+  const int feat_tile = swap ? BM : g.bn, tok_tile = swap ? g.bn : BM;
+  const int gF = (int)((N + feat_tile - 1) / feat_tile);
+  // host upper bound of the units: every group's partial token tile + the full ones
+  const int64_t max_units = ((rows + tok_tile - 1) / tok_tile + groups) * (int64_t)gF;
+  g.tiles_m = swap ? gF : 1;
+  g.tiles_n = swap ? 1 : gF;
+  Params p = make_params(g, rows, N, K, Cp, ldc, nullptr, nullptr, 0, nullptr);
+  p.goff = goff;
+  p.groups = groups;
+  p.gN = N;
+  p.gF = gF;
+  p.gRows = rows;
+  CUtensorMap tw, tt;  // weights [groups * N, K], tokens [rows, K]
+  if (!make_tmap(&tw, B, (int64_t)groups * N, K, ldb, swap ? BM : g.bn) ||
+      !make_tmap(&tt, A, rows, K, lda, swap ? g.bn : BM))
+    return B200_ERROR_UNSUPPORTED;
+  const int grid = (int)std::min<int64_t>(max_units, num_sms());
+  if (swap)
+    return epi == B200_EPI_SWIGLU ? launch_t<64, B200_EPI_SWIGLU, true, false, true>(tw, tt, p, grid, st)
+                                  : launch_t<64, B200_EPI_NONE, true, false, true>(tw, tt, p, grid, st);
+  if (g.bn == 256)
+    return epi == B200_EPI_SWIGLU ? launch_t<256, B200_EPI_SWIGLU, false, false, true>(tt, tw, p, grid, st)
+                                  : launch_t<256, B200_EPI_NONE, false, false, true>(tt, tw, p, grid, st);
+  return epi == B200_EPI_SWIGLU ? launch_t<128, B200_EPI_SWIGLU, false, false, true>(tt, tw, p, grid, st)
+                                : launch_t<128, B200_EPI_NONE, false, false, true>(tt, tw, p, grid, st);
+}
+
 int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
              int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
              cudaStream_t st) {
@@ -611,6 +766,12 @@ extern "C" int b200_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t
                               void* workspace, int64_t workspace_bytes, b200_stream_t stream) {
   return b200::gemm_run(A, lda, B, ldb, C, ldc, M, N, K, epilogue, bias, residual, ldr, workspace, workspace_bytes,
                         stream);
+}
+
+extern "C" int b200_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                                      const int32_t* group_offsets, int groups, int64_t rows, int64_t N, int64_t K,
+                                      int epilogue, b200_stream_t stream) {
+  return b200::grouped_gemm_launch(A, lda, B, ldb, C, ldc, group_offsets, groups, rows, N, K, epilogue, stream);
 }
 
 extern "C" int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int epilogue) {

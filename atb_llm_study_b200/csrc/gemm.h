@@ -30,6 +30,13 @@ int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epilogu
                   int64_t ldr, void* C, int64_t ldc, cudaStream_t stream);
 
 // gemm_launch followed by splitk_reduce when K was split (the C ABI call).
+// Grouped (per-expert) GEMM: for each group g, rows [goff[g], goff[g+1]) of A
+// (goff on the device, e.g. written by the expert permutation) times the
+// weights B[g*N:(g+1)*N, :]^T into the same rows of C.  Epilogue NONE or SWIGLU.
+int grouped_gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                        const int32_t* goff, int groups, int64_t rows, int64_t N, int64_t K, int epilogue,
+                        cudaStream_t stream);
+
 int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
              int64_t K, int epilogue, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
              cudaStream_t stream);

@@ -167,6 +167,58 @@ B200_API int b200_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t l
 /* Bytes of workspace b200_gemm_bf16 uses for split-K at this shape (0 = none). */
 B200_API int64_t b200_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int epilogue);
 
+/* ---------------------------------------------------------------- experts */
+
+/* Grouped expert GEMM: for each group g < groups (<= 256), the rows
+ * [group_offsets[g], group_offsets[g+1]) of A ([rows, K], the tokens routed to
+ * expert g) times B[g*N:(g+1)*N, :]^T into the same rows of C.  group_offsets
+ * ([groups + 1], int32) is read on the device, so it can come straight from
+ * b200_moe_permute.  Epilogue NONE or SWIGLU (gate/up rows interleaved as in
+ * b200_gemm_bf16; C then has N/2 columns).  Fills the grouped expert GEMMs the
+ * reference leaves to its MoE stubs (MoeBuilder,
+ * atb_cpp_llm/src/components/common/mlp_builder.h:73-82; MoEMlpGraph,
+ * atb_cpp_llm/src/components/moe/moe_mlp_graph.h:22-29). */
+B200_API int b200_grouped_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                                    const int32_t* group_offsets, int groups, int64_t rows, int64_t N, int64_t K,
+                                    int epilogue, b200_stream_t stream);
+
+/* Router: logits = x [T, H] (bf16, row stride ldx) . gate_weight [E, H]^T in
+ * fp32, softmax over the E (<= 128) experts, the top_k (<= 8) largest logits
+ * (ties to the lower expert index) -> topk_ids [T, top_k] (int32, in
+ * descending order) and topk_weights [T, top_k] (fp32): the chosen softmax
+ * probabilities renormalised to sum 1 when `renormalize` (Mixtral), else
+ * multiplied by `scale` (DeepSeek routed_scaling_factor).  logits [T, E] (fp32)
+ * is written when not NULL.  Fills MlpConfig.num_experts / top_k
+ * (atb_cpp_llm/include/atb_llm/layer_desc.h:59-60), which the reference never
+ * routes. */
+B200_API int b200_moe_route(const void* x, int64_t ldx, const void* gate_weight, int64_t T, int64_t H,
+                            int num_experts, int top_k, int renormalize, float scale, int32_t* topk_ids,
+                            float* topk_weights, float* logits, b200_stream_t stream);
+
+/* The selection of b200_moe_route from given fp32 logits [T, E]. */
+B200_API int b200_moe_topk(const float* logits, int64_t T, int num_experts, int top_k, int renormalize, float scale,
+                           int32_t* topk_ids, float* topk_weights, b200_stream_t stream);
+
+/* Expert permutation of the T*top_k (token, choice) entries: entry i = t*top_k
+ * + j goes to slot perm_pos[i] = expert_offsets[e] + (entries of expert e
+ * before i), so each expert's slots hold its tokens in token order
+ * (deterministic, bit-exact); perm_src[slot] = t; expert_offsets [E + 1].
+ * When x_perm is not NULL, x_perm[slot, :] = x[t, :] (bf16, H columns).
+ * Workspace: b200_moe_permute_workspace_bytes().  Out-of-range expert ids set
+ * the device error word and get perm_pos = -1. */
+B200_API int64_t b200_moe_permute_workspace_bytes(int64_t T, int top_k, int num_experts);
+B200_API int b200_moe_permute(const int32_t* topk_ids, int64_t T, int top_k, int num_experts, const void* x,
+                              int64_t ldx, int64_t H, void* x_perm, int32_t* expert_offsets, int32_t* perm_pos,
+                              int32_t* perm_src, void* workspace, int64_t workspace_bytes, b200_stream_t stream);
+
+/* out[t] = residual[t] + shared[t] + sum_j topk_weights[t, j] * y_perm[perm_pos[t*top_k + j]]
+ * (fp32, one rounding to bf16; residual / shared optional, out may alias
+ * residual); when norm_weight is not NULL also normed[t] = RMSNorm(out[t]) *
+ * norm_weight (the next layer's input norm).  H <= 8192. */
+B200_API int b200_moe_combine(const void* y_perm, const int32_t* perm_pos, const float* topk_weights, int64_t T,
+                              int top_k, int64_t H, const void* residual, const void* shared, void* out,
+                              const void* norm_weight, void* normed, float eps, b200_stream_t stream);
+
 /* -------------------------------------------------------------- attention */
 
 /* Prefill attention over packed sequences: softmax(q k^T * scale [+ causal]) v,
