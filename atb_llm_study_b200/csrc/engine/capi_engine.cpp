@@ -54,6 +54,8 @@ class ModelRegistry {
     entries_["qwen3"] = {"qwen3", 10, nullptr};
     entries_["qwen3_vl"] = {"qwen3_vl", 10, nullptr};  // text decoder (mrope) + vision tower
     entries_["qwen2"] = {"qwen2", 5, nullptr};
+    entries_["mixtral"] = {"mixtral", 10, nullptr};      // GQA + 8 routed SwiGLU experts, top-2
+    entries_["qwen3_moe"] = {"qwen3_moe", 10, nullptr};  // GQA + QK-norm + routed experts
     entries_["llama"] = {"llama", 1, dense};
   }
   mutable std::mutex mu_;

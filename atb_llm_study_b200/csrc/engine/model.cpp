@@ -48,6 +48,26 @@ Status ModelConfig::FromJson(const JsonConfig& root, ModelConfig& c) {
   c.rope_theta = t.GetFloat("rope_theta", 1e6f);
   c.tie_embeddings = root.GetBool("tie_word_embeddings", t.GetBool("tie_word_embeddings", false));
   c.qk_norm = starts_with(c.model_type, "qwen3");
+  if (t.HasKey("kv_lora_rank") && t.GetInt("kv_lora_rank") > 0) return ERROR_UNSUPPORTED;  // MLA: not this runner
+  if (t.HasKey("num_local_experts")) {  // Mixtral
+    c.experts = t.GetInt("num_local_experts");
+    c.top_k = t.GetInt("num_experts_per_tok", 2);
+    c.moe_intermediate = c.intermediate;
+    c.norm_topk = true;
+  } else if (t.HasKey("num_experts") && t.GetInt("num_experts") > 0) {  // Qwen3-MoE
+    c.experts = t.GetInt("num_experts");
+    c.top_k = t.GetInt("num_experts_per_tok", 8);
+    c.moe_intermediate = t.GetInt("moe_intermediate_size");
+    c.norm_topk = t.GetBool("norm_topk_prob", true);
+    if (t.HasKey("mlp_only_layers") && !t.GetIntArray("mlp_only_layers").empty()) return ERROR_UNSUPPORTED;
+    if (t.GetInt("decoder_sparse_step", 1) != 1) return ERROR_UNSUPPORTED;
+  }
+  if (c.experts > 0) {
+    c.routed_scale = t.GetFloat("routed_scaling_factor", 1.0f);
+    if (c.top_k <= 0 || c.top_k > 8 || c.top_k > c.experts || c.experts > 128 || c.moe_intermediate <= 0 ||
+        c.moe_intermediate % 8)
+      return c.experts > 128 ? ERROR_UNSUPPORTED : ERROR_INVALID_PARAM;
+  }
   if (t.HasKey("rope_scaling")) {
     JsonConfig rs = t.GetSubConfig("rope_scaling");
     std::vector<int> sec = rs.GetIntArray("mrope_section");
@@ -97,8 +117,27 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(final_norm_, DType::BF16, {H}));
   B200_RETURN_IF(A(wqkv_, DType::BF16, {L, QKV, H}));
   B200_RETURN_IF(A(wo_, DType::BF16, {L, H, AO}));
-  B200_RETURN_IF(A(wgu_, DType::BF16, {L, 2 * I, H}));
-  B200_RETURN_IF(A(wdown_, DType::BF16, {L, H, I}));
+  dense_idx_.assign(L, -1);
+  moe_idx_.assign(L, -1);
+  int n_dense = 0, n_moe = 0;
+  for (int l = 0; l < L; ++l) {
+    if (cfg.moe_layer(l)) moe_idx_[l] = n_moe++;
+    else dense_idx_[l] = n_dense++;
+  }
+  if (n_dense > 0) {
+    B200_RETURN_IF(A(wgu_, DType::BF16, {n_dense, 2 * I, H}));
+    B200_RETURN_IF(A(wdown_, DType::BF16, {n_dense, H, I}));
+  }
+  const int64_t E = cfg.experts, Im = cfg.moe_intermediate, Is = cfg.shared_intermediate;
+  if (n_moe > 0) {
+    B200_RETURN_IF(A(router_, DType::BF16, {n_moe, E, H}));
+    B200_RETURN_IF(A(egu_, DType::BF16, {n_moe, E, 2 * Im, H}));
+    B200_RETURN_IF(A(edown_, DType::BF16, {n_moe, E, H, Im}));
+    if (Is > 0) {
+      B200_RETURN_IF(A(sgu_, DType::BF16, {n_moe, 2 * Is, H}));
+      B200_RETURN_IF(A(sdown_, DType::BF16, {n_moe, H, Is}));
+    }
+  }
   B200_RETURN_IF(A(qnorm_, DType::BF16, {L, hd}));
   B200_RETURN_IF(A(knorm_, DType::BF16, {L, hd}));
   B200_RETURN_IF(A(iln_, DType::BF16, {L, H}));
@@ -125,7 +164,7 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(normed_, DType::BF16, {max_t_, H}));
   B200_RETURN_IF(A(qkv_, DType::BF16, {max_t_, QKV}));
   B200_RETURN_IF(A(attn_, DType::BF16, {max_t_, AO}));
-  B200_RETURN_IF(A(act_, DType::BF16, {max_t_, I}));
+  B200_RETURN_IF(A(act_, DType::BF16, {max_t_, n_dense > 0 ? I : 8}));
   B200_RETURN_IF(A(cos_, DType::FP32, {max_t_, hd}));
   B200_RETURN_IF(A(sin_, DType::FP32, {max_t_, hd}));
   B200_RETURN_IF(A(pos_, DType::INT64, {3, max_t_}));
@@ -140,12 +179,30 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(bt_batch_, DType::INT32, {opt.max_batch, max_blocks_}));
   B200_RETURN_IF(A(inject_idx_, DType::INT32, {max_t_}));
   B200_RETURN_IF(A(pooled_, DType::FP32, {H}));
+  if (n_moe > 0) {
+    const int64_t R = max_t_ * cfg.top_k;  // (token, choice) rows
+    B200_RETURN_IF(A(topk_ids_, DType::INT32, {R}));
+    B200_RETURN_IF(A(topk_w_, DType::FP32, {R}));
+    B200_RETURN_IF(A(xperm_, DType::BF16, {R, H}));
+    B200_RETURN_IF(A(eact_, DType::BF16, {R, Im}));
+    B200_RETURN_IF(A(ey_, DType::BF16, {R, H}));
+    B200_RETURN_IF(A(eoff_, DType::INT32, {E + 1}));
+    B200_RETURN_IF(A(ppos_, DType::INT32, {R}));
+    B200_RETURN_IF(A(psrc_, DType::INT32, {R}));
+    pws_bytes_ = b200_moe_permute_workspace_bytes(max_t_, cfg.top_k, cfg.experts);
+    B200_RETURN_IF(A(pws_, DType::INT32, {std::max<int64_t>(pws_bytes_ / 4, 1)}));
+    if (Is > 0) {
+      B200_RETURN_IF(A(sact_, DType::BF16, {max_t_, Is}));
+      B200_RETURN_IF(A(sout_, DType::BF16, {max_t_, H}));
+    }
+  }
 
   // split-K workspace: the largest any projection asks for at any token count
   // this engine runs (K is split only while the output tiles leave SMs idle,
   // so the need stops growing after a few thousand tokens)
   int64_t ws = 0;
-  const int64_t shapes[5][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}};
+  const int64_t Isx = std::max<int64_t>(Is, 8);
+  const int64_t shapes[7][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}, {2 * Isx, H}, {H, Isx}};
   std::vector<int64_t> ms = {1, (int64_t)opt.max_batch};
   for (int64_t m = 64; m <= std::min<int64_t>(max_t_, 65536); m += 64) ms.push_back(m);
   for (int64_t m : ms)
@@ -175,6 +232,7 @@ Status DecoderModel::InitRandomWeights(uint64_t seed, float std) {
   B200_RETURN_IF(N(wo_));
   B200_RETURN_IF(N(wgu_));
   B200_RETURN_IF(N(wdown_));
+  for (DeviceTensor* t : {&router_, &egu_, &edown_, &sgu_, &sdown_}) B200_RETURN_IF(N(*t));
   B200_RETURN_IF(O(final_norm_));
   B200_RETURN_IF(O(qnorm_));
   B200_RETURN_IF(O(knorm_));
@@ -224,15 +282,46 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
   if (leaf == "self_attn.k_norm.weight") return put(knorm_, (int64_t)l * hd, hd);
   if (leaf == "input_layernorm.weight") return put(iln_, (int64_t)l * H, H);
   if (leaf == "post_attention_layernorm.weight") return put(pln_, (int64_t)l * H, H);
-  if (leaf == "mlp.down_proj.weight") return put(wdown_, (int64_t)l * H * I, H * I);
-  if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight") {
-    // rows 2j / 2j+1 of the fused matrix hold gate[j] / up[j] (SwiGLU epilogue layout)
-    if (numel != I * H) return ERROR_INVALID_PARAM;
-    uint16_t* dst = static_cast<uint16_t*>(wgu_.data) + (int64_t)l * 2 * I * H + (leaf[4] == 'u' ? H : 0);
+  // rows 2j / 2j+1 of a fused gate/up matrix hold gate[j] / up[j] (SwiGLU epilogue layout)
+  auto put_interleaved = [&](const DeviceTensor& t, int64_t elem_off, int64_t inter, bool up) -> Status {
+    if (numel != inter * H) return ERROR_INVALID_PARAM;
+    uint16_t* dst = static_cast<uint16_t*>(t.data) + elem_off + (up ? H : 0);
     B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(dst, (size_t)2 * H * 2, b16.data(), (size_t)H * 2, (size_t)H * 2,
-                                              (size_t)I, cudaMemcpyHostToDevice, st)));
+                                              (size_t)inter, cudaMemcpyHostToDevice, st)));
     return ctx_->Synchronize();
+  };
+  const int di = dense_idx_[l], mi = moe_idx_[l];
+  if (di >= 0) {
+    if (leaf == "mlp.down_proj.weight") return put(wdown_, (int64_t)di * H * I, H * I);
+    if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight")
+      return put_interleaved(wgu_, (int64_t)di * 2 * I * H, I, leaf[4] == 'u');
+    return ERROR_WEIGHT_LOAD;
   }
+  // MoE layer: Mixtral "block_sparse_moe.{gate, experts.E.w1/w3/w2}", Qwen3-MoE /
+  // DeepSeek "mlp.{gate, experts.E.gate_proj/up_proj/down_proj, shared_experts.*}"
+  const int64_t E = cfg_.experts, Im = cfg_.moe_intermediate, Is = cfg_.shared_intermediate;
+  std::string m;
+  if (starts_with(leaf, "block_sparse_moe.")) m = leaf.substr(17);
+  else if (starts_with(leaf, "mlp.")) m = leaf.substr(4);
+  else return ERROR_WEIGHT_LOAD;
+  if (m == "gate.weight") return put(router_, (int64_t)mi * E * H, E * H);
+  if (starts_with(m, "shared_experts.") && Is > 0) {
+    const std::string s = m.substr(15);
+    if (s == "down_proj.weight") return put(sdown_, (int64_t)mi * H * Is, H * Is);
+    if (s == "gate_proj.weight" || s == "up_proj.weight")
+      return put_interleaved(sgu_, (int64_t)mi * 2 * Is * H, Is, s[0] == 'u');
+    return ERROR_WEIGHT_LOAD;
+  }
+  if (!starts_with(m, "experts.")) return ERROR_WEIGHT_LOAD;
+  const size_t d2 = m.find('.', 8);
+  if (d2 == std::string::npos) return ERROR_WEIGHT_LOAD;
+  const int e = std::atoi(m.substr(8, d2 - 8).c_str());
+  if (e < 0 || e >= E) return ERROR_WEIGHT_LOAD;
+  const std::string w = m.substr(d2 + 1);
+  const int64_t ge = (int64_t)mi * E + e;  // expert slot in the MoE stacks
+  if (w == "w2.weight" || w == "down_proj.weight") return put(edown_, ge * H * Im, H * Im);
+  if (w == "w1.weight" || w == "gate_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, false);
+  if (w == "w3.weight" || w == "up_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, true);
   return ERROR_WEIGHT_LOAD;
 }
 
@@ -317,16 +406,21 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     else
       B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(pln_, (int64_t)l * H), normed_.data, nullptr, T, H, H,
                                   cfg_.eps, st));
+    const void* next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
+    if (cfg_.moe_layer(l)) {  // routed experts; the combine adds the residual and applies the next norm
+      B200_RETURN_IF(MoeBlock(l, T, next_norm));
+      continue;
+    }
     // MLP block
-    B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, (int64_t)l * 2 * I * H), H, act_.data, I, 2 * I, H,
-                        B200_EPI_SWIGLU, nullptr, 0, &s_gu));
+    const int64_t dl = dense_idx_[l];
+    B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, dl * 2 * I * H), H, act_.data, I, 2 * I, H, B200_EPI_SWIGLU,
+                        nullptr, 0, &s_gu));
     if (s_gu > 1) {
       ++launches_;
       B200_RETURN_IF(b200::splitk_reduce(ws, s_gu, T, 2 * I, B200_EPI_SWIGLU, nullptr, nullptr, 0, act_.data, I, st));
     }
-    B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, (int64_t)l * H * I), I, hidden_.data, H, H, I, B200_EPI_RESIDUAL,
+    B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, dl * H * I), I, hidden_.data, H, H, I, B200_EPI_RESIDUAL,
                         hidden_.data, H, &s_d));
-    const void* next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
     if (l < (int)inject_feats_.size() && inject_n_ > 0) {
       // deepstack: hidden[rows] += feature[l] between this layer and the next norm
       if (s_d > 1) {
@@ -355,6 +449,49 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     }
   }
   return STATUS_OK;
+}
+
+// Routed-expert MLP of layer l on normed_ (the post-attention norm of
+// hidden_): router -> permutation -> grouped gate/up (SwiGLU) -> grouped down
+// -> weighted combine + shared expert + residual into hidden_, with the next
+// layer's input norm fused into the combine.
+Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, E = cfg_.experts, Im = cfg_.moe_intermediate, Is = cfg_.shared_intermediate;
+  const int k = cfg_.top_k;
+  const int64_t mi = moe_idx_[l], R = T * k;
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  launches_ += 1 + 4 + 2 + 1;  // route, permutation (count, scan, scatter, gather), 2 grouped GEMMs, combine
+  B200_RETURN_IF(b200_moe_route(normed_.data, H, bf(router_, mi * E * H), T, H, (int)E, k, cfg_.norm_topk ? 1 : 0,
+                                cfg_.routed_scale, topk_ids_.as<int32_t>(), topk_w_.as<float>(), nullptr, st));
+  B200_RETURN_IF(b200_moe_permute(topk_ids_.as<int32_t>(), T, k, (int)E, normed_.data, H, H, xperm_.data,
+                                  eoff_.as<int32_t>(), ppos_.as<int32_t>(), psrc_.as<int32_t>(), pws_.data,
+                                  pws_bytes_, st));
+  B200_RETURN_IF(b200::grouped_gemm_launch(xperm_.data, H, bf(egu_, mi * E * 2 * Im * H), H, eact_.data, Im,
+                                           eoff_.as<int32_t>(), (int)E, R, 2 * Im, H, B200_EPI_SWIGLU, st));
+  B200_RETURN_IF(b200::grouped_gemm_launch(eact_.data, Im, bf(edown_, mi * E * H * Im), Im, ey_.data, H,
+                                           eoff_.as<int32_t>(), (int)E, R, H, Im, B200_EPI_NONE, st));
+  const void* shared = nullptr;
+  if (Is > 0) {
+    float* ws = gemm_ws_.as<float>();
+    int s1 = 1, s2 = 1;
+    launches_ += 2;
+    B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(sgu_, mi * 2 * Is * H), H, sact_.data, Is, T, 2 * Is, H,
+                                     B200_EPI_SWIGLU, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s1));
+    if (s1 > 1) {
+      ++launches_;
+      B200_RETURN_IF(b200::splitk_reduce(ws, s1, T, 2 * Is, B200_EPI_SWIGLU, nullptr, nullptr, 0, sact_.data, Is, st));
+    }
+    B200_RETURN_IF(b200::gemm_launch(sact_.data, Is, bf(sdown_, mi * H * Is), Is, sout_.data, H, T, H, Is,
+                                     B200_EPI_NONE, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s2));
+    if (s2 > 1) {
+      ++launches_;
+      B200_RETURN_IF(b200::splitk_reduce(ws, s2, T, H, B200_EPI_NONE, nullptr, nullptr, 0, sout_.data, H, st));
+    }
+    shared = sout_.data;
+  }
+  return (Status)b200_moe_combine(ey_.data, ppos_.as<int32_t>(), topk_w_.as<float>(), T, k, H, hidden_.data, shared,
+                                  hidden_.data, next_norm, next_norm ? normed_.data : nullptr, cfg_.eps, st);
 }
 
 Status DecoderModel::Head(int64_t rows, bool gather, int64_t* next_tokens, bool next_on_device, void* logits) {

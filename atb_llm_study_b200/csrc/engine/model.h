@@ -11,6 +11,7 @@
 // allocation); the decode step is captured in a CUDA graph per batch size.
 #pragma once
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <string>
@@ -30,10 +31,20 @@ struct ModelConfig {
   bool qk_norm = true, tie_embeddings = false;
   bool mrope = false;
   int mrope_section[3] = {0, 0, 0};
+  // Mixture of experts (Mixtral "mixtral", Qwen3-MoE "qwen3_moe"): layers
+  // l >= first_dense route each token to top_k of `experts` SwiGLU experts of
+  // width moe_intermediate (+ an always-on shared expert of width
+  // shared_intermediate); experts == 0 is a dense model.
+  int experts = 0, top_k = 0, moe_intermediate = 0, shared_intermediate = 0, first_dense = 0;
+  bool norm_topk = true;     // renormalise the chosen weights (else times routed_scale)
+  float routed_scale = 1.0f;
 
-  // Reads a HF config.json (Qwen3 "qwen3", or the "text_config" of "qwen3_vl").
+  // Reads a HF config.json (Qwen3 "qwen3", the "text_config" of "qwen3_vl",
+  // Mixtral "mixtral", Qwen3-MoE "qwen3_moe").
   static Status FromJson(const JsonConfig& cfg, ModelConfig& out);
   int qkv_dim() const { return (heads + 2 * kv_heads) * head_dim; }
+  bool moe_layer(int l) const { return experts > 0 && l >= first_dense; }
+  int dense_layers() const { return experts > 0 ? std::min(first_dense, layers) : layers; }
 };
 
 struct EngineOptions {
@@ -118,9 +129,18 @@ class DecoderModel {
   std::vector<const void*> inject_feats_;
   int64_t inject_n_ = 0;
 
-  // weights (all layers stacked)
+  Status MoeBlock(int l, int64_t T, const void* next_norm);
+
+  // weights (all layers stacked; dense MLPs over the dense layers only)
   DeviceTensor embed_, lm_head_, final_norm_;
   DeviceTensor wqkv_, wo_, wgu_, wdown_, qnorm_, knorm_, iln_, pln_;
+  // MoE layers: router [Lm, E, H], experts gate/up [Lm, E, 2*Im, H] (rows
+  // interleaved gate/up), down [Lm, E, H, Im], shared expert gate/up [Lm, 2*Is, H], down [Lm, H, Is]
+  DeviceTensor router_, egu_, edown_, sgu_, sdown_;
+  std::vector<int> dense_idx_, moe_idx_;  // per layer: index into the dense / MoE stacks (-1 = other kind)
+  // MoE activations
+  DeviceTensor topk_ids_, topk_w_, xperm_, eact_, ey_, eoff_, ppos_, psrc_, pws_, sact_, sout_;
+  int64_t pws_bytes_ = 0;
   // KV cache [layers][2][num_blocks][kv_heads][block_size][head_dim]
   DeviceTensor kv_;
   DeviceTensor block_tables_, ctx_lens_;

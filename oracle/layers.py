@@ -114,7 +114,7 @@ def swiglu_mlp(x, gate_w, up_w, down_w):
     return linear(silu(linear(x, gate_w)) * linear(x, up_w), down_w)
 
 
-def decoder_layer(x, w, cos, sin, nh, kvh, hd, eps=1e-6, mask=None, causal=False):
+def decoder_layer(x, w, cos, sin, nh, kvh, hd, eps=1e-6, mask=None, causal=False, mlp=None):
     """One pre-norm decoder layer.
 
     ``h1 = x + O(attn(rope(qknorm(QKV(rmsnorm(x))))))``;
@@ -126,7 +126,8 @@ def decoder_layer(x, w, cos, sin, nh, kvh, hd, eps=1e-6, mask=None, causal=False
     ``GqaAttentionBuilder::Build``
     (atb_cpp_llm/src/components/common/gqa_attention_builder.cpp:13-185).
     ``w`` holds ``q_w k_w v_w o_w qn_w kn_w gate_w up_w down_w iln_w pln_w``
-    (``qn_w``/``kn_w`` may be None to skip the per-head norm).
+    (``qn_w``/``kn_w`` may be None to skip the per-head norm); ``mlp``, when
+    given, replaces the SwiGLU MLP (a mixture-of-experts block).
     """
     S = x.shape[0]
     normed = rms_norm(x, w["iln_w"], eps)
@@ -141,4 +142,6 @@ def decoder_layer(x, w, cos, sin, nh, kvh, hd, eps=1e-6, mask=None, causal=False
     a = sdpa_gqa(q, k, v, nh, kvh, mask=mask, causal=causal)
     h1 = x + linear(a.reshape(S, nh * hd), w["o_w"])
     n2 = rms_norm(h1, w["pln_w"], eps)
+    if mlp is not None:
+        return h1 + mlp(n2)
     return h1 + swiglu_mlp(n2, w["gate_w"], w["up_w"], w["down_w"])

@@ -20,13 +20,23 @@ def forward_last_logits(ids, w, cfg):
 
     ``w``: dict with ``embed [V,H]``, ``lm_head [V,H]``, ``norm [H]`` and a
     list ``layers`` of per-layer dicts (q_w k_w v_w o_w qn_w kn_w gate_w up_w
-    down_w iln_w pln_w).  ``cfg``: heads, kv_heads, head_dim, eps, theta.
+    down_w iln_w pln_w; a mixture-of-experts layer has ``router``, ``experts``
+    and optionally ``shared`` instead of the MLP weights).  ``cfg``: heads,
+    kv_heads, head_dim, eps, theta (+ top_k, renorm, scale for MoE layers).
     """
+    from .moe import moe_ffn
+
     ids = np.asarray(ids, np.int64)
     x = w["embed"][ids].astype(np.float32)
     cos, sin = rope1d_cos_sin(np.arange(len(ids)), cfg["head_dim"], cfg["theta"])
     for lw in w["layers"]:
-        x = decoder_layer(x, lw, cos, sin, cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"], causal=True)
+        mlp = None
+        if "experts" in lw:
+            def mlp(n2, lw=lw):
+                return moe_ffn(n2, lw["router"], lw["experts"], cfg["top_k"], cfg.get("renorm", True),
+                               cfg.get("scale", 1.0), lw.get("shared"))[0]
+        x = decoder_layer(x, lw, cos, sin, cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"], causal=True,
+                          mlp=mlp)
     h = rms_norm(x[-1:], w["norm"], cfg["eps"])
     return linear(h, w["lm_head"])[0]
 
