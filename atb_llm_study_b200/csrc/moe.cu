@@ -21,49 +21,78 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
 constexpr int kPermChunk = 256;  // entries per permutation block (one warp)
 
-// One warp per token.  Expert e's logit lives in lane e % 32, slot e / 32.
-template <int EP>
-__global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ wg,
-                                 const float* __restrict__ logits_in, int64_t T, int64_t H, int E, int k, int renorm,
-                                 float scale, int32_t* __restrict__ ids, float* __restrict__ wts,
-                                 float* __restrict__ logits_out) {
+// Router: a CTA of 256 threads per TPB tokens.  Each thread accumulates the
+// dot products of its H/8-chunks with every expert row (the gate rows are
+// read once per CTA for all its tokens), the warps' partial sums meet in
+// shared memory, and warp tt finishes token tt: softmax and top-k, with
+// expert e's logit in lane e % 32, slot e / 32.
+constexpr int kRouteThreads = 256;
+
+template <int EA, int TPB>
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ wg,
+    const float* __restrict__ logits_in, int64_t T, int64_t H, int E, int k, int renorm, float scale,
+    int32_t* __restrict__ ids, float* __restrict__ wts, float* __restrict__ logits_out) {
   pdl_trigger();
   pdl_wait();
-  constexpr int PER = EP / 32;
-  const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  float lg[PER];
-  if (logits_in) {
+  constexpr int PER = (EA + 31) / 32, NW = kRouteThreads / 32;
+  __shared__ float red[NW][TPB][EA];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = (int64_t)blockIdx.x * TPB;
+  if (!logits_in) {
+    float acc[TPB][EA];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane + 32 * i;
-      lg[i] = e < E ? logits_in[t * E + e] : -INFINITY;
-    }
-  } else {
-    float acc[EP];
+    for (int tt = 0; tt < TPB; ++tt)
 #pragma unroll
-    for (int e = 0; e < EP; ++e) acc[e] = 0.f;
-    const __nv_bfloat16* xr = x + t * ldx;
-    for (int64_t c = lane; c < H / 8; c += 32) {
-      float xv[8];
-      unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), xv);
+      for (int e = 0; e < EA; ++e) acc[tt][e] = 0.f;
+    for (int64_t c = threadIdx.x; c < H / 8; c += kRouteThreads) {
+      float xv[TPB][8];
 #pragma unroll
-      for (int e = 0; e < EP; ++e) {
+      for (int tt = 0; tt < TPB; ++tt) {
+        if (t0 + tt < T) {
+          unpack8(*reinterpret_cast<const uint4*>(x + (t0 + tt) * ldx + c * 8), xv[tt]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[tt][j] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < EA; ++e) {
         if (e < E) {
           float w[8];
           unpack8(*reinterpret_cast<const uint4*>(wg + (int64_t)e * H + c * 8), w);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[e] = fmaf(xv[j], w[j], acc[e]);
+          for (int tt = 0; tt < TPB; ++tt)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[tt][e] = fmaf(xv[tt][j], w[j], acc[tt][e]);
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) lg[i] = -INFINITY;
+    for (int tt = 0; tt < TPB; ++tt)
 #pragma unroll
-    for (int e = 0; e < EP; ++e) {
-      const float s = warp_sum(acc[e]);
-      if (e < E && (e & 31) == lane) lg[e >> 5] = s;
+      for (int e = 0; e < EA; ++e) {
+        const float s = warp_sum(acc[tt][e]);
+        if (lane == 0) red[warp][tt][e] = s;
+      }
+    __syncthreads();
+  }
+  if (warp >= TPB) return;
+  const int64_t t = t0 + warp;
+  if (t >= T) return;
+  float lg[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    if (e >= E) {
+      lg[i] = -INFINITY;
+    } else if (logits_in) {
+      lg[i] = logits_in[t * E + e];
+    } else {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s += red[w][warp][e];
+      lg[i] = s;
     }
   }
   if (logits_out) {
@@ -321,13 +350,22 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int route_launch(const void* x, int64_t ldx, const void* wg, const float* logits_in, int64_t T, int64_t H, int E,
                  int k, int renorm, float scale, int32_t* ids, float* wts, float* logits_out, cudaStream_t st) {
-  const unsigned grid = (unsigned)((T * 32 + 255) / 256);
   auto xb = static_cast<const __nv_bfloat16*>(x);
   auto wb = static_cast<const __nv_bfloat16*>(wg);
-  if (E <= 32) launch_kernel(moe_route_kernel<32>, dim3(grid), 256, 0, st, xb, ldx, wb, logits_in, T, H, E, k, renorm, scale, ids, wts, logits_out);
-  else if (E <= 64) launch_kernel(moe_route_kernel<64>, dim3(grid), 256, 0, st, xb, ldx, wb, logits_in, T, H, E, k, renorm, scale, ids, wts, logits_out);
-  else if (E <= 128) launch_kernel(moe_route_kernel<128>, dim3(grid), 256, 0, st, xb, ldx, wb, logits_in, T, H, E, k, renorm, scale, ids, wts, logits_out);
+  // Accumulators per thread: experts (rounded up) x tokens per CTA.  Many
+  // tokens: several per CTA, so the gate rows are read once for all of them;
+  // few (decode): one per CTA, for more CTAs in flight.
+  const bool many = T >= 1024;
+#define B200_ROUTE(EA, TPB)                                                                                       \
+  launch_kernel(moe_route_kernel<EA, TPB>, dim3((unsigned)((T + TPB - 1) / TPB)), kRouteThreads, 0, st, xb, ldx, \
+                wb, logits_in, T, H, E, k, renorm, scale, ids, wts, logits_out)
+  if (E <= 8) many ? B200_ROUTE(8, 4) : B200_ROUTE(8, 1);
+  else if (E <= 16) many ? B200_ROUTE(16, 4) : B200_ROUTE(16, 1);
+  else if (E <= 32) many ? B200_ROUTE(32, 2) : B200_ROUTE(32, 1);
+  else if (E <= 64) many ? B200_ROUTE(64, 2) : B200_ROUTE(64, 1);
+  else if (E <= 128) B200_ROUTE(128, 1);
   else return B200_ERROR_UNSUPPORTED;
+#undef B200_ROUTE
   B200_CHECK_LAUNCH();
   return B200_OK;
 }

@@ -350,6 +350,111 @@ def bench_qwen3vl(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
+MIXTRAL_8X7B = dict(model_type="mixtral", hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
+                    num_key_value_heads=8, intermediate_size=14336, num_local_experts=8, num_experts_per_tok=2,
+                    vocab_size=32000, rms_norm_eps=1e-5, rope_theta=1e6, tie_word_embeddings=False)
+MX_PREFILL_SEQS, MX_PREFILL_LEN, MX_BATCH, MX_CTX = 8, 1024, 32, 4096
+# per layer: attention 4096*(4096+2*1024+4096) + 8 experts * 3 * 4096*14336 (+ router 8*4096)
+MX_LAYER_PARAMS = 4096 * (4096 + 2 * 1024 + 4096) + 8 * 3 * 4096 * 14336 + 8 * 4096
+MX_ACTIVE_LAYER_PARAMS = 4096 * (4096 + 2 * 1024 + 4096) + 2 * 3 * 4096 * 14336 + 8 * 4096
+# one decode step reads every expert (P(an expert idle over 64 choices) ~ 1e-4), lm_head and the KV of 32 x 4096 tokens
+MX_DECODE_BYTES = (32 * MX_LAYER_PARAMS + 32000 * 4096) * 2 + MX_BATCH * MX_CTX * 32 * 2 * 8 * 128 * 2
+MX_PREFILL_FLOP = (2 * 32 * MX_ACTIVE_LAYER_PARAMS * MX_PREFILL_SEQS * MX_PREFILL_LEN
+                   + 32 * MX_PREFILL_SEQS * 2 * MX_PREFILL_LEN ** 2 * 4096 + 2 * 32000 * 4096 * MX_PREFILL_SEQS)
+
+
+def bench_mixtral(L, torch, dev, steps, warm, stream_of):
+    """Mixtral-8x7B on one GPU (93 GB of bf16 weights): prefill 8 x 1024 per
+    step; decode batch 32 at context 4096 (paged KV, block 128)."""
+    import numpy as np
+
+    max_ctx = MX_CTX + 2 * (warm + steps) + 16  # device-fed then host-fed decode steps
+    cfg = EngineConfig(None, json.dumps(MIXTRAL_8X7B).encode(), dev.index, MX_BATCH, max_ctx,
+                       MX_PREFILL_SEQS * MX_PREFILL_LEN, BLOCK, 77, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create mixtral")
+    est = stream_of(eng)
+    try:
+        V = MIXTRAL_8X7B["vocab_size"]
+        rng = np.random.default_rng(7)
+        T = MX_PREFILL_SEQS * MX_PREFILL_LEN
+        ids_pf = torch.from_numpy(rng.integers(0, V, T).astype(np.int64)).to(dev)
+        lens_pf = np.full(MX_PREFILL_SEQS, MX_PREFILL_LEN, np.int32)
+        nxt = torch.empty(MX_BATCH, dtype=torch.int64, device=dev)
+
+        def timed(fn, n):
+            for i in range(warm):
+                fn(i)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(est)
+            for i in range(n):
+                fn(i)
+            e1.record(est)
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1) / n
+
+        def prefill(i):
+            slots = np.arange(MX_PREFILL_SEQS, dtype=np.int32) + (i % (MX_BATCH // MX_PREFILL_SEQS)) * MX_PREFILL_SEQS
+            check(L.b200_engine_prefill(eng, ids_pf.data_ptr(), 1, lens_pf.ctypes.data, slots.ctypes.data,
+                                        MX_PREFILL_SEQS, None, nxt.data_ptr(), 1, None), "prefill")
+
+        pf_ms = timed(prefill, max(3, min(steps, 5)))
+        # fill every slot to context 4096 (2 distinct random sequences of 4096 per call)
+        check(L.b200_engine_reset(eng), "reset")
+        lens_ctx = np.full(2, MX_CTX, np.int32)
+        for g in range(MX_BATCH // 2):
+            ids_ctx = torch.from_numpy(rng.integers(0, V, 2 * MX_CTX).astype(np.int64)).to(dev)
+            slots = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, ids_ctx.data_ptr(), 1, lens_ctx.ctypes.data, slots.ctypes.data, 2,
+                                        None, nxt[2 * g:].data_ptr(), 1, None), "prefill ctx")
+        slots_all = np.arange(MX_BATCH, dtype=np.int32)
+        # Each step feeds fresh random tokens (teacher forcing) so that routing
+        # stays near-uniform across the experts, as with real traffic; greedy
+        # feedback from random weights can collapse onto a few tokens.
+        feed_host = rng.integers(0, V, (warm + steps + 1, MX_BATCH)).astype(np.int64)
+        feed = torch.from_numpy(feed_host).to(dev)
+        out_d = torch.empty(MX_BATCH, dtype=torch.int64, device=dev)
+        counter = {"i": 0}
+
+        def decode(_):
+            i = counter["i"] % len(feed_host)
+            counter["i"] += 1
+            check(L.b200_engine_decode(eng, feed[i].data_ptr(), 1, slots_all.ctypes.data, MX_BATCH,
+                                       out_d.data_ptr(), 1, None), "decode")
+
+        dec_ms = timed(decode, steps)
+        host_next = np.zeros(MX_BATCH, np.int64)
+
+        def decode_host(_):
+            i = counter["i"] % len(feed_host)
+            counter["i"] += 1
+            check(L.b200_engine_decode(eng, feed_host[i].ctypes.data, 0, slots_all.ctypes.data, MX_BATCH,
+                                       host_next.ctypes.data, 0, None), "decode")
+
+        e2e_ms = timed(decode_host, steps)
+        v = ctypes.c_int64()
+        check(L.b200_engine_query(eng, 2, ctypes.byref(v)), "query")
+        hbm, tf_burst, tf_sus, src = peaks()
+        return {
+            "workload": "Mixtral-8x7B (46.7 B params, 8 experts top-2) on one GPU: decode batch 32 at context 4096, "
+                        "prefill 8x1024",
+            "decode_tok_s": MX_BATCH / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+            "decode_e2e_tok_s": MX_BATCH / (e2e_ms / 1e3),
+            "decode_roofline": {"bound": "hbm", "bytes_per_step": MX_DECODE_BYTES,
+                                "achieved": MX_DECODE_BYTES / (dec_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                                "frac": MX_DECODE_BYTES / (dec_ms / 1e3) / 1e9 / hbm, "peak_source": f"{src} copy"},
+            "prefill_tok_s": MX_PREFILL_SEQS * MX_PREFILL_LEN / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
+            "prefill_roofline": {"bound": "tensor", "flop_per_step": MX_PREFILL_FLOP,
+                                 "achieved": MX_PREFILL_FLOP / (pf_ms / 1e3) / 1e12, "peak": tf_sus,
+                                 "unit": "TFLOP/s", "frac": MX_PREFILL_FLOP / (pf_ms / 1e3) / 1e12 / tf_sus,
+                                 "peak_source": f"{src} bf16 sustained"},
+            "decode_launches_per_step": v.value,
+        }
+    finally:
+        L.b200_engine_destroy(eng)
+
+
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -481,6 +586,7 @@ def run_b200(args, rank, world, local_rank):
         return torch.cuda.ExternalStream(s.value, device=dev)
 
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+    mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
 
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
     pf_tok_s = world * T * steps / (pf_ms / 1e3)
@@ -528,6 +634,8 @@ def run_b200(args, rank, world, local_rank):
     }
     if vl:
         result["qwen3vl_embedding"] = vl
+    if mx:
+        result["mixtral_8x7b"] = mx
     if dist:
         dist.barrier()
     if rank == 0:
@@ -578,6 +686,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-vl", action="store_true", help="skip the Qwen3-VL-2B embedding section")
     ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
+    ap.add_argument("--no-mixtral", action="store_true", help="skip the Mixtral-8x7B section")
+    ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm"],
                     help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
@@ -600,7 +710,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.vl_only:
+    if args.vl_only or args.mixtral_only:
         import torch
 
         from atb_llm_study_b200 import capi
@@ -614,7 +724,8 @@ def main():
             check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
             return torch.cuda.ExternalStream(s.value, device=dev)
 
-        print(json.dumps(bench_qwen3vl(L, torch, dev, args.steps, args.warmup, stream_of)), flush=True)
+        fn = bench_qwen3vl if args.vl_only else bench_mixtral
+        print(json.dumps(fn(L, torch, dev, args.steps, args.warmup, stream_of)), flush=True)
         return
     run_b200(args, rank, world, local_rank)
 
