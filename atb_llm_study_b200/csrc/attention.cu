@@ -38,12 +38,12 @@ __device__ __forceinline__ int swz(int r, int c) {
 // ===========================================================================
 // Prefill
 // ===========================================================================
-template <int HD>
+template <int HDK, int HDV>
 struct PrefillCfg {
   static constexpr int BM = 64, BN = 64;
-  static constexpr int CH = HD / 8;                 // 16-byte chunks per row
-  static constexpr int TILE_BYTES = BN * HD * 2;    // one K or V tile
-  static constexpr int SMEM = BM * HD * 2 + 4 * TILE_BYTES;  // Q + 2 stages x (K, V)
+  static constexpr int CHK = HDK / 8, CHV = HDV / 8;  // 16-byte chunks per Q/K row, per V row
+  static constexpr int TILE_K = BN * HDK * 2, TILE_V = BN * HDV * 2;
+  static constexpr int SMEM = BM * HDK * 2 + 2 * TILE_K + 2 * TILE_V;  // Q + 2 stages x (K, V)
 };
 
 template <int HD>
@@ -60,19 +60,23 @@ __device__ __forceinline__ void load_tile_async(uint8_t* s, const __nv_bfloat16*
   }
 }
 
-template <int HD, bool CAUSAL>
-__global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16* __restrict__ q, int64_t q_stride,
-                                                            const __nv_bfloat16* __restrict__ k,
-                                                            const __nv_bfloat16* __restrict__ v, int64_t kv_stride,
-                                                            __nv_bfloat16* __restrict__ out, int64_t out_stride,
-                                                            const int32_t* __restrict__ cu_seqlens, int nq, int nkv,
-                                                            float scale_log2, int m_blocks) {
-  using Cf = PrefillCfg<HD>;
-  constexpr int CH = Cf::CH;
+// Flash attention over packed variable-length sequences (one CTA = 64 query
+// rows of one head of one sequence, 4 warps x 16 rows).  Q/K heads are HDK
+// wide and V/out heads HDV wide (they differ for MLA's decompressed heads:
+// 128 + 64 rope dims against 128 value dims); every operand has its own row
+// and head stride.
+template <int HDK, int HDV, bool CAUSAL>
+__global__ void __launch_bounds__(128) flash_prefill_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t q_stride, int64_t q_hs, const __nv_bfloat16* __restrict__ k,
+    int64_t k_stride, int64_t k_hs, const __nv_bfloat16* __restrict__ v, int64_t v_stride, int64_t v_hs,
+    __nv_bfloat16* __restrict__ out, int64_t out_stride, int64_t o_hs, const int32_t* __restrict__ cu_seqlens, int nq,
+    int nkv, float scale_log2, int m_blocks) {
+  using Cf = PrefillCfg<HDK, HDV>;
+  constexpr int CHK = Cf::CHK, CHV = Cf::CHV;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sQ = smem;
-  uint8_t* sK[2] = {smem + Cf::BM * HD * 2, smem + Cf::BM * HD * 2 + Cf::TILE_BYTES};
-  uint8_t* sV[2] = {smem + Cf::BM * HD * 2 + 2 * Cf::TILE_BYTES, smem + Cf::BM * HD * 2 + 3 * Cf::TILE_BYTES};
+  uint8_t* sK[2] = {smem + Cf::BM * HDK * 2, smem + Cf::BM * HDK * 2 + Cf::TILE_K};
+  uint8_t* sV[2] = {smem + Cf::BM * HDK * 2 + 2 * Cf::TILE_K, smem + Cf::BM * HDK * 2 + 2 * Cf::TILE_K + Cf::TILE_V};
 
   pdl_trigger();
   pdl_wait();
@@ -84,32 +88,32 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
 
-  const __nv_bfloat16* qb = q + (int64_t)s0 * q_stride + h * HD;
-  const __nv_bfloat16* kb = k + (int64_t)s0 * kv_stride + kh * HD;
-  const __nv_bfloat16* vb = v + (int64_t)s0 * kv_stride + kh * HD;
+  const __nv_bfloat16* qb = q + (int64_t)s0 * q_stride + h * q_hs;
+  const __nv_bfloat16* kb = k + (int64_t)s0 * k_stride + kh * k_hs;
+  const __nv_bfloat16* vb = v + (int64_t)s0 * v_stride + kh * v_hs;
   const int q0 = mb * Cf::BM;
-  load_tile_async<HD>(sQ, qb, q_stride, q0, min(Cf::BM, len - q0));
+  load_tile_async<HDK>(sQ, qb, q_stride, q0, min(Cf::BM, len - q0));
   cp_async_commit();
 
   const int n_blocks = CAUSAL ? min((len + Cf::BN - 1) / Cf::BN, mb + 1) : (len + Cf::BN - 1) / Cf::BN;
-  load_tile_async<HD>(sK[0], kb, kv_stride, 0, min(Cf::BN, len));
-  load_tile_async<HD>(sV[0], vb, kv_stride, 0, min(Cf::BN, len));
+  load_tile_async<HDK>(sK[0], kb, k_stride, 0, min(Cf::BN, len));
+  load_tile_async<HDV>(sV[0], vb, v_stride, 0, min(Cf::BN, len));
   cp_async_commit();
 
   cp_async_wait<1>();
   __syncthreads();
-  uint32_t qf[HD / 16][4];
+  uint32_t qf[HDK / 16][4];
 #pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
+  for (int kk = 0; kk < HDK / 16; ++kk) {
     const int mat = lane >> 3;
     const int r = warp * 16 + (lane & 7) + ((mat & 1) ? 8 : 0);
     const int c = kk * 2 + (mat >> 1);
-    ldmatrix_x4(qf[kk], smem_u32(sQ + r * HD * 2 + swz<CH>(r, c) * 16));
+    ldmatrix_x4(qf[kk], smem_u32(sQ + r * HDK * 2 + swz<CHK>(r, c) * 16));
   }
 
-  float o[HD / 8][4];
+  float o[HDV / 8][4];
 #pragma unroll
-  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < HDV / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   const int qi0 = q0 + warp * 16 + g;  // query rows of this thread: qi0, qi0 + 8
 
@@ -117,8 +121,8 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
     const int st = nb & 1;
     if (nb + 1 < n_blocks) {
       const int r0 = (nb + 1) * Cf::BN;
-      load_tile_async<HD>(sK[st ^ 1], kb, kv_stride, r0, min(Cf::BN, len - r0));
-      load_tile_async<HD>(sV[st ^ 1], vb, kv_stride, r0, min(Cf::BN, len - r0));
+      load_tile_async<HDK>(sK[st ^ 1], kb, k_stride, r0, min(Cf::BN, len - r0));
+      load_tile_async<HDV>(sV[st ^ 1], vb, v_stride, r0, min(Cf::BN, len - r0));
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -128,14 +132,14 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < HD / 16; ++kk) {
+    for (int kk = 0; kk < HDK / 16; ++kk) {
 #pragma unroll
       for (int jp = 0; jp < 4; ++jp) {
         const int mat = lane >> 3;
         const int r = (2 * jp + (mat >> 1)) * 8 + (lane & 7);
         const int c = kk * 2 + (mat & 1);
         uint32_t bf[4];
-        ldmatrix_x4(bf, smem_u32(sK[st] + r * HD * 2 + swz<CH>(r, c) * 16));
+        ldmatrix_x4(bf, smem_u32(sK[st] + r * HDK * 2 + swz<CHK>(r, c) * 16));
         mma_bf16_16816(s[2 * jp], qf[kk], bf);
         mma_bf16_16816(s[2 * jp + 1], qf[kk], bf + 2);
       }
@@ -181,7 +185,7 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
+    for (int j = 0; j < HDV / 8; ++j) {
       o[j][0] *= corr[0];
       o[j][1] *= corr[0];
       o[j][2] *= corr[1];
@@ -196,12 +200,12 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
       pa[2] = pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
       pa[3] = pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-      for (int jp = 0; jp < HD / 16; ++jp) {
+      for (int jp = 0; jp < HDV / 16; ++jp) {
         const int mat = lane >> 3;
         const int r = kk * 16 + (mat & 1) * 8 + (lane & 7);
         const int c = 2 * jp + (mat >> 1);
         uint32_t bf[4];
-        ldmatrix_x4_trans(bf, smem_u32(sV[st] + r * HD * 2 + swz<CH>(r, c) * 16));
+        ldmatrix_x4_trans(bf, smem_u32(sV[st] + r * HDV * 2 + swz<CHV>(r, c) * 16));
         mma_bf16_16816(o[2 * jp], pa, bf);
         mma_bf16_16816(o[2 * jp + 1], pa, bf + 2);
       }
@@ -220,9 +224,9 @@ __global__ void __launch_bounds__(128) flash_prefill_kernel(const __nv_bfloat16*
     const int qi = qi0 + r * 8;
     if (qi >= len) continue;
     const float inv = l_run[r] > 0.f ? 1.f / l_run[r] : 0.f;
-    __nv_bfloat16* orow = out + (int64_t)(s0 + qi) * out_stride + h * HD;
+    __nv_bfloat16* orow = out + (int64_t)(s0 + qi) * out_stride + h * o_hs;
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j)
+    for (int j = 0; j < HDV / 8; ++j)
       *reinterpret_cast<uint32_t*>(orow + j * 8 + 2 * t4) = pack2(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
   }
 }
@@ -582,16 +586,18 @@ bool set_smem(int bytes) {
   return done[dev];
 }
 
-template <int HD, bool CAUSAL>
-int launch_prefill(const void* q, int64_t qs, const void* k, const void* v, int64_t kvs, void* out, int64_t os,
-                   const int32_t* cu, int num_seqs, int max_seqlen, int nq, int nkv, float scale, cudaStream_t st) {
-  auto kern = flash_prefill_kernel<HD, CAUSAL>;
-  if (!set_smem<flash_prefill_kernel<HD, CAUSAL>>(PrefillCfg<HD>::SMEM)) return B200_ERROR_UNSUPPORTED;
+template <int HDK, int HDV, bool CAUSAL>
+int launch_prefill(const void* q, int64_t qs, int64_t qhs, const void* k, int64_t ks, int64_t khs, const void* v,
+                   int64_t vs, int64_t vhs, void* out, int64_t os, int64_t ohs, const int32_t* cu, int num_seqs,
+                   int max_seqlen, int nq, int nkv, float scale, cudaStream_t st) {
+  using Cf = PrefillCfg<HDK, HDV>;
+  auto kern = flash_prefill_kernel<HDK, HDV, CAUSAL>;
+  if (!set_smem<flash_prefill_kernel<HDK, HDV, CAUSAL>>(Cf::SMEM)) return B200_ERROR_UNSUPPORTED;
   const int mblocks = (max_seqlen + 63) / 64;
   dim3 grid(mblocks, nq, num_seqs);
-  launch_kernel(kern, grid, 128, PrefillCfg<HD>::SMEM, st, static_cast<const __nv_bfloat16*>(q), qs,
-                static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), kvs,
-                static_cast<__nv_bfloat16*>(out), os, cu, nq, nkv, scale * kLog2e, mblocks);
+  launch_kernel(kern, grid, 128, Cf::SMEM, st, static_cast<const __nv_bfloat16*>(q), qs, qhs,
+                static_cast<const __nv_bfloat16*>(k), ks, khs, static_cast<const __nv_bfloat16*>(v), vs, vhs,
+                static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq, nkv, scale * kLog2e, mblocks);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -600,31 +606,53 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
+extern "C" int b200_flash_prefill_ex(const void* q, int64_t q_stride, int64_t q_head_stride, const void* k,
+                                     int64_t k_stride, int64_t k_head_stride, const void* v, int64_t v_stride,
+                                     int64_t v_head_stride, void* out, int64_t out_stride, int64_t out_head_stride,
+                                     const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int nq, int nkv,
+                                     int head_dim_qk, int head_dim_v, float scale, int causal, b200_stream_t stream) {
+  if (!q || !k || !v || !out || !cu_seqlens || num_seqs < 0 || max_seqlen < 0 || nq <= 0 || nkv <= 0 || nq % nkv)
+    return B200_ERROR_INVALID_PARAM;
+  for (int64_t s : {q_stride, q_head_stride, k_stride, k_head_stride, v_stride, v_head_stride, out_stride,
+                    out_head_stride})
+    if (s < 0 || s % 8) return B200_ERROR_INVALID_PARAM;
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(out)) return B200_ERROR_INVALID_PARAM;
+  if (q_stride < (int64_t)(nq - 1) * q_head_stride + head_dim_qk ||
+      k_stride < (int64_t)(nkv - 1) * k_head_stride + head_dim_qk ||
+      v_stride < (int64_t)(nkv - 1) * v_head_stride + head_dim_v ||
+      out_stride < (int64_t)(nq - 1) * out_head_stride + head_dim_v)
+    return B200_ERROR_INVALID_PARAM;
+  if (num_seqs == 0 || max_seqlen == 0) return B200_OK;
+  if (num_seqs > 65535 || nq > 65535) return B200_ERROR_UNSUPPORTED;
+#define B200_PF(HK, HV)                                                                                          \
+  return causal ? launch_prefill<HK, HV, true>(q, q_stride, q_head_stride, k, k_stride, k_head_stride, v, v_stride, \
+                                               v_head_stride, out, out_stride, out_head_stride, cu_seqlens,        \
+                                               num_seqs, max_seqlen, nq, nkv, scale, stream)                     \
+                : launch_prefill<HK, HV, false>(q, q_stride, q_head_stride, k, k_stride, k_head_stride, v, v_stride, \
+                                                v_head_stride, out, out_stride, out_head_stride, cu_seqlens,       \
+                                                num_seqs, max_seqlen, nq, nkv, scale, stream)
+  if (head_dim_qk == head_dim_v) {
+    switch (head_dim_qk) {
+      case 16: B200_PF(16, 16);
+      case 32: B200_PF(32, 32);
+      case 64: B200_PF(64, 64);
+      case 128: B200_PF(128, 128);
+      default: return B200_ERROR_UNSUPPORTED;
+    }
+  }
+  if (head_dim_qk == 192 && head_dim_v == 128) B200_PF(192, 128);
+  return B200_ERROR_UNSUPPORTED;
+#undef B200_PF
+}
+
 extern "C" int b200_flash_prefill(const void* q, int64_t q_stride, const void* k, const void* v, int64_t kv_stride,
                                   void* out, int64_t out_stride, const int32_t* cu_seqlens, int num_seqs,
                                   int max_seqlen, int nq, int nkv, int head_dim, float scale, int causal,
                                   b200_stream_t stream) {
-  if (!q || !k || !v || !out || !cu_seqlens || num_seqs < 0 || max_seqlen < 0 || nq <= 0 || nkv <= 0 || nq % nkv)
-    return B200_ERROR_INVALID_PARAM;
-  if (q_stride % 8 || kv_stride % 8 || out_stride % 8 || !al16(q) || !al16(k) || !al16(v) || !al16(out))
-    return B200_ERROR_INVALID_PARAM;
-  if (q_stride < (int64_t)nq * head_dim || kv_stride < (int64_t)nkv * head_dim || out_stride < (int64_t)nq * head_dim)
-    return B200_ERROR_INVALID_PARAM;
-  if (num_seqs == 0 || max_seqlen == 0) return B200_OK;
-  if (num_seqs > 65535 || nq > 65535) return B200_ERROR_UNSUPPORTED;
-#define B200_PF(HD)                                                                                           \
-  return causal ? launch_prefill<HD, true>(q, q_stride, k, v, kv_stride, out, out_stride, cu_seqlens, num_seqs, \
-                                           max_seqlen, nq, nkv, scale, stream)                                 \
-                : launch_prefill<HD, false>(q, q_stride, k, v, kv_stride, out, out_stride, cu_seqlens, num_seqs, \
-                                            max_seqlen, nq, nkv, scale, stream)
-  switch (head_dim) {
-    case 16: B200_PF(16);
-    case 32: B200_PF(32);
-    case 64: B200_PF(64);
-    case 128: B200_PF(128);
-    default: return B200_ERROR_UNSUPPORTED;
-  }
-#undef B200_PF
+  if (head_dim <= 0) return B200_ERROR_INVALID_PARAM;
+  return b200_flash_prefill_ex(q, q_stride, head_dim, k, kv_stride, head_dim, v, kv_stride, head_dim, out, out_stride,
+                               head_dim, cu_seqlens, num_seqs, max_seqlen, nq, nkv, head_dim, head_dim, scale, causal,
+                               stream);
 }
 
 // ---------------------------------------------------------------------------

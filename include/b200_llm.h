@@ -233,6 +233,55 @@ B200_API int b200_flash_prefill(const void* q, int64_t q_stride, const void* k, 
                        void* out, int64_t out_stride, const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
                        int nq, int nkv, int head_dim, float scale, int causal, b200_stream_t stream);
 
+/* b200_flash_prefill with a row and a head stride per operand (elements) and
+ * separate query/key and value head widths: (qk, v) in {(16,16), (32,32),
+ * (64,64), (128,128), (192,128)} — the last is a decompressed MLA head
+ * (128 no-rope + 64 rope dims against 128 value dims).  Same causal rule. */
+B200_API int b200_flash_prefill_ex(const void* q, int64_t q_stride, int64_t q_head_stride, const void* k,
+                                   int64_t k_stride, int64_t k_head_stride, const void* v, int64_t v_stride,
+                                   int64_t v_head_stride, void* out, int64_t out_stride, int64_t out_head_stride,
+                                   const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int nq, int nkv,
+                                   int head_dim_qk, int head_dim_v, float scale, int causal, b200_stream_t stream);
+
+/* ---- multi-head latent attention (DeepSeek-V2): fills the reference's stubs
+ * MlaAttentionBuilder (atb_cpp_llm/src/components/common/attention_builder.h:60-69)
+ * and AttnConfig.kv_lora_rank / q_lora_rank (atb_cpp_llm/include/atb_llm/layer_desc.h:47-49).
+ * Latent cache: [num_blocks * block_size, 576] bf16 — per token the 512
+ * normalised compressed-KV values, then the 64 roped key dims shared by all
+ * heads. */
+
+/* Per token t < T: c = RMSNorm(kv_a[t, :512]) * kv_norm_weight and k_pe =
+ * rope(kv_a[t, 512:576]) into latent-cache row slot_mapping[t] (skipped when
+ * slot_mapping is NULL or the slot is -1) and into ckv_out [T, 512] /
+ * kpe_out [T, 64] when not NULL; the 64 rope dims at q_rope_offset of each
+ * of the num_heads query heads (head stride q_head_stride) are rotated in
+ * place.  Rope pairs are the interleaved (2i, 2i+1) of the projection, stored
+ * de-interleaved (DeepSeek-V2's layout); cos/sin [T, 64] from
+ * b200_rope_table_freqs. */
+B200_API int b200_mla_prep(void* q, int64_t q_stride, int64_t q_head_stride, int num_heads, int q_rope_offset,
+                           const void* kv_a, int64_t kv_a_stride, const void* kv_norm_weight, float eps,
+                           const float* cos_tab, const float* sin_tab, const int64_t* slot_mapping,
+                           void* latent_cache, int64_t num_slots, void* ckv_out, void* kpe_out, int64_t T,
+                           b200_stream_t stream);
+
+/* Absorbed-latent decode attention: q [batch, q_stride] holds per head (576
+ * wide) the query projected into the latent space (512) then its roped dims
+ * (64); out [batch, out_stride] receives per head (512 wide) sum_t softmax_t
+ * (q . cache_t * scale) cache_t[:512].  num_heads % 16 == 0, block_size % 64
+ * == 0; workspace (b200_mla_decode_workspace_bytes) enables splitting the
+ * context across CTAs. */
+B200_API int b200_mla_decode(const void* q, int64_t q_stride, const void* latent_cache, const int32_t* block_tables,
+                             int max_blocks_per_seq, const int32_t* context_lens, int batch, int num_heads,
+                             int block_size, int64_t num_blocks, float scale, void* out, int64_t out_stride,
+                             void* workspace, int64_t workspace_bytes, int max_context, b200_stream_t stream);
+B200_API int64_t b200_mla_decode_workspace_bytes(int batch, int num_heads, int max_context);
+
+/* cos/sin tables [T, rot_dim] (fp32) = cos/sin(positions[t] * inv_freq[i]) *
+ * mscale, i = d mod rot_dim/2, for a host array of rot_dim/2 (<= 128)
+ * frequencies — e.g. DeepSeek-V2's YaRN-scaled ones. */
+B200_API int b200_rope_table_freqs(const int64_t* positions, int64_t T, int rot_dim, const float* inv_freq,
+                                   float mscale, float* cos_out, float* sin_out, b200_stream_t stream);
+
 /* Single-token decode attention over a paged KV cache
  * (k_cache/v_cache [num_blocks, nkv, block_size, head_dim], block_size 128 or 64):
  * sequence b attends to its first context_lens[b] cached positions through
