@@ -4,6 +4,8 @@
 // and the model registry (atb_cpp_llm/src/engine/model_registry.cpp:32-121).
 #include <sys/stat.h>
 
+#include <cstdio>
+
 #include <functional>
 #include <map>
 #include <mutex>
@@ -56,6 +58,7 @@ class ModelRegistry {
     entries_["qwen2"] = {"qwen2", 5, nullptr};
     entries_["mixtral"] = {"mixtral", 10, nullptr};      // GQA + 8 routed SwiGLU experts, top-2
     entries_["qwen3_moe"] = {"qwen3_moe", 10, nullptr};  // GQA + QK-norm + routed experts
+    entries_["deepseek_v2"] = {"deepseek_v2", 10, nullptr};  // latent attention + routed & shared experts
     entries_["llama"] = {"llama", 1, dense};
   }
   mutable std::mutex mu_;
@@ -95,6 +98,24 @@ static Status set_vision_weight(b200_engine_s* e, const std::string& name, const
 static bool file_exists(const std::string& p) {
   struct stat st;
   return stat(p.c_str(), &st) == 0;
+}
+
+extern "C" int b200_engine_config_check(const char* config_json, char* model_type, int model_type_len) {
+  if (!config_json) return ERROR_INVALID_PARAM;
+  JsonConfig cfg = JsonConfig::Parse(config_json);
+  if (!cfg.IsValid()) return ERROR_INVALID_PARAM;
+  const std::string mt = ModelRegistry::Instance().Resolve(cfg);
+  if (model_type && model_type_len > 0) {
+    std::snprintf(model_type, (size_t)model_type_len, "%s", mt.c_str());
+  }
+  if (mt.empty()) return ERROR_UNSUPPORTED;
+  ModelConfig mc;
+  B200_RETURN_IF(ModelConfig::FromJson(cfg, mc));
+  if (cfg.HasKey("vision_config")) {
+    VisionConfig vc;
+    B200_RETURN_IF(VisionConfig::FromJson(cfg, vc));
+  }
+  return STATUS_OK;
 }
 
 extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* out) {

@@ -7,6 +7,7 @@
 #include "engine/engine_kernels.h"
 #include "fused.h"
 #include "gemm.h"
+#include "mla.h"
 
 namespace b200 {
 unsigned* error_word(int device);
@@ -48,8 +49,44 @@ Status ModelConfig::FromJson(const JsonConfig& root, ModelConfig& c) {
   c.rope_theta = t.GetFloat("rope_theta", 1e6f);
   c.tie_embeddings = root.GetBool("tie_word_embeddings", t.GetBool("tie_word_embeddings", false));
   c.qk_norm = starts_with(c.model_type, "qwen3");
-  if (t.HasKey("kv_lora_rank") && t.GetInt("kv_lora_rank") > 0) return ERROR_UNSUPPORTED;  // MLA: not this runner
-  if (t.HasKey("num_local_experts")) {  // Mixtral
+  if (t.HasKey("kv_lora_rank") && t.GetInt("kv_lora_rank", 0) > 0) {  // DeepSeek-V2 multi-head latent attention
+    if (t.GetInt("q_lora_rank", 0) > 0) return ERROR_UNSUPPORTED;      // the V2-Lite form (no query LoRA)
+    c.kv_lora = t.GetInt("kv_lora_rank");
+    c.qk_nope = t.GetInt("qk_nope_head_dim");
+    c.qk_rope = t.GetInt("qk_rope_head_dim");
+    c.v_head = t.GetInt("v_head_dim");
+    if (c.kv_lora != 512 || c.qk_rope != 64 || c.qk_nope != 128 || c.v_head != 128 || c.heads % 16)
+      return ERROR_UNSUPPORTED;
+    c.head_dim = c.qk_nope + c.qk_rope;
+    c.kv_heads = c.heads;
+    c.qk_norm = false;
+    if (t.HasKey("rope_scaling")) {
+      JsonConfig rs = t.GetSubConfig("rope_scaling");
+      const std::string type = rs.GetString("type", rs.GetString("rope_type"));
+      if (type != "yarn") return ERROR_UNSUPPORTED;
+      c.yarn_factor = rs.GetFloat("factor", 1.f);
+      c.yarn_orig_max = rs.GetFloat("original_max_position_embeddings", 4096.f);
+      c.yarn_beta_fast = rs.GetFloat("beta_fast", 32.f);
+      c.yarn_beta_slow = rs.GetFloat("beta_slow", 1.f);
+      c.yarn_mscale = rs.GetFloat("mscale", 1.f);
+      c.yarn_mscale_all = rs.GetFloat("mscale_all_dim", 0.f);
+    }
+    auto mscale = [](float s, float m) { return s <= 1.f ? 1.f : 0.1f * m * std::log(s) + 1.f; };
+    const float m = mscale(c.yarn_factor, c.yarn_mscale_all);
+    c.attn_scale = 1.0f / std::sqrt((float)(c.qk_nope + c.qk_rope)) * m * m;
+  }
+  if (t.HasKey("n_routed_experts") && t.GetInt("n_routed_experts", 0) > 0) {  // DeepSeek MoE
+    c.experts = t.GetInt("n_routed_experts");
+    c.top_k = t.GetInt("num_experts_per_tok", 6);
+    c.moe_intermediate = t.GetInt("moe_intermediate_size");
+    c.shared_intermediate = t.GetInt("n_shared_experts", 0) * c.moe_intermediate;
+    c.first_dense = t.GetInt("first_k_dense_replace", 0);
+    c.norm_topk = t.GetBool("norm_topk_prob", false);
+    if (t.GetInt("moe_layer_freq", 1) != 1) return ERROR_UNSUPPORTED;
+    const std::string tm = t.GetString("topk_method", "greedy");
+    const std::string sf = t.GetString("scoring_func", "softmax");
+    if (tm != "greedy" || sf != "softmax") return ERROR_UNSUPPORTED;
+  } else if (t.HasKey("num_local_experts")) {  // Mixtral
     c.experts = t.GetInt("num_local_experts");
     c.top_k = t.GetInt("num_experts_per_tok", 2);
     c.moe_intermediate = c.intermediate;
@@ -79,7 +116,7 @@ Status ModelConfig::FromJson(const JsonConfig& root, ModelConfig& c) {
   if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.head_dim <= 0 ||
       c.intermediate <= 0 || c.vocab <= 0)
     return ERROR_INVALID_PARAM;
-  if (c.hidden % 8 || c.intermediate % 8 || c.head_dim != 128) return ERROR_UNSUPPORTED;
+  if (c.hidden % 8 || c.intermediate % 8 || (!c.mla() && c.head_dim != 128)) return ERROR_UNSUPPORTED;
   return STATUS_OK;
 }
 
@@ -105,7 +142,14 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   alloc_.reset(new TensorAllocator(ctx_->GetStream()));
   err_ = b200::error_word(opt.device);
   const int64_t H = cfg.hidden, L = cfg.layers, hd = cfg.head_dim, I = cfg.intermediate, V = cfg.vocab;
-  const int64_t QKV = cfg.qkv_dim(), AO = (int64_t)cfg.heads * hd;
+  const bool mla = cfg.mla();
+  const int64_t nh = cfg.heads;
+  // MLA: fused projection widths (prefill q + kv_a, decode absorbed q + kv_a)
+  const int64_t NQP = nh * (cfg.qk_nope + cfg.qk_rope) + cfg.kv_lora + cfg.qk_rope;
+  const int64_t NQD = nh * (cfg.kv_lora + cfg.qk_rope) + cfg.kv_lora + cfg.qk_rope;
+  const int64_t QKV = mla ? std::max(NQP, NQD) : cfg.qkv_dim();
+  const int64_t AO = mla ? nh * cfg.v_head : (int64_t)cfg.heads * hd;  // attention output fed to o_proj
+  if (mla && opt.block_size % 64) return ERROR_INVALID_PARAM;
   max_t_ = std::max<int64_t>(opt.max_prefill_tokens, opt.max_batch);
   max_blocks_ = (opt.max_context + opt.block_size - 1) / opt.block_size;
   num_blocks_ = (int64_t)opt.max_batch * max_blocks_;
@@ -115,7 +159,35 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   if (!cfg.tie_embeddings) B200_RETURN_IF(A(lm_head_, DType::BF16, {V, H}));
   else lm_head_ = embed_;
   B200_RETURN_IF(A(final_norm_, DType::BF16, {H}));
-  B200_RETURN_IF(A(wqkv_, DType::BF16, {L, QKV, H}));
+  if (mla) {
+    B200_RETURN_IF(A(wq_, DType::BF16, {L, NQP, H}));
+    B200_RETURN_IF(A(wqabs_, DType::BF16, {L, NQD, H}));
+    B200_RETURN_IF(A(kvnorm_, DType::BF16, {L, cfg.kv_lora}));
+    B200_RETURN_IF(A(wkvb_, DType::BF16, {L, nh * (cfg.qk_nope + cfg.v_head), cfg.kv_lora}));
+    B200_RETURN_IF(A(woabs_, DType::BF16, {L, H, nh * cfg.kv_lora}));
+    // YaRN frequencies of the rope dims (DeepSeek-V2's yarn_find_correction_range + linear ramp)
+    const int d = cfg.qk_rope;
+    const double base = cfg.rope_theta;
+    auto corr_dim = [&](double rot) {
+      return (d * std::log(cfg.yarn_orig_max / (rot * 2 * M_PI))) / (2 * std::log(base));
+    };
+    double low = std::max(std::floor(corr_dim(cfg.yarn_beta_fast)), 0.0);
+    double high = std::min(std::ceil(corr_dim(cfg.yarn_beta_slow)), (double)(d - 1));
+    if (low == high) high += 0.001;
+    inv_freq_.resize(d / 2);
+    for (int i = 0; i < d / 2; ++i) {
+      const float e = (float)(2 * i) / (float)d;
+      const float extra = 1.0f / std::pow((float)base, e);
+      const float inter = 1.0f / ((float)cfg.yarn_factor * std::pow((float)base, e));
+      const float ramp = std::min(1.0f, std::max(0.0f, (float)((i - low) / (high - low))));
+      const float mask = cfg.yarn_factor > 1.f ? 1.0f - ramp : 1.0f;
+      inv_freq_[i] = inter * (1.0f - mask) + extra * mask;
+    }
+    auto ms = [](float s, float m) { return s <= 1.f ? 1.f : 0.1f * m * std::log(s) + 1.f; };
+    rope_mscale_ = ms(cfg.yarn_factor, cfg.yarn_mscale) / ms(cfg.yarn_factor, cfg.yarn_mscale_all);
+  } else {
+    B200_RETURN_IF(A(wqkv_, DType::BF16, {L, QKV, H}));
+  }
   B200_RETURN_IF(A(wo_, DType::BF16, {L, H, AO}));
   dense_idx_.assign(L, -1);
   moe_idx_.assign(L, -1);
@@ -138,16 +210,24 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
       B200_RETURN_IF(A(sdown_, DType::BF16, {n_moe, H, Is}));
     }
   }
-  B200_RETURN_IF(A(qnorm_, DType::BF16, {L, hd}));
-  B200_RETURN_IF(A(knorm_, DType::BF16, {L, hd}));
+  if (!mla) {
+    B200_RETURN_IF(A(qnorm_, DType::BF16, {L, hd}));
+    B200_RETURN_IF(A(knorm_, DType::BF16, {L, hd}));
+  }
   B200_RETURN_IF(A(iln_, DType::BF16, {L, H}));
   B200_RETURN_IF(A(pln_, DType::BF16, {L, H}));
   weight_bytes_ = alloc_->BytesInUse();
 
-  B200_RETURN_IF(A(kv_, DType::BF16, {L, 2, num_blocks_, cfg.kv_heads, opt.block_size, hd}));
-  kv_bytes_ = kv_.bytes();
   // finite contents everywhere: tiles past a sequence's end are read (and masked)
-  B200_RETURN_IF(FromCuda(cudaMemsetAsync(kv_.data, 0, kv_.bytes(), ctx_->GetStream())));
+  if (mla) {
+    B200_RETURN_IF(A(lat_, DType::BF16, {L, num_blocks_ * opt.block_size, cfg.kv_lora + cfg.qk_rope}));
+    kv_bytes_ = lat_.bytes();
+    B200_RETURN_IF(FromCuda(cudaMemsetAsync(lat_.data, 0, lat_.bytes(), ctx_->GetStream())));
+  } else {
+    B200_RETURN_IF(A(kv_, DType::BF16, {L, 2, num_blocks_, cfg.kv_heads, opt.block_size, hd}));
+    kv_bytes_ = kv_.bytes();
+    B200_RETURN_IF(FromCuda(cudaMemsetAsync(kv_.data, 0, kv_.bytes(), ctx_->GetStream())));
+  }
   B200_RETURN_IF(A(block_tables_, DType::INT32, {opt.max_batch, max_blocks_}));
   B200_RETURN_IF(A(ctx_lens_, DType::INT32, {opt.max_batch}));
   {
@@ -163,7 +243,15 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   B200_RETURN_IF(A(hidden_, DType::BF16, {max_t_, H}));
   B200_RETURN_IF(A(normed_, DType::BF16, {max_t_, H}));
   B200_RETURN_IF(A(qkv_, DType::BF16, {max_t_, QKV}));
-  B200_RETURN_IF(A(attn_, DType::BF16, {max_t_, AO}));
+  B200_RETURN_IF(A(attn_, DType::BF16, {max_t_, mla ? std::max(AO, nh * cfg.kv_lora) : AO}));
+  if (mla) {
+    B200_RETURN_IF(A(ckv_, DType::BF16, {max_t_, cfg.kv_lora}));
+    B200_RETURN_IF(A(kpe_, DType::BF16, {max_t_, cfg.qk_rope}));
+    B200_RETURN_IF(A(kvb_, DType::BF16, {max_t_, nh * (cfg.qk_nope + cfg.v_head)}));
+    B200_RETURN_IF(A(kbuf_, DType::BF16, {max_t_, nh * (cfg.qk_nope + cfg.qk_rope)}));
+    mla_ws_bytes_ = b200_mla_decode_workspace_bytes(opt.max_batch, (int)nh, opt.max_context);
+    if (mla_ws_bytes_ > 0) B200_RETURN_IF(A(mla_ws_, DType::FP32, {(mla_ws_bytes_ + 3) / 4}));
+  }
   B200_RETURN_IF(A(act_, DType::BF16, {max_t_, n_dense > 0 ? I : 8}));
   B200_RETURN_IF(A(cos_, DType::FP32, {max_t_, hd}));
   B200_RETURN_IF(A(sin_, DType::FP32, {max_t_, hd}));
@@ -202,7 +290,8 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   // so the need stops growing after a few thousand tokens)
   int64_t ws = 0;
   const int64_t Isx = std::max<int64_t>(Is, 8);
-  const int64_t shapes[7][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}, {2 * Isx, H}, {H, Isx}};
+  const int64_t AOx = mla ? nh * cfg.kv_lora : AO;  // decode output projection of MLA reads the latent heads
+  const int64_t shapes[8][2] = {{QKV, H}, {H, AO}, {2 * I, H}, {H, I}, {V, H}, {2 * Isx, H}, {H, Isx}, {H, AOx}};
   std::vector<int64_t> ms = {1, (int64_t)opt.max_batch};
   for (int64_t m = 64; m <= std::min<int64_t>(max_t_, 65536); m += 64) ms.push_back(m);
   for (int64_t m : ms)
@@ -213,7 +302,7 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
     // split-K accumulator + tile counters start at zero; every GEMM leaves them zero
     B200_RETURN_IF(FromCuda(cudaMemsetAsync(gemm_ws_.data, 0, gemm_ws_.bytes(), ctx_->GetStream())));
   }
-  attn_ws_bytes_ = b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
+  attn_ws_bytes_ = mla ? 0 : b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
   if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
 
   pinned_bytes_ = (size_t)max_t_ * 8 * 5 + (size_t)(opt.max_batch + 1) * 16 + (size_t)H * 4 + 4096;
@@ -232,7 +321,9 @@ Status DecoderModel::InitRandomWeights(uint64_t seed, float std) {
   B200_RETURN_IF(N(wo_));
   B200_RETURN_IF(N(wgu_));
   B200_RETURN_IF(N(wdown_));
-  for (DeviceTensor* t : {&router_, &egu_, &edown_, &sgu_, &sdown_}) B200_RETURN_IF(N(*t));
+  for (DeviceTensor* t : {&router_, &egu_, &edown_, &sgu_, &sdown_, &wq_, &wkvb_}) B200_RETURN_IF(N(*t));
+  B200_RETURN_IF(O(kvnorm_));
+  absorb_dirty_ = true;
   B200_RETURN_IF(O(final_norm_));
   B200_RETURN_IF(O(qnorm_));
   B200_RETURN_IF(O(knorm_));
@@ -273,6 +364,19 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
   const int l = std::atoi(name.substr(pre.size(), dot - pre.size()).c_str());
   if (l < 0 || l >= cfg_.layers) return ERROR_WEIGHT_LOAD;
   const std::string leaf = name.substr(dot + 1);
+  if (cfg_.mla() && starts_with(leaf, "self_attn.")) {
+    const int64_t nh = cfg_.heads, R = cfg_.kv_lora, dr = cfg_.qk_rope;
+    const int64_t NQP = nh * (cfg_.qk_nope + dr) + R + dr, KVB = nh * (cfg_.qk_nope + cfg_.v_head);
+    const int64_t AOm = nh * cfg_.v_head;
+    absorb_dirty_ = true;
+    if (leaf == "self_attn.q_proj.weight") return put(wq_, (int64_t)l * NQP * H, nh * (cfg_.qk_nope + dr) * H);
+    if (leaf == "self_attn.kv_a_proj_with_mqa.weight")
+      return put(wq_, (int64_t)l * NQP * H + nh * (cfg_.qk_nope + dr) * H, (R + dr) * H);
+    if (leaf == "self_attn.kv_a_layernorm.weight") return put(kvnorm_, (int64_t)l * R, R);
+    if (leaf == "self_attn.kv_b_proj.weight") return put(wkvb_, (int64_t)l * KVB * R, KVB * R);
+    if (leaf == "self_attn.o_proj.weight") return put(wo_, (int64_t)l * H * AOm, H * AOm);
+    return ERROR_WEIGHT_LOAD;
+  }
   const int64_t nq = (int64_t)cfg_.heads * hd, nk = (int64_t)cfg_.kv_heads * hd;
   if (leaf == "self_attn.q_proj.weight") return put(wqkv_, (int64_t)l * QKV * H, nq * H);
   if (leaf == "self_attn.k_proj.weight") return put(wqkv_, (int64_t)l * QKV * H + nq * H, nk * H);
@@ -375,6 +479,9 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
       B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, 0), normed_.data, nullptr, T, H, H, cfg_.eps, st));
     }
     // attention block
+    if (cfg_.mla()) {
+      B200_RETURN_IF(MlaBlock(l, T, decode, batch, &s_o));
+    } else {
     B200_RETURN_IF(gemm(normed_.data, H, bf(wqkv_, (int64_t)l * QKV * H), H, qkv_.data, QKV, QKV, H, B200_EPI_NONE,
                         nullptr, 0, &s_qkv));
     uint16_t* kc = bf(kv_, (int64_t)l * kv_layer);
@@ -399,6 +506,7 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     }
     B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, H, AO, B200_EPI_RESIDUAL,
                         hidden_.data, H, &s_o));
+    }  // GQA attention
     ++launches_;
     if (s_o > 1)  // hidden += sum(partials); normed = rmsnorm(hidden)
       B200_RETURN_IF(b200::splitk_residual_rmsnorm(ws, s_o, T, H, hidden_.data, bf(pln_, (int64_t)l * H),
@@ -449,6 +557,98 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     }
   }
   return STATUS_OK;
+}
+
+Status DecoderModel::RopeTables(int64_t T) {
+  cudaStream_t st = ctx_->GetStream();
+  const int hd = cfg_.head_dim;
+  if (cfg_.mla())
+    return (Status)b200_rope_table_freqs(pos_.as<int64_t>(), T, cfg_.qk_rope, inv_freq_.data(), rope_mscale_,
+                                         cos_.as<float>(), sin_.as<float>(), st);
+  if (cfg_.mrope)
+    return (Status)b200_rope_table_mrope(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cfg_.mrope_section[0],
+                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
+                                         sin_.as<float>(), st);
+  return (Status)b200_rope_table_1d(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
+                                    st);
+}
+
+// Latent attention of layer l on normed_, ending with the output projection
+// added into hidden_ (*s_o = its split count, reduced by the caller's norm).
+// Prefill decompresses the heads (q_nope|q_pe against k_nope|k_pe, v from
+// kv_b) and writes the latent cache; decode runs absorbed over the cache.
+Status DecoderModel::MlaBlock(int l, int64_t T, bool decode, int batch, int* s_o) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, nh = cfg_.heads, R = cfg_.kv_lora, dr = cfg_.qk_rope, dn = cfg_.qk_nope;
+  const int64_t dv = cfg_.v_head;
+  const int64_t NQP = nh * (dn + dr) + R + dr, NQD = nh * (R + dr) + R + dr, KVB = nh * (dn + dv);
+  const int64_t rows = num_blocks_ * opt_.block_size;
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  uint16_t* lat = bf(lat_, (int64_t)l * rows * (R + dr));
+  uint16_t* q = static_cast<uint16_t*>(qkv_.data);
+  float* ws = gemm_ws_.as<float>();
+  const int64_t* slots = write_kv_ ? slots_.as<int64_t>() : nullptr;
+  if (!decode) {
+    launches_ += 6;
+    B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(wq_, (int64_t)l * NQP * H), H, q, NQP, T, NQP, H,
+                                     B200_EPI_NONE, nullptr, nullptr, 0, nullptr, 0, st, nullptr));
+    B200_RETURN_IF(b200_mla_prep(q, NQP, dn + dr, (int)nh, (int)dn, q + nh * (dn + dr), NQP, bf(kvnorm_, l * R),
+                                 cfg_.eps, cos_.as<float>(), sin_.as<float>(), slots, lat, rows, ckv_.data, kpe_.data,
+                                 T, st));
+    B200_RETURN_IF(b200::gemm_launch(ckv_.data, R, bf(wkvb_, (int64_t)l * KVB * R), R, kvb_.data, KVB, T, KVB, R,
+                                     B200_EPI_NONE, nullptr, nullptr, 0, nullptr, 0, st, nullptr));
+    B200_RETURN_IF(b200::mla_build_k(kvb_.data, KVB, kpe_.data, kbuf_.data, T, (int)nh, st));
+    B200_RETURN_IF(b200_flash_prefill_ex(q, NQP, dn + dr, kbuf_.data, nh * (dn + dr), dn + dr,
+                                         static_cast<uint16_t*>(kvb_.data) + dn, KVB, dn + dv, attn_.data, nh * dv,
+                                         dv, cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, (int)nh, (int)nh,
+                                         (int)(dn + dr), (int)dv, cfg_.attn_scale, 1, st));
+    return (Status)b200::gemm_launch(attn_.data, nh * dv, bf(wo_, (int64_t)l * H * nh * dv), nh * dv, hidden_.data,
+                                     H, T, H, nh * dv, B200_EPI_RESIDUAL, nullptr, hidden_.data, H, ws,
+                                     gemm_ws_bytes_, st, s_o);
+  }
+  launches_ += 4 + (mla_ws_bytes_ > 0 ? 1 : 0);
+  B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(wqabs_, (int64_t)l * NQD * H), H, q, NQD, T, NQD, H,
+                                   B200_EPI_NONE, nullptr, nullptr, 0, nullptr, 0, st, nullptr));
+  B200_RETURN_IF(b200_mla_prep(q, NQD, R + dr, (int)nh, (int)R, q + nh * (R + dr), NQD, bf(kvnorm_, l * R), cfg_.eps,
+                               cos_.as<float>(), sin_.as<float>(), slots, lat, rows, nullptr, nullptr, T, st));
+  B200_RETURN_IF(b200_mla_decode(q, NQD, lat, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(), batch,
+                                 (int)nh, opt_.block_size, num_blocks_, cfg_.attn_scale, attn_.data, nh * R,
+                                 mla_ws_.data, mla_ws_bytes_, opt_.max_context, st));
+  return (Status)b200::gemm_launch(attn_.data, nh * R, bf(woabs_, (int64_t)l * H * nh * R), nh * R, hidden_.data, H,
+                                   T, H, nh * R, B200_EPI_RESIDUAL, nullptr, hidden_.data, H, ws, gemm_ws_bytes_, st,
+                                   s_o);
+}
+
+// Fold W_UK into the decode query projection and W_UV into the decode output
+// projection (once after the weights change):
+//   Wqabs[h*576 + c, :] = sum_d Wkvb[h*256 + d, c] Wq[h*192 + d, :]   (c < 512)
+//   Wqabs[h*576 + 512 + i, :] = Wq[h*192 + 128 + i, :]                 (rope rows)
+//   Woabs[:, h*512 + c] = sum_d Wo[:, h*128 + d] Wkvb[h*256 + 128 + d, c]
+Status DecoderModel::MlaAbsorb() {
+  if (!cfg_.mla() || !absorb_dirty_) return STATUS_OK;
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, nh = cfg_.heads, R = cfg_.kv_lora, dr = cfg_.qk_rope, dn = cfg_.qk_nope;
+  const int64_t dv = cfg_.v_head;
+  const int64_t NQP = nh * (dn + dr) + R + dr, NQD = nh * (R + dr) + R + dr, KVB = nh * (dn + dv);
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  for (int l = 0; l < cfg_.layers; ++l) {
+    uint16_t* wq = bf(wq_, (int64_t)l * NQP * H);
+    uint16_t* wkvb = bf(wkvb_, (int64_t)l * KVB * R);
+    uint16_t* wqa = bf(wqabs_, (int64_t)l * NQD * H);
+    uint16_t* wo = bf(wo_, (int64_t)l * H * nh * dv);
+    uint16_t* woa = bf(woabs_, (int64_t)l * H * nh * R);
+    B200_RETURN_IF(b200::mla_absorb(wkvb, 1, R, (dn + dv) * R, wq, H, 1, (dn + dr) * H, wqa, H, 1, (R + dr) * H,
+                                    (int)R, (int)H, (int)dn, (int)nh, st));
+    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(wqa + R * H, (size_t)(R + dr) * H * 2, wq + dn * H,
+                                              (size_t)(dn + dr) * H * 2, (size_t)dr * H * 2, (size_t)nh,
+                                              cudaMemcpyDeviceToDevice, st)));
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(wqa + nh * (R + dr) * H, wq + nh * (dn + dr) * H, (size_t)(R + dr) * H * 2,
+                                            cudaMemcpyDeviceToDevice, st)));
+    B200_RETURN_IF(b200::mla_absorb(wo, nh * dv, 1, dv, wkvb + dn * R, R, 1, (dn + dv) * R, woa, nh * R, 1, R,
+                                    (int)H, (int)R, (int)dv, (int)nh, st));
+  }
+  absorb_dirty_ = false;
+  return ctx_->Synchronize();
 }
 
 // Routed-expert MLP of layer l on normed_ (the post-attention norm of
@@ -571,14 +771,7 @@ Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32
   cur_num_seqs_ = num_seqs;
   cur_max_len_ = max_len;
 
-  const int hd = cfg_.head_dim;
-  if (cfg_.mrope)
-    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cfg_.mrope_section[0],
-                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
-                                         sin_.as<float>(), st));
-  else
-    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), T, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
-                                      st));
+  B200_RETURN_IF(RopeTables(T));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), T, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
   launches_ = 2;  // rope table + embedding
   B200_RETURN_IF(RunLayers(T, false, 0));
@@ -598,14 +791,7 @@ Status DecoderModel::DecodeDevice(int batch) {
   B200_RETURN_IF(DecodePrepare(seq_slots_.as<int32_t>(), batch, ctx_lens_.as<int32_t>(), block_tables_.as<int32_t>(),
                                max_blocks_, opt_.block_size, pos_.as<int64_t>(), slots_.as<int64_t>(),
                                ctx_batch_.as<int32_t>(), bt_batch_.as<int32_t>(), err_, st));
-  const int hd = cfg_.head_dim;
-  if (cfg_.mrope)
-    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), batch, hd, cfg_.rope_theta, cfg_.mrope_section[0],
-                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
-                                         sin_.as<float>(), st));
-  else
-    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), batch, hd, cfg_.rope_theta, cos_.as<float>(),
-                                      sin_.as<float>(), st));
+  B200_RETURN_IF(RopeTables(batch));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), batch, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
   launches_ = 3;  // prepare + rope table + embedding
   B200_RETURN_IF(RunLayers(batch, true, batch));
@@ -617,6 +803,7 @@ Status DecoderModel::DecodeDevice(int batch) {
 Status DecoderModel::Decode(const int64_t* ids, bool ids_on_device, const int32_t* slots, int batch,
                             int64_t* next_tokens, bool next_on_device, void* logits) {
   if (!ids || !slots || !next_tokens || batch <= 0 || batch > opt_.max_batch) return ERROR_INVALID_PARAM;
+  B200_RETURN_IF(MlaAbsorb());  // absorbed projections after a weight change (outside any capture)
   std::set<int> seen;
   for (int i = 0; i < batch; ++i) {
     if (slots[i] < 0 || slots[i] >= opt_.max_batch || !seen.insert(slots[i]).second) return ERROR_INVALID_PARAM;
@@ -714,14 +901,7 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
   cur_num_seqs_ = 1;
   cur_max_len_ = (int)S;
 
-  const int hd = cfg_.head_dim;
-  if (cfg_.mrope)
-    B200_RETURN_IF(b200_rope_table_mrope(pos_.as<int64_t>(), S, hd, cfg_.rope_theta, cfg_.mrope_section[0],
-                                         cfg_.mrope_section[1], cfg_.mrope_section[2], cos_.as<float>(),
-                                         sin_.as<float>(), st));
-  else
-    B200_RETURN_IF(b200_rope_table_1d(pos_.as<int64_t>(), S, hd, cfg_.rope_theta, cos_.as<float>(), sin_.as<float>(),
-                                      st));
+  B200_RETURN_IF(RopeTables(S));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), S, embed_.data, cfg_.vocab, H, hidden_.data, st));
   launches_ = 2;
   if (n_vis) {

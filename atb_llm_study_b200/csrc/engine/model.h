@@ -38,6 +38,13 @@ struct ModelConfig {
   int experts = 0, top_k = 0, moe_intermediate = 0, shared_intermediate = 0, first_dense = 0;
   bool norm_topk = true;     // renormalise the chosen weights (else times routed_scale)
   float routed_scale = 1.0f;
+  // Multi-head latent attention (DeepSeek-V2 "deepseek_v2"): kv_lora > 0
+  // replaces GQA; rope over qk_rope dims with YaRN-scaled frequencies.
+  int kv_lora = 0, qk_nope = 0, qk_rope = 0, v_head = 0;
+  float yarn_factor = 1.f, yarn_orig_max = 4096.f, yarn_beta_fast = 32.f, yarn_beta_slow = 1.f;
+  float yarn_mscale = 1.f, yarn_mscale_all = 1.f;
+  float attn_scale = 0.f;  // softmax scale of the MLA heads
+  bool mla() const { return kv_lora > 0; }
 
   // Reads a HF config.json (Qwen3 "qwen3", the "text_config" of "qwen3_vl",
   // Mixtral "mixtral", Qwen3-MoE "qwen3_moe").
@@ -130,6 +137,20 @@ class DecoderModel {
   int64_t inject_n_ = 0;
 
   Status MoeBlock(int l, int64_t T, const void* next_norm);
+  Status MlaBlock(int l, int64_t T, bool decode, int batch, int* s_o);
+  Status MlaAbsorb();
+  Status RopeTables(int64_t T);
+
+  // MLA weights per layer: prefill projection [q (nh*192) ; kv_a (576)] x H,
+  // decode projection [absorbed q (nh*576) ; kv_a (576)] x H, kv_a RMSNorm,
+  // kv_b [nh*256, 512], absorbed output projection [H, nh*512] (wo_ holds the
+  // plain one); the latent cache [L][num_blocks*block_size][576]
+  DeviceTensor wq_, wqabs_, kvnorm_, wkvb_, woabs_, lat_;
+  DeviceTensor ckv_, kpe_, kvb_, kbuf_, mla_ws_;
+  int64_t mla_ws_bytes_ = 0;
+  bool absorb_dirty_ = true;
+  std::vector<float> inv_freq_;  // rope frequencies (YaRN for MLA)
+  float rope_mscale_ = 1.f;
 
   // weights (all layers stacked; dense MLPs over the dense layers only)
   DeviceTensor embed_, lm_head_, final_norm_;

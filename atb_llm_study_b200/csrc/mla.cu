@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "mla.h"
 
 using namespace b200;
 
@@ -450,6 +451,20 @@ __global__ void absorb_kernel(const __nv_bfloat16* __restrict__ A, int64_t a_sm,
   }
 }
 
+// kbuf[t, h, 0:128] = kvb[t, h*256 + 0:128]; kbuf[t, h, 128:192] = kpe[t, 0:64]
+__global__ void mla_build_k_kernel(const __nv_bfloat16* __restrict__ kvb, int64_t kvb_stride,
+                                   const __nv_bfloat16* __restrict__ kpe, __nv_bfloat16* __restrict__ kbuf, int nh) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t t = blockIdx.x;
+  for (int i = threadIdx.x; i < nh * 24; i += blockDim.x) {
+    const int h = i / 24, c = i % 24;  // 24 chunks of 8 per 192-wide head
+    const uint4 v = c < 16 ? *reinterpret_cast<const uint4*>(kvb + t * kvb_stride + (int64_t)h * 256 + c * 8)
+                           : *reinterpret_cast<const uint4*>(kpe + t * kRope + (c - 16) * 8);
+    *reinterpret_cast<uint4*>(kbuf + (t * nh + h) * 192 + c * 8) = v;
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -511,6 +526,16 @@ int mla_absorb(const void* A, int64_t a_sm, int64_t a_sk, int64_t a_z, const voi
   absorb_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A), a_sm, a_sk, a_z,
                                       static_cast<const __nv_bfloat16*>(B), b_sk, b_sn, b_z,
                                       static_cast<__nv_bfloat16*>(C), c_sm, c_sn, c_z, M, N, K);
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+int mla_build_k(const void* kvb, int64_t kvb_stride, const void* kpe, void* kbuf, int64_t T, int nh, cudaStream_t st) {
+  if (!kvb || !kpe || !kbuf || T < 0 || nh <= 0 || kvb_stride < (int64_t)nh * 256 || kvb_stride % 8 || !al16(kvb) ||
+      !al16(kpe) || !al16(kbuf))
+    return B200_ERROR_INVALID_PARAM;
+  if (T == 0) return B200_OK;
+  launch_kernel(mla_build_k_kernel, dim3((unsigned)T), 128, 0, st, static_cast<const __nv_bfloat16*>(kvb), kvb_stride,
+                static_cast<const __nv_bfloat16*>(kpe), static_cast<__nv_bfloat16*>(kbuf), nh);
   B200_CHECK_LAUNCH();
   return B200_OK;
 }

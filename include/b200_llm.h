@@ -393,6 +393,12 @@ enum b200_engine_query_key {
  * exact match first, then priority-ordered compatibility checks
  * (atb_cpp_llm/src/engine/model_registry.cpp:90-121). */
 B200_API int b200_engine_create(const b200_engine_config* config, b200_engine_t* out);
+
+/* Host function (no GPU): resolve and validate a config.json text the way
+ * b200_engine_create does, without allocating anything; the registry entry it
+ * resolves to is written to model_type (when not NULL).  Returns the status
+ * b200_engine_create would return for the config. */
+B200_API int b200_engine_config_check(const char* config_json, char* model_type, int model_type_len);
 B200_API int b200_engine_destroy(b200_engine_t engine);
 
 /* Load one weight by its HF name from host memory (dtype 0 = bf16, 1 = fp16,

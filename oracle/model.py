@@ -77,3 +77,28 @@ def embed_forward(ids, w, cfg, position_ids=None, vis_rows=None, vis_embeds=None
     if normalize:
         p = p / np.sqrt(np.sum(p * p) + np.float32(1e-12))
     return p.astype(np.float32), h
+
+
+def forward_last_logits_mla(ids, w, cfg):
+    """Logits of the last token of ``ids`` for a DeepSeek-V2-style model:
+    latent attention (oracle.mla, decompressed form) and dense or routed +
+    shared expert MLPs.  ``w`` layers carry q_w kva_w kv_norm kvb_w o_w iln_w
+    pln_w and either gate_w up_w down_w or router experts shared; ``cfg`` is an
+    oracle.mla config plus top_k, renorm, scale."""
+    from .layers import swiglu_mlp
+    from .mla import mla_attention
+    from .moe import moe_ffn
+
+    ids = np.asarray(ids, np.int64)
+    x = w["embed"][ids].astype(np.float32)
+    pos = np.arange(len(ids))
+    for lw in w["layers"]:
+        h = x + mla_attention(rms_norm(x, lw["iln_w"], cfg["eps"]), lw, pos, cfg)
+        n2 = rms_norm(h, lw["pln_w"], cfg["eps"])
+        if "experts" in lw:
+            m = moe_ffn(n2, lw["router"], lw["experts"], cfg["top_k"], cfg.get("renorm", False), cfg.get("scale", 1.0),
+                        lw.get("shared"))[0]
+        else:
+            m = swiglu_mlp(n2, lw["gate_w"], lw["up_w"], lw["down_w"])
+        x = h + m
+    return linear(rms_norm(x[-1:], w["norm"], cfg["eps"]), w["lm_head"])[0]
