@@ -271,6 +271,7 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
     const int64_t R = max_t_ * cfg.top_k;  // (token, choice) rows
     B200_RETURN_IF(A(topk_ids_, DType::INT32, {R}));
     B200_RETURN_IF(A(topk_w_, DType::FP32, {R}));
+    B200_RETURN_IF(A(rlogits_, DType::FP32, {max_t_, E}));
     B200_RETURN_IF(A(xperm_, DType::BF16, {R, H}));
     B200_RETURN_IF(A(eact_, DType::BF16, {R, Im}));
     B200_RETURN_IF(A(ey_, DType::BF16, {R, H}));
@@ -607,8 +608,13 @@ Status DecoderModel::MlaBlock(int l, int64_t T, bool decode, int batch, int* s_o
                                      gemm_ws_bytes_, st, s_o);
   }
   launches_ += 4 + (mla_ws_bytes_ > 0 ? 1 : 0);
+  int sq = 1;  // the query projection splits K at decode sizes; reduce before the latent preparation
   B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(wqabs_, (int64_t)l * NQD * H), H, q, NQD, T, NQD, H,
-                                   B200_EPI_NONE, nullptr, nullptr, 0, nullptr, 0, st, nullptr));
+                                   B200_EPI_NONE, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &sq));
+  if (sq > 1) {
+    ++launches_;
+    B200_RETURN_IF(b200::splitk_reduce(ws, sq, T, NQD, B200_EPI_NONE, nullptr, nullptr, 0, q, NQD, st));
+  }
   B200_RETURN_IF(b200_mla_prep(q, NQD, R + dr, (int)nh, (int)R, q + nh * (R + dr), NQD, bf(kvnorm_, l * R), cfg_.eps,
                                cos_.as<float>(), sin_.as<float>(), slots, lat, rows, nullptr, nullptr, T, st));
   B200_RETURN_IF(b200_mla_decode(q, NQD, lat, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(), batch,
@@ -661,9 +667,12 @@ Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm) {
   const int k = cfg_.top_k;
   const int64_t mi = moe_idx_[l], R = T * k;
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
-  launches_ += 1 + 4 + 2 + 1;  // route, permutation (count, scan, scatter, gather), 2 grouped GEMMs, combine
+  // route (logits + selection when few tokens), permutation (count, scan,
+  // scatter, gather), 2 grouped GEMMs, combine
+  launches_ += (T < 1024 ? 2 : 1) + 4 + 2 + 1;
   B200_RETURN_IF(b200_moe_route(normed_.data, H, bf(router_, mi * E * H), T, H, (int)E, k, cfg_.norm_topk ? 1 : 0,
-                                cfg_.routed_scale, topk_ids_.as<int32_t>(), topk_w_.as<float>(), nullptr, st));
+                                cfg_.routed_scale, topk_ids_.as<int32_t>(), topk_w_.as<float>(),
+                                rlogits_.as<float>(), st));
   B200_RETURN_IF(b200_moe_permute(topk_ids_.as<int32_t>(), T, k, (int)E, normed_.data, H, H, xperm_.data,
                                   eoff_.as<int32_t>(), ppos_.as<int32_t>(), psrc_.as<int32_t>(), pws_.data,
                                   pws_bytes_, st));

@@ -160,7 +160,7 @@ class DecoderModel {
   DeviceTensor router_, egu_, edown_, sgu_, sdown_;
   std::vector<int> dense_idx_, moe_idx_;  // per layer: index into the dense / MoE stacks (-1 = other kind)
   // MoE activations
-  DeviceTensor topk_ids_, topk_w_, xperm_, eact_, ey_, eoff_, ppos_, psrc_, pws_, sact_, sout_;
+  DeviceTensor topk_ids_, topk_w_, rlogits_, xperm_, eact_, ey_, eoff_, ppos_, psrc_, pws_, sact_, sout_;
   int64_t pws_bytes_ = 0;
   // KV cache [layers][2][num_blocks][kv_heads][block_size][head_dim]
   DeviceTensor kv_;

@@ -504,13 +504,30 @@ int num_sms() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
-// KV splits: enough (sequence, head group, split) CTAs for one per SM, each
-// split >= 4 tiles, at most 32.
+// KV splits.  One CTA fills an SM (172 KB of shared memory), so the time of a
+// launch is about (waves of CTAs) x (tiles per split); each extra split also
+// writes and combines a partial output.  Pick the split count minimising
+// waves * tiles_per_split + splits / 2 (e.g. batch 32 x 16 heads at context
+// 4096: 4 splits of 16 tiles, 128 CTAs in one wave, rather than 5 splits whose
+// 160 CTAs need a second, nearly empty wave).
 int mla_splits(int batch, int nh, int max_context) {
   const int64_t pairs = (int64_t)batch * (nh / 16);
-  const int max_split = std::max(1, std::min(32, (max_context + 4 * kTile - 1) / (4 * kTile)));
-  if (pairs >= num_sms()) return 1;
-  return (int)std::max<int64_t>(1, std::min<int64_t>((num_sms() + pairs - 1) / pairs, max_split));
+  const int64_t sms = num_sms();
+  const int ntiles = (max_context + kTile - 1) / kTile;
+  const int max_split = std::max(1, std::min(32, ntiles / 2));
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= max_split; ++s) {
+    const int tp = (ntiles + s - 1) / s;
+    const int eff = (ntiles + tp - 1) / tp;
+    const int64_t waves = (pairs * eff + sms - 1) / sms;
+    const double cost = (double)waves * tp + (eff > 1 ? 0.5 * eff : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = eff;
+    }
+  }
+  return best;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -348,10 +348,42 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Gate logits with one warp per (token, expert): the few-token (decode) form,
+// which keeps every SM busy where one CTA per token would leave most idle.
+__global__ void moe_gate_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                       const __nv_bfloat16* __restrict__ wg, int64_t T, int64_t H, int E,
+                                       float* __restrict__ logits) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= T * E) return;
+  const int64_t t = w / E;
+  const int e = (int)(w % E);
+  float acc = 0.f;
+  for (int64_t c = lane; c < H / 8; c += 32) {
+    float xv[8], wv[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + t * ldx + c * 8), xv);
+    unpack8(*reinterpret_cast<const uint4*>(wg + (int64_t)e * H + c * 8), wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf(xv[j], wv[j], acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) logits[t * E + e] = acc;
+}
+
 int route_launch(const void* x, int64_t ldx, const void* wg, const float* logits_in, int64_t T, int64_t H, int E,
                  int k, int renorm, float scale, int32_t* ids, float* wts, float* logits_out, cudaStream_t st) {
   auto xb = static_cast<const __nv_bfloat16*>(x);
   auto wb = static_cast<const __nv_bfloat16*>(wg);
+  if (!logits_in && logits_out && T < 1024) {
+    // few tokens: logits with a warp per (token, expert), then the selection from them
+    const int64_t warps = T * E;
+    launch_kernel(moe_gate_logits_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), 256, 0, st, xb, ldx, wb, T, H,
+                  E, logits_out);
+    B200_CHECK_LAUNCH();
+    return route_launch(nullptr, 0, nullptr, logits_out, T, H, E, k, renorm, scale, ids, wts, nullptr, st);
+  }
   // Accumulators per thread: experts (rounded up) x tokens per CTA.  Many
   // tokens: several per CTA, so the gate rows are read once for all of them;
   // few (decode): one per CTA, for more CTAs in flight.

@@ -455,6 +455,108 @@ def bench_mixtral(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
+DEEPSEEK_V2_LITE = dict(
+    model_type="deepseek_v2", hidden_size=2048, num_hidden_layers=27, num_attention_heads=16, num_key_value_heads=16,
+    q_lora_rank=None, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+    intermediate_size=10944, moe_intermediate_size=1408, n_routed_experts=64, num_experts_per_tok=6,
+    n_shared_experts=2, first_k_dense_replace=1, norm_topk_prob=False, routed_scaling_factor=1.0,
+    topk_method="greedy", scoring_func="softmax", moe_layer_freq=1, vocab_size=102400, rms_norm_eps=1e-6,
+    rope_theta=10000.0, tie_word_embeddings=False,
+    rope_scaling=dict(type="yarn", factor=40.0, original_max_position_embeddings=4096, beta_fast=32, beta_slow=1,
+                      mscale=0.707, mscale_all_dim=0.707))
+DS_BATCH, DS_CTX = 32, 4096
+
+
+def ds_decode_bytes():
+    """One decode step's algorithmic bytes, counted conservatively: the plain
+    (not absorbed) attention projections, the dense first layer, the routed
+    experts the 32 x 6 choices are expected to reach at uniform routing
+    (64 * (1 - (58/64)^32) = 61.27 of 64), the shared experts, the router,
+    lm_head, plus the latent cache of 32 x 4096 tokens.  The absorbed decode
+    projections this engine streams are larger (+0.6 GB a step), uncounted."""
+    H, nh, L = 2048, 16, 27
+    attn = H * nh * 192 + H * 576 + 512 + nh * 256 * 512 + H * nh * 128
+    dense = 3 * H * 10944
+    touched = 64 * (1 - (58 / 64) ** DS_BATCH)
+    moe = touched * 3 * H * 1408 + 3 * H * 2 * 1408 + 64 * H
+    weights = L * attn + dense + (L - 1) * moe + 102400 * H
+    cache = DS_BATCH * DS_CTX * L * 576
+    return 2 * (weights + cache)
+
+
+def bench_deepseek(L, torch, dev, steps, warm, stream_of):
+    """DeepSeek-V2-Lite on one GPU: decode batch 32 at context 4096 over the
+    latent cache (filled by real prefill calls), fresh random tokens each step."""
+    import numpy as np
+
+    max_ctx = DS_CTX + 2 * (warm + steps) + 16
+    cfg = EngineConfig(None, json.dumps(DEEPSEEK_V2_LITE).encode(), dev.index, DS_BATCH, max_ctx, 2 * DS_CTX, BLOCK,
+                       55, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create deepseek")
+    est = stream_of(eng)
+    try:
+        V = DEEPSEEK_V2_LITE["vocab_size"]
+        rng = np.random.default_rng(9)
+        nxt = torch.empty(DS_BATCH, dtype=torch.int64, device=dev)
+        lens = np.full(2, DS_CTX, np.int32)
+        t0 = time.perf_counter()
+        for g in range(DS_BATCH // 2):
+            ids = torch.from_numpy(rng.integers(0, V, 2 * DS_CTX).astype(np.int64)).to(dev)
+            slots = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, ids.data_ptr(), 1, lens.ctypes.data, slots.ctypes.data, 2, None,
+                                        nxt[2 * g:].data_ptr(), 1, None), "prefill ctx")
+        torch.cuda.synchronize(dev)
+        fill_s = time.perf_counter() - t0
+        slots_all = np.arange(DS_BATCH, dtype=np.int32)
+        feed_host = rng.integers(0, V, (warm + steps + 1, DS_BATCH)).astype(np.int64)
+        feed = torch.from_numpy(feed_host).to(dev)
+        out_d = torch.empty(DS_BATCH, dtype=torch.int64, device=dev)
+        host_next = np.zeros(DS_BATCH, np.int64)
+        counter = {"i": 0}
+
+        def decode(on_device):
+            i = counter["i"] % len(feed_host)
+            counter["i"] += 1
+            if on_device:
+                check(L.b200_engine_decode(eng, feed[i].data_ptr(), 1, slots_all.ctypes.data, DS_BATCH,
+                                           out_d.data_ptr(), 1, None), "decode")
+            else:
+                check(L.b200_engine_decode(eng, feed_host[i].ctypes.data, 0, slots_all.ctypes.data, DS_BATCH,
+                                           host_next.ctypes.data, 0, None), "decode")
+
+        def timed(on_device):
+            for _ in range(warm):
+                decode(on_device)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(est)
+            for _ in range(steps):
+                decode(on_device)
+            e1.record(est)
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1) / steps
+
+        dec_ms = timed(True)
+        e2e_ms = timed(False)
+        v = ctypes.c_int64()
+        check(L.b200_engine_query(eng, 2, ctypes.byref(v)), "query")
+        hbm, _, _, src = peaks()
+        nbytes = ds_decode_bytes()
+        return {
+            "workload": "DeepSeek-V2-Lite (15.7 B params, MLA kv_lora 512 + 64 routed experts top-6 + 2 shared) on "
+                        "one GPU: decode batch 32 at context 4096 over the latent cache",
+            "decode_tok_s": DS_BATCH / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+            "decode_e2e_tok_s": DS_BATCH / (e2e_ms / 1e3),
+            "decode_roofline": {"bound": "hbm", "bytes_per_step": nbytes, "achieved": nbytes / (dec_ms / 1e3) / 1e9,
+                                "peak": hbm, "unit": "GB/s", "frac": nbytes / (dec_ms / 1e3) / 1e9 / hbm,
+                                "peak_source": f"{src} copy"},
+            "prefill_fill_s": fill_s, "decode_launches_per_step": v.value,
+        }
+    finally:
+        L.b200_engine_destroy(eng)
+
+
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -587,6 +689,7 @@ def run_b200(args, rank, world, local_rank):
 
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+    ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
 
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
     pf_tok_s = world * T * steps / (pf_ms / 1e3)
@@ -636,6 +739,8 @@ def run_b200(args, rank, world, local_rank):
         result["qwen3vl_embedding"] = vl
     if mx:
         result["mixtral_8x7b"] = mx
+    if ds:
+        result["deepseek_v2_lite"] = ds
     if dist:
         dist.barrier()
     if rank == 0:
@@ -688,6 +793,8 @@ def main():
     ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
     ap.add_argument("--no-mixtral", action="store_true", help="skip the Mixtral-8x7B section")
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
+    ap.add_argument("--no-deepseek", action="store_true", help="skip the DeepSeek-V2-Lite section")
+    ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm"],
                     help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
@@ -710,7 +817,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.vl_only or args.mixtral_only:
+    if args.vl_only or args.mixtral_only or args.deepseek_only:
         import torch
 
         from atb_llm_study_b200 import capi
@@ -724,7 +831,7 @@ def main():
             check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
             return torch.cuda.ExternalStream(s.value, device=dev)
 
-        fn = bench_qwen3vl if args.vl_only else bench_mixtral
+        fn = bench_qwen3vl if args.vl_only else bench_mixtral if args.mixtral_only else bench_deepseek
         print(json.dumps(fn(L, torch, dev, args.steps, args.warmup, stream_of)), flush=True)
         return
     run_b200(args, rank, world, local_rank)
