@@ -230,6 +230,68 @@ def kernel_roofline_decode_attention(L, torch, dev, reps=20):
     return ms, algo
 
 
+def _time_launches(torch, dev, run, reps):
+    st = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        run(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for _ in range(reps):
+        run(st)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
+def kernel_roofline_mla_decode(L, torch, dev, reps=20):
+    """Absorbed-latent decode attention alone at the DeepSeek-V2-Lite decode
+    shape (batch 32, 16 heads, context 4096, block 128): algorithmic bytes =
+    the latent rows of every context token = 32*4096*576*2 B (+ q and out)."""
+    B, nh, ctx, blk = DS_BATCH, 16, DS_CTX, BLOCK
+    nbs = ctx // blk
+    nblk = B * nbs
+    g = torch.Generator(device=dev).manual_seed(3)
+    cache = (torch.randn(nblk * blk, 576, device=dev, generator=g)).to(torch.bfloat16)
+    tables = torch.randperm(nblk, device=dev, generator=g).to(torch.int32).reshape(B, nbs)
+    ctxl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = (torch.randn(B, nh * 576, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    out = torch.empty(B, nh * 512, dtype=torch.bfloat16, device=dev)
+    wsb = L.b200_mla_decode_workspace_bytes(B, nh, ctx)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+
+    def run(st):
+        check(L.b200_mla_decode(q.data_ptr(), nh * 576, cache.data_ptr(), tables.data_ptr(), nbs, ctxl.data_ptr(), B,
+                                nh, blk, nblk, 0.1, out.data_ptr(), nh * 512, ws.data_ptr(), wsb, ctx, st.cuda_stream),
+              "mla_decode")
+
+    ms = _time_launches(torch, dev, run, reps)
+    del cache
+    return ms, B * ctx * 576 * 2 + B * nh * (576 + 512) * 2
+
+
+def kernel_roofline_moe_gemm(L, torch, dev, reps=10):
+    """Grouped expert gate/up GEMM (SwiGLU epilogue) at the Mixtral-8x7B decode
+    shape: 64 (token, expert) rows over 8 experts of [2 x 14336, 4096]:
+    algorithmic bytes = every expert's weights = 8*28672*4096*2 B (+ tokens)."""
+    import numpy as np
+
+    E, N, K, rows = 8, 2 * 14336, 4096, 64
+    g = torch.Generator(device=dev).manual_seed(4)
+    W = (torch.randn(E * N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    A = torch.randn(rows, K, device=dev, generator=g).to(torch.bfloat16)
+    C = torch.empty(rows, N // 2, dtype=torch.bfloat16, device=dev)
+    off = torch.from_numpy(np.arange(0, rows + 1, rows // E, dtype=np.int32)).to(dev)
+
+    def run(st):
+        check(L.b200_grouped_gemm_bf16(A.data_ptr(), K, W.data_ptr(), K, C.data_ptr(), N // 2, off.data_ptr(), E, rows,
+                                       N, K, 3, st.cuda_stream), "grouped_gemm")
+
+    ms = _time_launches(torch, dev, run, reps)
+    del W
+    return ms, E * N * K * 2 + rows * K * 2 + rows * N // 2 * 2
+
+
 def kernel_roofline_prefill_gemm(L, torch, dev, reps=10):
     """gate/up projection with the fused SwiGLU epilogue at the prefill shape
     (M 16384, N 2 x 12288, K 4096): 2*M*N*K flops per launch."""
@@ -691,6 +753,19 @@ def run_b200(args, rank, world, local_rank):
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
 
+    def kernel_line(fn, name):
+        ms, nbytes = fn(L, torch, dev)
+        return {"kernel": name, "bound": "hbm", "ms": ms, "bytes_per_launch": nbytes,
+                "achieved": nbytes / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": nbytes / (ms / 1e3) / 1e9 / hbm, "peak_source": f"{src} copy bandwidth"}
+
+    if mx:
+        mx["kernel_roofline"] = kernel_line(kernel_roofline_moe_gemm,
+                                            "grouped expert gate/up GEMM + SwiGLU, 64 rows over 8 x [28672, 4096]")
+    if ds:
+        ds["kernel_roofline"] = kernel_line(kernel_roofline_mla_decode,
+                                            "mla_decode_kernel (+combine), batch 32 x 16 heads, context 4096")
+
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
     pf_tok_s = world * T * steps / (pf_ms / 1e3)
     result = {
@@ -795,7 +870,7 @@ def main():
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
     ap.add_argument("--no-deepseek", action="store_true", help="skip the DeepSeek-V2-Lite section")
     ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
-    ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm"],
+    ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "mla_decode", "moe_gemm"],
                     help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -809,8 +884,8 @@ def main():
         from atb_llm_study_b200 import capi
 
         dev = torch.device("cuda", local_rank)
-        fn = kernel_roofline_decode_attention if args.profile_kernel == "decode_attention" \
-            else kernel_roofline_prefill_gemm
+        fn = {"decode_attention": kernel_roofline_decode_attention, "prefill_gemm": kernel_roofline_prefill_gemm,
+              "mla_decode": kernel_roofline_mla_decode, "moe_gemm": kernel_roofline_moe_gemm}[args.profile_kernel]
         ms, work = fn(capi.lib(), torch, dev, reps=3)
         print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
         return
