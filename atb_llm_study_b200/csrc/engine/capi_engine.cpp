@@ -118,7 +118,7 @@ extern "C" int b200_engine_config_check(const char* config_json, char* model_typ
   return STATUS_OK;
 }
 
-extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* out) {
+static int create_engine(const b200_engine_config* c, b200_comm_t comm, b200_engine_t* out) {
   if (!c || !out) return ERROR_INVALID_PARAM;
   *out = nullptr;
   JsonConfig cfg;
@@ -144,6 +144,7 @@ extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* ou
   o.block_size = c->kv_block_size > 0 ? c->kv_block_size : 128;
   o.seed = c->init_seed;
   o.init_std = c->init_std > 0 ? c->init_std : 0.02f;
+  o.comm = comm;
   auto* e = new (std::nothrow) b200_engine_s();
   if (!e) return ERROR_DEVICE_MEMORY;
   s = e->model.Init(mc, o);
@@ -190,6 +191,15 @@ extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* ou
   }
   *out = e;
   return STATUS_OK;
+}
+
+extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* out) {
+  return create_engine(c, nullptr, out);
+}
+
+extern "C" int b200_engine_create_tp(const b200_engine_config* c, b200_comm_t comm, b200_engine_t* out) {
+  if (!comm) return ERROR_INVALID_PARAM;
+  return create_engine(c, comm, out);
 }
 
 extern "C" int b200_engine_destroy(b200_engine_t e) {

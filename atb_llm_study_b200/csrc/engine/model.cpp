@@ -132,12 +132,31 @@ DecoderModel::~DecoderModel() {
   ctx_.reset();
 }
 
-Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
-  cfg_ = cfg;
+Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
+  gcfg_ = whole;
   opt_ = opt;
   if (opt.max_batch <= 0 || opt.max_context <= 0 || opt.max_prefill_tokens <= 0 ||
       (opt.block_size != 64 && opt.block_size != 128))
     return ERROR_INVALID_PARAM;
+  // Tensor parallel: this rank keeps nq/P query heads (and the matching kv
+  // heads), I/P of the MLP width and V/P of the vocabulary; everything below
+  // sizes from that local view.
+  ModelConfig cfg = whole;
+  if (opt.comm) {
+    B200_RETURN_IF(b200_comm_info(opt.comm, &tp_, &tp_rank_, &tp_buf_[0], &tp_buf_[1], nullptr));
+    if (tp_ > 1) {
+      if (whole.mla() || whole.experts > 0 || whole.mrope) return ERROR_UNSUPPORTED;  // dense GQA models only
+      if (whole.heads % tp_ || whole.kv_heads % tp_ || whole.intermediate % tp_ || whole.vocab % tp_ ||
+          (whole.intermediate / tp_) % 8 || (whole.vocab / tp_) % 8 || whole.hidden > 8192)
+        return ERROR_UNSUPPORTED;
+      cfg.heads /= tp_;
+      cfg.kv_heads /= tp_;
+      cfg.intermediate /= tp_;
+      cfg.vocab /= tp_;
+      cfg.tie_embeddings = false;  // lm_head is this rank's vocabulary rows, the embedding stays whole
+    }
+  }
+  cfg_ = cfg;
   B200_RETURN_IF(ContextManager::Create(opt.device, ctx_));
   alloc_.reset(new TensorAllocator(ctx_->GetStream()));
   err_ = b200::error_word(opt.device);
@@ -151,11 +170,16 @@ Status DecoderModel::Init(const ModelConfig& cfg, const EngineOptions& opt) {
   const int64_t AO = mla ? nh * cfg.v_head : (int64_t)cfg.heads * hd;  // attention output fed to o_proj
   if (mla && opt.block_size % 64) return ERROR_INVALID_PARAM;
   max_t_ = std::max<int64_t>(opt.max_prefill_tokens, opt.max_batch);
+  if (tp_ > 1) {  // the partial sums of max_t_ rows must fit one symmetric buffer
+    int64_t bb = 0;
+    B200_RETURN_IF(b200_comm_info(opt.comm, nullptr, nullptr, nullptr, nullptr, &bb));
+    if (bb < max_t_ * H * 2) return ERROR_INVALID_PARAM;
+  }
   max_blocks_ = (opt.max_context + opt.block_size - 1) / opt.block_size;
   num_blocks_ = (int64_t)opt.max_batch * max_blocks_;
   auto A = [&](DeviceTensor& t, DType d, std::vector<int64_t> s) { return alloc_->Alloc(t, d, std::move(s)); };
 
-  B200_RETURN_IF(A(embed_, DType::BF16, {V, H}));
+  B200_RETURN_IF(A(embed_, DType::BF16, {gcfg_.vocab, H}));
   if (!cfg.tie_embeddings) B200_RETURN_IF(A(lm_head_, DType::BF16, {V, H}));
   else lm_head_ = embed_;
   B200_RETURN_IF(A(final_norm_, DType::BF16, {H}));
@@ -349,13 +373,33 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
                                             (size_t)numel * 2, cudaMemcpyHostToDevice, st)));
     return ctx_->Synchronize();
   };
+  // Tensor parallel: the whole tensor arrives; this rank keeps a block of rows
+  // (column-parallel q/k/v, gate/up, lm_head) or of columns (row-parallel o, down).
+  const int64_t P = tp_, rk = tp_rank_;
+  auto put_rows = [&](const DeviceTensor& t, int64_t elem_off, int64_t expect, int64_t rows_local,
+                      int64_t row_len) -> Status {
+    if (numel != expect) return ERROR_INVALID_PARAM;
+    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(static_cast<uint16_t*>(t.data) + elem_off,
+                                            b16.data() + rk * rows_local * row_len,
+                                            (size_t)(rows_local * row_len) * 2, cudaMemcpyHostToDevice, st)));
+    return ctx_->Synchronize();
+  };
+  auto put_cols = [&](const DeviceTensor& t, int64_t elem_off, int64_t rows, int64_t cols_local) -> Status {
+    if (numel != rows * cols_local * P) return ERROR_INVALID_PARAM;
+    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(static_cast<uint16_t*>(t.data) + elem_off, (size_t)cols_local * 2,
+                                              b16.data() + rk * cols_local, (size_t)cols_local * P * 2,
+                                              (size_t)cols_local * 2, (size_t)rows, cudaMemcpyHostToDevice, st)));
+    return ctx_->Synchronize();
+  };
   if (name == "model.embed_tokens.weight") {
-    Status s = put(embed_, 0, cfg_.vocab * H);
-    return s;
+    B200_RETURN_IF(put(embed_, 0, gcfg_.vocab * H));
+    if (gcfg_.tie_embeddings && !cfg_.tie_embeddings)  // tensor parallel: lm_head = this rank's rows
+      return put_rows(lm_head_, 0, gcfg_.vocab * H, cfg_.vocab, H);
+    return STATUS_OK;
   }
   if (name == "lm_head.weight") {
     if (cfg_.tie_embeddings) return STATUS_OK;
-    return put(lm_head_, 0, cfg_.vocab * H);
+    return put_rows(lm_head_, 0, gcfg_.vocab * H, cfg_.vocab, H);
   }
   if (name == "model.norm.weight") return put(final_norm_, 0, H);
   const std::string pre = "model.layers.";
@@ -379,27 +423,30 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
     return ERROR_WEIGHT_LOAD;
   }
   const int64_t nq = (int64_t)cfg_.heads * hd, nk = (int64_t)cfg_.kv_heads * hd;
-  if (leaf == "self_attn.q_proj.weight") return put(wqkv_, (int64_t)l * QKV * H, nq * H);
-  if (leaf == "self_attn.k_proj.weight") return put(wqkv_, (int64_t)l * QKV * H + nq * H, nk * H);
-  if (leaf == "self_attn.v_proj.weight") return put(wqkv_, (int64_t)l * QKV * H + (nq + nk) * H, nk * H);
-  if (leaf == "self_attn.o_proj.weight") return put(wo_, (int64_t)l * H * AO, H * AO);
+  if (leaf == "self_attn.q_proj.weight") return put_rows(wqkv_, (int64_t)l * QKV * H, nq * P * H, nq, H);
+  if (leaf == "self_attn.k_proj.weight") return put_rows(wqkv_, (int64_t)l * QKV * H + nq * H, nk * P * H, nk, H);
+  if (leaf == "self_attn.v_proj.weight")
+    return put_rows(wqkv_, (int64_t)l * QKV * H + (nq + nk) * H, nk * P * H, nk, H);
+  if (leaf == "self_attn.o_proj.weight") return put_cols(wo_, (int64_t)l * H * AO, H, AO);
   if (leaf == "self_attn.q_norm.weight") return put(qnorm_, (int64_t)l * hd, hd);
   if (leaf == "self_attn.k_norm.weight") return put(knorm_, (int64_t)l * hd, hd);
   if (leaf == "input_layernorm.weight") return put(iln_, (int64_t)l * H, H);
   if (leaf == "post_attention_layernorm.weight") return put(pln_, (int64_t)l * H, H);
-  // rows 2j / 2j+1 of a fused gate/up matrix hold gate[j] / up[j] (SwiGLU epilogue layout)
-  auto put_interleaved = [&](const DeviceTensor& t, int64_t elem_off, int64_t inter, bool up) -> Status {
-    if (numel != inter * H) return ERROR_INVALID_PARAM;
+  // rows 2j / 2j+1 of a fused gate/up matrix hold gate[j] / up[j] (SwiGLU epilogue layout);
+  // `inter` rows of the source starting at row src_row
+  auto put_interleaved = [&](const DeviceTensor& t, int64_t elem_off, int64_t inter, bool up,
+                             int64_t src_row = 0, int64_t parts = 1) -> Status {
+    if (numel != inter * parts * H) return ERROR_INVALID_PARAM;
     uint16_t* dst = static_cast<uint16_t*>(t.data) + elem_off + (up ? H : 0);
-    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(dst, (size_t)2 * H * 2, b16.data(), (size_t)H * 2, (size_t)H * 2,
-                                              (size_t)inter, cudaMemcpyHostToDevice, st)));
+    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(dst, (size_t)2 * H * 2, b16.data() + src_row * H, (size_t)H * 2,
+                                              (size_t)H * 2, (size_t)inter, cudaMemcpyHostToDevice, st)));
     return ctx_->Synchronize();
   };
   const int di = dense_idx_[l], mi = moe_idx_[l];
   if (di >= 0) {
-    if (leaf == "mlp.down_proj.weight") return put(wdown_, (int64_t)di * H * I, H * I);
+    if (leaf == "mlp.down_proj.weight") return put_cols(wdown_, (int64_t)di * H * I, H, I);
     if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight")
-      return put_interleaved(wgu_, (int64_t)di * 2 * I * H, I, leaf[4] == 'u');
+      return put_interleaved(wgu_, (int64_t)di * 2 * I * H, I, leaf[4] == 'u', rk * I, P);
     return ERROR_WEIGHT_LOAD;
   }
   // MoE layer: Mixtral "block_sparse_moe.{gate, experts.E.w1/w3/w2}", Qwen3-MoE /
@@ -505,9 +552,26 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
                                        batch, nq, nkv, (int)hd, opt_.block_size, num_blocks_, scale, attn_.data, AO,
                                        attn_ws_.data, attn_ws_bytes_, opt_.max_context, st));
     }
+    if (tp_ > 1) {  // row-parallel o: partial sums, all-reduced with the residual and the post-attention norm
+      B200_RETURN_IF(TpProject(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), T, decode, 0, bf(pln_, (int64_t)l * H)));
+    } else {
     B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, H, AO, B200_EPI_RESIDUAL,
                         hidden_.data, H, &s_o));
+    }
     }  // GQA attention
+    if (tp_ > 1) {
+      // MLP: column-parallel gate/up, row-parallel down, all-reduce fused with the next input norm
+      const int64_t dl = dense_idx_[l];
+      B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, dl * 2 * I * H), H, act_.data, I, 2 * I, H, B200_EPI_SWIGLU,
+                          nullptr, 0, &s_gu));
+      if (s_gu > 1) {
+        ++launches_;
+        B200_RETURN_IF(b200::splitk_reduce(ws, s_gu, T, 2 * I, B200_EPI_SWIGLU, nullptr, nullptr, 0, act_.data, I, st));
+      }
+      B200_RETURN_IF(TpProject(act_.data, I, bf(wdown_, dl * H * I), T, decode, 1,
+                               l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr));
+      continue;
+    }
     ++launches_;
     if (s_o > 1)  // hidden += sum(partials); normed = rmsnorm(hidden)
       B200_RETURN_IF(b200::splitk_residual_rmsnorm(ws, s_o, T, H, hidden_.data, bf(pln_, (int64_t)l * H),
@@ -558,6 +622,36 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     }
   }
   return STATUS_OK;
+}
+
+// Row-parallel projection of this rank's K columns: partial = A W^T into the
+// group's buffer `parity`, then hidden += (sum over ranks) and normed =
+// RMSNorm(hidden) * norm_w (skipped when norm_w is null).  Decode-sized calls
+// use the fused peer-memory all-reduce (capturable in the decode graph);
+// prefill-sized ones NCCL followed by the residual + RMSNorm kernel.
+Status DecoderModel::TpProject(const void* A, int64_t K, const void* W, int64_t T, bool decode, int parity,
+                               const void* norm_w) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden;
+  void* buf = tp_buf_[parity];
+  float* ws = gemm_ws_.as<float>();
+  int s = 1;
+  ++launches_;
+  B200_RETURN_IF(b200::gemm_launch(A, K, W, K, buf, H, T, H, K, B200_EPI_NONE, nullptr, nullptr, 0, ws, gemm_ws_bytes_,
+                                   st, &s));
+  if (s > 1) {
+    ++launches_;
+    B200_RETURN_IF(b200::splitk_reduce(ws, s, T, H, B200_EPI_NONE, nullptr, nullptr, 0, buf, H, st));
+  }
+  ++launches_;
+  if (decode || T <= 256)
+    return (Status)b200_comm_allreduce_rmsnorm(opt_.comm, parity, T, H, hidden_.data, norm_w,
+                                               norm_w ? normed_.data : nullptr, cfg_.eps, st);
+  B200_RETURN_IF(b200_comm_allreduce_bf16(opt_.comm, buf, T * H, st));
+  // hidden = sum + hidden; normed = RMSNorm(hidden) (the final norm's weight stands in when no norm follows:
+  // that normed output is then unused)
+  return (Status)b200_rmsnorm(buf, hidden_.data, norm_w ? norm_w : final_norm_.data, normed_.data, hidden_.data, T,
+                              H, H, cfg_.eps, st);
 }
 
 Status DecoderModel::RopeTables(int64_t T) {
@@ -723,8 +817,13 @@ Status DecoderModel::Head(int64_t rows, bool gather, int64_t* next_tokens, bool 
     B200_RETURN_IF(b200::splitk_reduce(gemm_ws_.as<float>(), splits, rows, V, B200_EPI_NONE, nullptr, nullptr, 0,
                                        logits_.data, V, st));
   }
-  ++launches_;
-  B200_RETURN_IF(b200_argmax(logits_.data, rows, V, V, next_.as<int64_t>(), st));
+  if (tp_ > 1) {  // vocabulary-parallel: local argmax, exchanged over the group
+    launches_ += 2;
+    B200_RETURN_IF(b200_comm_argmax(opt_.comm, logits_.data, rows, V, V, next_.as<int64_t>(), st));
+  } else {
+    ++launches_;
+    B200_RETURN_IF(b200_argmax(logits_.data, rows, V, V, next_.as<int64_t>(), st));
+  }
   (void)next_tokens;
   (void)next_on_device;
   (void)logits;
@@ -781,7 +880,7 @@ Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32
   cur_max_len_ = max_len;
 
   B200_RETURN_IF(RopeTables(T));
-  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), T, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), T, embed_.data, gcfg_.vocab, cfg_.hidden, hidden_.data, st));
   launches_ = 2;  // rope table + embedding
   B200_RETURN_IF(RunLayers(T, false, 0));
   B200_RETURN_IF(Head(num_seqs, true, next_tokens, next_on_device, logits));
@@ -801,7 +900,7 @@ Status DecoderModel::DecodeDevice(int batch) {
                                max_blocks_, opt_.block_size, pos_.as<int64_t>(), slots_.as<int64_t>(),
                                ctx_batch_.as<int32_t>(), bt_batch_.as<int32_t>(), err_, st));
   B200_RETURN_IF(RopeTables(batch));
-  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), batch, embed_.data, cfg_.vocab, cfg_.hidden, hidden_.data, st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), batch, embed_.data, gcfg_.vocab, cfg_.hidden, hidden_.data, st));
   launches_ = 3;  // prepare + rope table + embedding
   B200_RETURN_IF(RunLayers(batch, true, batch));
   B200_RETURN_IF(Head(batch, false, nullptr, true, nullptr));
@@ -911,7 +1010,7 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
   cur_max_len_ = (int)S;
 
   B200_RETURN_IF(RopeTables(S));
-  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), S, embed_.data, cfg_.vocab, H, hidden_.data, st));
+  B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), S, embed_.data, gcfg_.vocab, H, hidden_.data, st));
   launches_ = 2;
   if (n_vis) {
     ++launches_;

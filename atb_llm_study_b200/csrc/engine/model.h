@@ -1,4 +1,6 @@
-// Dense GQA decoder model runner (Qwen3 and the Qwen3-VL text decoder).
+// Decoder model runner: GQA or multi-head latent attention, dense or
+// mixture-of-experts MLPs (Qwen3, the Qwen3-VL text decoder, Qwen3-MoE,
+// Mixtral, DeepSeek-V2), on one GPU or tensor-parallel over a b200_comm_t.
 //
 // Replaces the reference's per-model layer graph + runner + layer loop
 // (TextDecoderLayerGraph::Build, atb_cpp_llm/src/components/text/
@@ -62,6 +64,7 @@ struct EngineOptions {
   int block_size = 128;
   uint64_t seed = 0;
   float init_std = 0.02f;
+  b200_comm_t comm = nullptr;  // tensor-parallel group (null: one GPU)
 };
 
 class DecoderModel {
@@ -119,7 +122,11 @@ class DecoderModel {
     return static_cast<uint16_t*>(t.data) + (int64_t)l * per_layer_elems;
   }
 
-  ModelConfig cfg_;
+  ModelConfig cfg_;   // this rank's view (heads, kv heads, intermediate, vocab divided by tp_)
+  ModelConfig gcfg_;  // the whole model
+  int tp_ = 1, tp_rank_ = 0;
+  void* tp_buf_[2] = {nullptr, nullptr};  // this rank's partial-sum buffers in the group's symmetric memory
+  Status TpProject(const void* A, int64_t K, const void* W, int64_t T, bool decode, int parity, const void* norm_w);
   EngineOptions opt_;
   std::unique_ptr<ContextManager> ctx_;
   std::unique_ptr<TensorAllocator> alloc_;

@@ -351,6 +351,45 @@ B200_API int b200_scatter_add_rows(void* hidden, int64_t rows, int64_t dim, cons
 /* out[r] = argmax_j logits[r, j] (lowest index on ties), logits [rows, vocab] bf16. */
 B200_API int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t ld, int64_t* out, b200_stream_t stream);
 
+/* --------------------------------------------------------- tensor parallel */
+
+/* A tensor-parallel group of `world` (<= 8) processes, one GPU each: an NCCL
+ * communicator for large all-reduces and a symmetric device buffer that every
+ * rank maps over NVLink (CUDA IPC) for the fused decode-sized ones.
+ * Bootstrap: rank 0 calls b200_comm_unique_id and shares the 128 bytes;
+ * every rank calls b200_comm_create (collective), shares its 64-byte
+ * b200_comm_ipc_handle, then calls b200_comm_connect with all ranks' handles
+ * concatenated in rank order.  No reference counterpart: the reference runs
+ * on one device (SURVEY's TP rows for Qwen3-8B are new). */
+typedef struct b200_comm_s* b200_comm_t;
+B200_API int b200_comm_unique_id(void* nccl_id_out);
+B200_API int b200_comm_create(int world, int rank, int device, const void* nccl_id, int64_t symmetric_bytes,
+                              b200_comm_t* out);
+B200_API int b200_comm_ipc_handle(b200_comm_t comm, void* handle_out);
+B200_API int b200_comm_connect(b200_comm_t comm, const void* all_handles);
+B200_API int b200_comm_destroy(b200_comm_t comm);
+/* world, rank, and this rank's two partial-sum buffers (parity 0 / 1) of buffer_bytes each. */
+B200_API int b200_comm_info(b200_comm_t comm, int* world, int* rank, void** buffer0, void** buffer1,
+                            int64_t* buffer_bytes);
+/* In-place sum over the group (NCCL, bf16). */
+B200_API int b200_comm_allreduce_bf16(b200_comm_t comm, void* buf, int64_t count, b200_stream_t stream);
+/* recv [world * count] = every rank's send [count] in rank order (NCCL, bf16). */
+B200_API int b200_comm_allgather_bf16(b200_comm_t comm, const void* send, void* recv, int64_t count,
+                                      b200_stream_t stream);
+/* Fused decode all-reduce: each rank's partial rows [T, H] already sit in its
+ * buffer `parity`; every rank computes hidden[t] += sum over ranks (rank order,
+ * fp32, identical on all ranks) and, when norm_weight is not NULL, normed[t] =
+ * RMSNorm(hidden[t]) * norm_weight — reading the peers' partials over NVLink,
+ * with a bounded wait on the peers' epoch flags (timeouts set the device error
+ * word).  Consecutive calls must alternate parity. */
+B200_API int b200_comm_allreduce_rmsnorm(b200_comm_t comm, int parity, int64_t T, int64_t H, void* hidden,
+                                         const void* norm_weight, void* normed, float eps, b200_stream_t stream);
+/* Vocabulary-parallel greedy token: logits [rows, vocab_local] (row stride ld)
+ * are this rank's shard (rank r holds global ids r*vocab_local ..); out[rows]
+ * = the global argmax (lowest id on ties), identical on every rank. */
+B200_API int b200_comm_argmax(b200_comm_t comm, const void* logits, int64_t rows, int64_t vocab_local, int64_t ld,
+                              int64_t* out, b200_stream_t stream);
+
 /* ----------------------------------------------------------------- engine */
 
 /* A decoder model on one GPU: weights, a paged KV cache of max_batch slots x
@@ -393,6 +432,16 @@ enum b200_engine_query_key {
  * exact match first, then priority-ordered compatibility checks
  * (atb_cpp_llm/src/engine/model_registry.cpp:90-121). */
 B200_API int b200_engine_create(const b200_engine_config* config, b200_engine_t* out);
+
+/* Tensor-parallel engine over `comm` (dense GQA models): rank r holds heads
+ * [r*nq/P, (r+1)*nq/P) (and the matching kv heads), rows r*I/P.. of gate/up,
+ * the matching columns of o/down, vocabulary rows r*V/P.. of lm_head; two
+ * all-reduces per layer (fused with residual + RMSNorm for decode-sized
+ * batches, NCCL for prefill), a vocabulary-parallel argmax.  Weights are
+ * given whole through b200_engine_set_weight and sliced on the host.  Every
+ * rank must make the same prefill/decode calls in the same order; `logits`
+ * outputs receive this rank's vocabulary shard [rows, V/P]. */
+B200_API int b200_engine_create_tp(const b200_engine_config* config, b200_comm_t comm, b200_engine_t* out);
 
 /* Host function (no GPU): resolve and validate a config.json text the way
  * b200_engine_create does, without allocating anything; the registry entry it
