@@ -619,6 +619,91 @@ def bench_deepseek(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
+def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
+    """Qwen3-8B tensor-parallel over all ranks: the same decode (batch 64 at
+    context 2048) and prefill (8 x 2048) as the replica headline, one model
+    sharded P ways; two all-reduces per layer (fused peer-memory kernel for
+    decode, NCCL for prefill).  Timed with CUDA events, max over ranks."""
+    import numpy as np
+
+    uid = ctypes.create_string_buffer(128)
+    if rank == 0:
+        check(L.b200_comm_unique_id(uid), "comm_unique_id")
+    box = [uid.raw]
+    dist.broadcast_object_list(box, src=0)
+    uid = ctypes.create_string_buffer(box[0], 128)
+    T = PREFILL_SEQS * PREFILL_LEN
+    sym = 2 * T * QWEN3_8B["hidden_size"] * 2 + (16 << 20)
+    comm = ctypes.c_void_p()
+    check(L.b200_comm_create(world, rank, dev.index, uid, sym, ctypes.byref(comm)), "comm_create")
+    h = ctypes.create_string_buffer(64)
+    check(L.b200_comm_ipc_handle(comm, h), "comm_ipc_handle")
+    hs = [None] * world
+    dist.all_gather_object(hs, h.raw)
+    check(L.b200_comm_connect(comm, ctypes.create_string_buffer(b"".join(hs), 64 * world)), "comm_connect")
+    max_ctx = DECODE_CTX + warm + steps + 16
+    cfg = EngineConfig(None, json.dumps(QWEN3_8B).encode(), dev.index, DECODE_BATCH, max_ctx, T, BLOCK, 4321, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create_tp(ctypes.byref(cfg), comm, ctypes.byref(eng)), "engine_create_tp")
+    est = stream_of(eng)
+    try:
+        V = QWEN3_8B["vocab_size"]
+        rng = np.random.default_rng(2)  # the same prompts on every rank
+        lens = np.full(PREFILL_SEQS, PREFILL_LEN, np.int32)
+        groups = DECODE_BATCH // PREFILL_SEQS
+        ids = [torch.from_numpy(rng.integers(0, V, T).astype(np.int64)).to(dev) for _ in range(groups)]
+        nxt = torch.empty(DECODE_BATCH, dtype=torch.int64, device=dev)
+
+        def prefill(i):
+            g = i % groups
+            slots = np.arange(g * PREFILL_SEQS, (g + 1) * PREFILL_SEQS, dtype=np.int32)
+            check(L.b200_engine_prefill(eng, ids[g].data_ptr(), 1, lens.ctypes.data, slots.ctypes.data,
+                                        PREFILL_SEQS, None, nxt[g * PREFILL_SEQS:].data_ptr(), 1, None), "prefill")
+
+        def timed(fn, n):
+            for i in range(warm):
+                fn(i)
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(est)
+            for i in range(n):
+                fn(i)
+            e1.record(est)
+            torch.cuda.synchronize(dev)
+            t = torch.tensor([e0.elapsed_time(e1) / n], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        pf_ms = timed(prefill, max(1, min(steps, 3)))
+        check(L.b200_engine_reset(eng), "reset")
+        for g in range(groups):
+            prefill(g)
+        slots_all = np.arange(DECODE_BATCH, dtype=np.int32)
+        state = {"a": nxt.clone(), "b": torch.empty_like(nxt)}
+
+        def decode(_):
+            check(L.b200_engine_decode(eng, state["a"].data_ptr(), 1, slots_all.ctypes.data, DECODE_BATCH,
+                                       state["b"].data_ptr(), 1, None), "decode")
+            state["a"], state["b"] = state["b"], state["a"]
+
+        dec_ms = timed(decode, steps)
+        v = ctypes.c_int64()
+        check(L.b200_engine_query(eng, 2, ctypes.byref(v)), "query")
+        errs = ctypes.c_uint(0)
+        check(L.b200_device_error_read(ctypes.addressof(errs), 1, None), "device_error_read")
+        return {"tp": world, "decode_tok_s": DECODE_BATCH / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+                "prefill_tok_s": T / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
+                "decode_launches_per_step": v.value, "device_errors": errs.value,
+                "note": "one Qwen3-8B sharded over all ranks (latency-oriented); the headline `value` is "
+                        "independent replicas (throughput-oriented)"}
+    finally:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        L.b200_engine_destroy(eng)
+        L.b200_comm_destroy(comm)
+
+
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -749,6 +834,9 @@ def run_b200(args, rank, world, local_rank):
         check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
         return torch.cuda.ExternalStream(s.value, device=dev)
 
+    tp = None
+    if dist and not args.no_tp:
+        tp = bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of)
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
@@ -810,6 +898,8 @@ def run_b200(args, rank, world, local_rank):
                              f"{prefill_launches}",
         "clocks": clocks,
     }
+    if tp:
+        result["tensor_parallel"] = tp
     if vl:
         result["qwen3vl_embedding"] = vl
     if mx:
@@ -865,6 +955,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-vl", action="store_true", help="skip the Qwen3-VL-2B embedding section")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel Qwen3-8B section (N > 1)")
     ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
     ap.add_argument("--no-mixtral", action="store_true", help="skip the Mixtral-8x7B section")
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
