@@ -145,14 +145,20 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
   if (opt.comm) {
     B200_RETURN_IF(b200_comm_info(opt.comm, &tp_, &tp_rank_, &tp_buf_[0], &tp_buf_[1], nullptr));
     if (tp_ > 1) {
-      if (whole.mla() || whole.experts > 0 || whole.mrope) return ERROR_UNSUPPORTED;  // dense GQA models only
+      // GQA attention (dense or mixture-of-experts MLPs; an expert's width is split like a dense MLP's)
+      if (whole.mla() || whole.mrope) return ERROR_UNSUPPORTED;
       if (whole.heads % tp_ || whole.kv_heads % tp_ || whole.intermediate % tp_ || whole.vocab % tp_ ||
           (whole.intermediate / tp_) % 8 || (whole.vocab / tp_) % 8 || whole.hidden > 8192)
+        return ERROR_UNSUPPORTED;
+      if (whole.experts > 0 && (whole.moe_intermediate % tp_ || (whole.moe_intermediate / tp_) % 8 ||
+                                whole.shared_intermediate % tp_ || (whole.shared_intermediate / tp_) % 8))
         return ERROR_UNSUPPORTED;
       cfg.heads /= tp_;
       cfg.kv_heads /= tp_;
       cfg.intermediate /= tp_;
       cfg.vocab /= tp_;
+      cfg.moe_intermediate /= tp_;
+      cfg.shared_intermediate /= tp_;
       cfg.tie_embeddings = false;  // lm_head is this rank's vocabulary rows, the embedding stays whole
     }
   }
@@ -459,9 +465,9 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
   if (m == "gate.weight") return put(router_, (int64_t)mi * E * H, E * H);
   if (starts_with(m, "shared_experts.") && Is > 0) {
     const std::string s = m.substr(15);
-    if (s == "down_proj.weight") return put(sdown_, (int64_t)mi * H * Is, H * Is);
+    if (s == "down_proj.weight") return put_cols(sdown_, (int64_t)mi * H * Is, H, Is);
     if (s == "gate_proj.weight" || s == "up_proj.weight")
-      return put_interleaved(sgu_, (int64_t)mi * 2 * Is * H, Is, s[0] == 'u');
+      return put_interleaved(sgu_, (int64_t)mi * 2 * Is * H, Is, s[0] == 'u', rk * Is, P);
     return ERROR_WEIGHT_LOAD;
   }
   if (!starts_with(m, "experts.")) return ERROR_WEIGHT_LOAD;
@@ -471,9 +477,10 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
   if (e < 0 || e >= E) return ERROR_WEIGHT_LOAD;
   const std::string w = m.substr(d2 + 1);
   const int64_t ge = (int64_t)mi * E + e;  // expert slot in the MoE stacks
-  if (w == "w2.weight" || w == "down_proj.weight") return put(edown_, ge * H * Im, H * Im);
-  if (w == "w1.weight" || w == "gate_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, false);
-  if (w == "w3.weight" || w == "up_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, true);
+  if (w == "w2.weight" || w == "down_proj.weight") return put_cols(edown_, ge * H * Im, H, Im);
+  if (w == "w1.weight" || w == "gate_proj.weight")
+    return put_interleaved(egu_, ge * 2 * Im * H, Im, false, rk * Im, P);
+  if (w == "w3.weight" || w == "up_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, true, rk * Im, P);
   return ERROR_WEIGHT_LOAD;
 }
 
@@ -560,6 +567,10 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     }
     }  // GQA attention
     if (tp_ > 1) {
+      if (cfg_.moe_layer(l)) {  // experts split like dense MLPs; the combine's partial sum is all-reduced
+        B200_RETURN_IF(MoeBlock(l, T, l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr, decode));
+        continue;
+      }
       // MLP: column-parallel gate/up, row-parallel down, all-reduce fused with the next input norm
       const int64_t dl = dense_idx_[l];
       B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, dl * 2 * I * H), H, act_.data, I, 2 * I, H, B200_EPI_SWIGLU,
@@ -581,7 +592,7 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
                                   cfg_.eps, st));
     const void* next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
     if (cfg_.moe_layer(l)) {  // routed experts; the combine adds the residual and applies the next norm
-      B200_RETURN_IF(MoeBlock(l, T, next_norm));
+      B200_RETURN_IF(MoeBlock(l, T, next_norm, decode));
       continue;
     }
     // MLP block
@@ -643,6 +654,17 @@ Status DecoderModel::TpProject(const void* A, int64_t K, const void* W, int64_t 
     ++launches_;
     B200_RETURN_IF(b200::splitk_reduce(ws, s, T, H, B200_EPI_NONE, nullptr, nullptr, 0, buf, H, st));
   }
+  return TpReduce(T, decode, parity, norm_w);
+}
+
+// hidden += the group's sum of the partials in buffer `parity`; normed =
+// RMSNorm(hidden) * norm_w (skipped when norm_w is null).  Decode-sized calls
+// use the fused peer-memory all-reduce (capturable in the decode graph);
+// prefill-sized ones NCCL followed by the residual + RMSNorm kernel.
+Status DecoderModel::TpReduce(int64_t T, bool decode, int parity, const void* norm_w) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden;
+  void* buf = tp_buf_[parity];
   ++launches_;
   if (decode || T <= 256)
     return (Status)b200_comm_allreduce_rmsnorm(opt_.comm, parity, T, H, hidden_.data, norm_w,
@@ -755,7 +777,7 @@ Status DecoderModel::MlaAbsorb() {
 // hidden_): router -> permutation -> grouped gate/up (SwiGLU) -> grouped down
 // -> weighted combine + shared expert + residual into hidden_, with the next
 // layer's input norm fused into the combine.
-Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm) {
+Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm, bool decode) {
   cudaStream_t st = ctx_->GetStream();
   const int64_t H = cfg_.hidden, E = cfg_.experts, Im = cfg_.moe_intermediate, Is = cfg_.shared_intermediate;
   const int k = cfg_.top_k;
@@ -792,6 +814,11 @@ Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm) {
       B200_RETURN_IF(b200::splitk_reduce(ws, s2, T, H, B200_EPI_NONE, nullptr, nullptr, 0, sout_.data, H, st));
     }
     shared = sout_.data;
+  }
+  if (tp_ > 1) {  // this rank's share of every expert (and of the shared expert): all-reduce the combined sum
+    B200_RETURN_IF(b200_moe_combine(ey_.data, ppos_.as<int32_t>(), topk_w_.as<float>(), T, k, H, nullptr, shared,
+                                    tp_buf_[1], nullptr, nullptr, cfg_.eps, st));
+    return TpReduce(T, decode, 1, next_norm);
   }
   return (Status)b200_moe_combine(ey_.data, ppos_.as<int32_t>(), topk_w_.as<float>(), T, k, H, hidden_.data, shared,
                                   hidden_.data, next_norm, next_norm ? normed_.data : nullptr, cfg_.eps, st);

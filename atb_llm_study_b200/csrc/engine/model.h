@@ -127,6 +127,7 @@ class DecoderModel {
   int tp_ = 1, tp_rank_ = 0;
   void* tp_buf_[2] = {nullptr, nullptr};  // this rank's partial-sum buffers in the group's symmetric memory
   Status TpProject(const void* A, int64_t K, const void* W, int64_t T, bool decode, int parity, const void* norm_w);
+  Status TpReduce(int64_t T, bool decode, int parity, const void* norm_w);
   EngineOptions opt_;
   std::unique_ptr<ContextManager> ctx_;
   std::unique_ptr<TensorAllocator> alloc_;
@@ -143,7 +144,7 @@ class DecoderModel {
   std::vector<const void*> inject_feats_;
   int64_t inject_n_ = 0;
 
-  Status MoeBlock(int l, int64_t T, const void* next_norm);
+  Status MoeBlock(int l, int64_t T, const void* next_norm, bool decode);
   Status MlaBlock(int l, int64_t T, bool decode, int batch, int* s_o);
   Status MlaAbsorb();
   Status RopeTables(int64_t T);

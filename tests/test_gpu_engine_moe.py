@@ -56,38 +56,38 @@ def make_weights(C, seed):
     return w
 
 
+def weight_items(C, w):
+    """(HF name, fp32 array) of every weight of the model, in the checkpoint's naming."""
+    yield "model.embed_tokens.weight", w["embed"]
+    yield "lm_head.weight", w["lm_head"]
+    yield "model.norm.weight", w["norm"]
+    mix = C["model_type"] == "mixtral"
+    for i, lw in enumerate(w["layers"]):
+        p = f"model.layers.{i}."
+        for k, nm in (("q_w", "q_proj"), ("k_w", "k_proj"), ("v_w", "v_proj"), ("o_w", "o_proj")):
+            yield p + f"self_attn.{nm}.weight", lw[k]
+        if "qn_w" in lw:
+            yield p + "self_attn.q_norm.weight", lw["qn_w"]
+            yield p + "self_attn.k_norm.weight", lw["kn_w"]
+        yield p + "input_layernorm.weight", lw["iln_w"]
+        yield p + "post_attention_layernorm.weight", lw["pln_w"]
+        m = p + ("block_sparse_moe." if mix else "mlp.")
+        yield m + "gate.weight", lw["router"]
+        for e, ew in enumerate(lw["experts"]):
+            names = (("gate_w", "w1"), ("up_w", "w3"), ("down_w", "w2")) if mix else \
+                (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj"))
+            for k, nm in names:
+                yield m + f"experts.{e}.{nm}.weight", ew[k]
+
+
 def create(C, w, max_batch=8):
     L = G.L()
     cfg = EngineConfig(None, json.dumps(C).encode(), 0, max_batch, 256, 512, 128, 5, 0.02)
     eng = ctypes.c_void_p()
     G.check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create")
-    held = []
-
-    def put(name, a):
+    for name, a in weight_items(C, w):
         a = np.ascontiguousarray(a, np.float32)
-        held.append(a)
         G.check(L.b200_engine_set_weight(eng, name.encode(), a.ctypes.data, 2, a.size), name)
-
-    put("model.embed_tokens.weight", w["embed"])
-    put("lm_head.weight", w["lm_head"])
-    put("model.norm.weight", w["norm"])
-    mix = C["model_type"] == "mixtral"
-    for i, lw in enumerate(w["layers"]):
-        p = f"model.layers.{i}."
-        for k, nm in (("q_w", "q_proj"), ("k_w", "k_proj"), ("v_w", "v_proj"), ("o_w", "o_proj")):
-            put(p + f"self_attn.{nm}.weight", lw[k])
-        if "qn_w" in lw:
-            put(p + "self_attn.q_norm.weight", lw["qn_w"])
-            put(p + "self_attn.k_norm.weight", lw["kn_w"])
-        put(p + "input_layernorm.weight", lw["iln_w"])
-        put(p + "post_attention_layernorm.weight", lw["pln_w"])
-        m = p + ("block_sparse_moe." if mix else "mlp.")
-        put(m + "gate.weight", lw["router"])
-        for e, ew in enumerate(lw["experts"]):
-            names = (("gate_w", "w1"), ("up_w", "w3"), ("down_w", "w2")) if mix else \
-                (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj"))
-            for k, nm in names:
-                put(m + f"experts.{e}.{nm}.weight", ew[k])
     return eng
 
 

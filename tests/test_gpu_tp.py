@@ -1,7 +1,10 @@
 """Tensor-parallel engine on 2 GPUs (skipped with fewer): column-parallel
 q/k/v and gate/up, row-parallel o and down with the fused peer-memory
 all-reduce (+ residual + RMSNorm) for decode and NCCL for prefill, and the
-vocabulary-parallel argmax, against the numpy whole-model oracle.
+vocabulary-parallel argmax, against the numpy whole-model oracle.  The dense
+Qwen3 layout and both mixture-of-experts layouts (Mixtral, Qwen3-MoE: every
+expert's width split across the ranks, the router replicated, the weighted
+combine all-reduced) run the same packed prefill + greedy decode steps.
 
 Bar: the concatenated logits shards have cosine >= 0.999 with the oracle's
 logits; every rank returns the same greedy tokens, equal to the oracle's
@@ -22,7 +25,8 @@ pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
     import gpu_util as G  # noqa: F401  (makes the library's device helpers importable)
-    from test_gpu_engine import NARROW, make_weights, oracle_cfg
+    import test_gpu_engine as dense
+    import test_gpu_engine_moe as moe
 
 
 def _free_port():
@@ -31,18 +35,29 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_prefill_and_decode():
+def _dense_case():
+    C = dict(dense.NARROW, vocab_size=1200)
+    w = dense.make_weights(C, 3)
+    items = [("model.embed_tokens.weight", w["embed"]), ("lm_head.weight", w["lm_head"]),
+             ("model.norm.weight", w["norm"])]
+    for i, lw in enumerate(w["layers"]):
+        items += [(f"model.layers.{i}.{hf}.weight", lw[k]) for k, hf in dense.HF_NAMES.items()]
+    return C, w, items, dense.oracle_cfg(C)
+
+
+def _moe_case(base):
+    C = dict(base, vocab_size=1024)  # 512 vocabulary rows per rank (a multiple of 8)
+    w = moe.make_weights(C, 21)
+    return C, w, list(moe.weight_items(C, w)), moe.ocfg(C)
+
+
+def _run_tp2(C, items, seqs, steps):
     import tp_worker
 
-    C = dict(NARROW, vocab_size=1200)
-    w = make_weights(C, 3)
-    rng = np.random.default_rng(12)
-    seqs = [rng.integers(0, C["vocab_size"], n) for n in (7, 40, 230)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, w, seqs, 3, q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, items, seqs, steps, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -54,11 +69,24 @@ def test_tp2_prefill_and_decode():
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
         assert res[r]["errors"] == 0
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("kind", ["dense", "mixtral", "qwen3_moe"])
+def test_tp2_prefill_and_decode(kind):
+    if kind == "dense":
+        C, w, items, ocfg = _dense_case()
+    else:
+        C, w, items, ocfg = _moe_case(moe.MIXTRAL if kind == "mixtral" else moe.QWEN3_MOE)
+    rng = np.random.default_rng(12)
+    seqs = [rng.integers(0, C["vocab_size"], n) for n in (7, 40, 230)]
+    res = _run_tp2(C, items, seqs, 3)
 
     def check(shards, toks, prefixes):
         full = np.concatenate(shards, axis=1)
         for i, s in enumerate(prefixes):
-            ref = forward_last_logits(s, w, oracle_cfg(C))
+            ref = forward_last_logits(s, w, ocfg)
             assert G.cosine(full[i], ref) >= 0.999, (i, G.cosine(full[i], ref))
             top2 = np.sort(ref)[-2:]
             if top2[1] - top2[0] > 0.05 * np.abs(ref).max():
@@ -70,7 +98,7 @@ def test_tp2_prefill_and_decode():
     np.testing.assert_array_equal(t0, t1)
     check([l0, l1], t0, seqs)
     prefixes = [s.copy() for s in seqs]
-    for step in range(3):
+    for step in range(3):  # eager, captured, replayed
         (a0, fed0, o0), (a1, fed1, o1) = res[0]["decode"][step], res[1]["decode"][step]
         np.testing.assert_array_equal(o0, o1)
         prefixes = [np.append(p, t) for p, t in zip(prefixes, fed0)]

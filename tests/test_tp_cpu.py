@@ -112,3 +112,66 @@ def test_tp2_partitioning_matches_unsharded_layer():
     for r in range(2):
         np.testing.assert_allclose(out[r][0], ref, rtol=1e-4, atol=1e-5)
         np.testing.assert_array_equal(out[r][1], oracle.linear(ref, lm).argmax(1))
+
+
+def _moe_weights(rng, H=64, E=6, Im=48, Is=32):
+    def n(*s):
+        return (rng.standard_normal(s) * 0.1).astype(np.float32)
+
+    ex = [{"gate_w": n(Im, H), "up_w": n(Im, H), "down_w": n(H, Im)} for _ in range(E)]
+    sh = {"gate_w": n(Is, H), "up_w": n(Is, H), "down_w": n(H, Is)}
+    return n(E, H) * 5, ex, sh
+
+
+def _slice_mlp(m, P, r):
+    """The engine's expert split: gate/up rows r*I/P.., down columns r*I/P.."""
+    I = m["gate_w"].shape[0] // P
+    return {"gate_w": m["gate_w"][r * I:(r + 1) * I], "up_w": m["up_w"][r * I:(r + 1) * I],
+            "down_w": m["down_w"][:, r * I:(r + 1) * I]}
+
+
+def _moe_rank(r, P, port, q):
+    try:
+        import torch
+        import torch.distributed as dist
+
+        from oracle.moe import moe_ffn
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=r, world_size=P)
+        rng = np.random.default_rng(5)
+        router, ex, sh = _moe_weights(rng)
+        x = rng.standard_normal((11, 64)).astype(np.float32)
+        # replicated router (same selection on every rank), this rank's slice of every expert
+        part, ids, _ = moe_ffn(x, router, [_slice_mlp(e, P, r) for e in ex], 2, shared=_slice_mlp(sh, P, r))
+        t = torch.from_numpy(np.ascontiguousarray(part))
+        dist.all_reduce(t)
+        dist.destroy_process_group()
+        q.put((r, t.numpy(), ids))
+    except Exception:
+        q.put((r, traceback.format_exc(), None))
+
+
+def test_tp2_expert_split_matches_whole_moe():
+    from oracle.moe import moe_ffn
+
+    with socket.socket() as so:
+        so.bind(("127.0.0.1", 0))
+        port = so.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_moe_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict((r, (y, ids)) for r, y, ids in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(out[r][0], str), out[r][0]
+    rng = np.random.default_rng(5)
+    router, ex, sh = _moe_weights(rng)
+    x = rng.standard_normal((11, 64)).astype(np.float32)
+    ref, ids, _ = moe_ffn(x, router, ex, 2, shared=sh)
+    for r in range(2):
+        np.testing.assert_array_equal(out[r][1], ids)
+        np.testing.assert_allclose(out[r][0], ref, rtol=1e-4, atol=1e-5)

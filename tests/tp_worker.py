@@ -18,13 +18,13 @@ sys.path.insert(0, os.path.dirname(HERE))
 sys.path.insert(0, HERE)
 
 
-def run(rank, world, port, cfg, weights, seqs, steps, queue):
+def run(rank, world, port, cfg, items, seqs, steps, queue):
     try:
         import torch
         import torch.distributed as dist
 
         from atb_llm_study_b200 import capi
-        from test_gpu_engine import HF_NAMES, EngineConfig
+        from test_gpu_engine import EngineConfig
 
         from datetime import timedelta
 
@@ -50,19 +50,9 @@ def run(rank, world, port, cfg, weights, seqs, steps, queue):
         ec = EngineConfig(None, json.dumps(cfg).encode(), rank, 8, 256, 512, 128, 5, 0.02)
         eng = ctypes.c_void_p()
         capi.check(L.b200_engine_create_tp(ctypes.byref(ec), comm, ctypes.byref(eng)), "engine_create_tp")
-        held = []
-
-        def put(name, a):
+        for name, a in items:
             a = np.ascontiguousarray(a, np.float32)
-            held.append(a)
             capi.check(L.b200_engine_set_weight(eng, name.encode(), a.ctypes.data, 2, a.size), name)
-
-        put("model.embed_tokens.weight", weights["embed"])
-        put("lm_head.weight", weights["lm_head"])
-        put("model.norm.weight", weights["norm"])
-        for i, lw in enumerate(weights["layers"]):
-            for k, hf in HF_NAMES.items():
-                put(f"model.layers.{i}.{hf}.weight", lw[k])
 
         V = cfg["vocab_size"]
         Vl = V // world
