@@ -266,6 +266,226 @@ __global__ void gather_argmax_kernel(Peers pp, int64_t rows, int64_t* out, uint6
   finish(epoch, done, ep_s);
 }
 
+// ---- expert parallel: token dispatch and weighted combine over peer memory ----
+//
+// Each rank routes its own tokens and groups its (token, choice) rows by
+// expert (send rows + E+1 group offsets, both in its symmetric region).
+// Rank d owns experts [d*El, (d+1)*El).  Dispatch: rank d pulls, for each
+// local expert j and each source s in that order, source s's rows of expert
+// d*El+j straight from s's symmetric region into a contiguous receive buffer
+// (expert-major, then source rank, then the source's row order) and writes
+// the El+1 group offsets its grouped GEMMs read.  Combine: every rank pulls
+// the expert outputs of its own rows back from the owners' symmetric result
+// buffers and sums them with the routing weights, the residual and the
+// shared expert, then applies the next RMSNorm.
+
+constexpr int kEpThreads = 256;
+constexpr int kEpMaxExperts = 256;
+
+__device__ __forceinline__ int32_t clampi(int32_t v, int32_t lo, int32_t hi) { return v < lo ? lo : v > hi ? hi : v; }
+
+// One warp: exclusive scan of v[0..n) in place (n <= 2048), returns the total.
+__device__ int32_t warp_exclusive_scan(int32_t* v, int n) {
+  const int lane = threadIdx.x & 31;
+  int32_t carry = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const int32_t x = i < n ? v[i] : 0;
+    int32_t inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    if (i < n) v[i] = carry + inc - x;
+    carry += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  return carry;
+}
+
+__global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(Peers pp, int64_t off_offsets, int64_t off_rows,
+                                                                  int E, int El, int64_t H, int32_t send_cap,
+                                                                  __nv_bfloat16* __restrict__ recv, int32_t recv_cap,
+                                                                  int32_t* __restrict__ recv_offsets,
+                                                                  int32_t* __restrict__ row_base, uint64_t* epoch,
+                                                                  unsigned* done, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t ep_s;
+  __shared__ int32_t ro[kEpMaxExperts + 1];   // receive offset of group g = j*P + s
+  __shared__ int32_t start[kEpMaxExperts];    // first send row of group g at its source
+  __shared__ int32_t tot[kEpMaxExperts];      // block 0: rows of expert e over all sources
+  __shared__ int32_t before[kEpMaxExperts];   // block 0: rows of expert e from sources < this rank
+  if (threadIdx.x == 0) {
+    ep_s = *reinterpret_cast<volatile uint64_t*>(epoch) + 1;
+    exchange(pp, ep_s, err);
+  }
+  __syncthreads();
+  const int P = pp.world, G = El * P, e0 = pp.rank * El;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    const int j = g / P, s = g - j * P;
+    const int32_t* o = reinterpret_cast<const int32_t*>(pp.base[s] + off_offsets);
+    const int32_t a = clampi(__ldcg(o + e0 + j), 0, send_cap);
+    const int32_t b = clampi(__ldcg(o + e0 + j + 1), a, send_cap);
+    start[g] = a;
+    ro[g] = b - a;
+  }
+  if (blockIdx.x == 0) {
+    // where this rank's rows of every expert land on the expert's owner:
+    // row_base[e] = rows of the owner's earlier experts + rows of expert e from lower ranks
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int32_t t = 0, bsum = 0;
+      for (int s = 0; s < P; ++s) {
+        const int32_t* o = reinterpret_cast<const int32_t*>(pp.base[s] + off_offsets);
+        const int32_t a = clampi(__ldcg(o + e), 0, send_cap);
+        const int32_t n = clampi(__ldcg(o + e + 1), a, send_cap) - a;
+        t += n;
+        if (s < pp.rank) bsum += n;
+      }
+      tot[e] = t;
+      before[e] = bsum;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int32_t total = warp_exclusive_scan(ro, G);
+    if (threadIdx.x == 0) ro[G] = total;
+  }
+  if (blockIdx.x == 0) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int32_t b = before[e];
+      for (int f = (e / El) * El; f < e; ++f) b += tot[f];
+      row_base[e] = b;
+    }
+    for (int j = threadIdx.x; j <= El; j += blockDim.x) recv_offsets[j] = min(ro[j * P], recv_cap);
+  }
+  __syncthreads();
+  int32_t total = ro[G];
+  if (total > recv_cap) {
+    if (threadIdx.x == 0) raise_error(err, DEV_ERR_BAD_INDEX);
+    total = recv_cap;
+  }
+  // one warp per received row
+  const int64_t nch = H / 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (kEpThreads / 32);
+  for (int64_t i = (int64_t)blockIdx.x * (kEpThreads / 32) + (threadIdx.x >> 5); i < total; i += nw) {
+    int lo = 0, hi = G;  // ro[lo] <= i < ro[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (ro[mid] <= i) lo = mid;
+      else hi = mid;
+    }
+    const int s = lo % P;
+    const int64_t src = start[lo] + (i - ro[lo]);
+    const uint4* sp = reinterpret_cast<const uint4*>(pp.base[s] + off_rows) + src * nch;
+    uint4* dp = reinterpret_cast<uint4*>(recv) + i * nch;
+    for (int64_t c = lane; c < nch; c += 32) dp[c] = __ldcg(sp + c);
+  }
+  finish(epoch, done, ep_s);
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(
+    Peers pp, int64_t off_results, int32_t recv_cap, const int32_t* __restrict__ row_base,
+    const int32_t* __restrict__ own_offsets, const int32_t* __restrict__ ids, const float* __restrict__ w,
+    const int32_t* __restrict__ pos, int64_t T, int k, int E, int El, int64_t H, const __nv_bfloat16* residual,
+    const __nv_bfloat16* __restrict__ shared, __nv_bfloat16* out, const __nv_bfloat16* __restrict__ norm_w,
+    __nv_bfloat16* __restrict__ normed, float eps, uint64_t* epoch, unsigned* done, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t ep_s;
+  __shared__ float red[kEpThreads / 32];
+  if (threadIdx.x == 0) {
+    ep_s = *reinterpret_cast<volatile uint64_t*>(epoch) + 1;
+    exchange(pp, ep_s, err);
+  }
+  __syncthreads();
+  const int64_t nch = H / 8;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    float v[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
+      if (idx < nch) {
+        float a[8];
+        if (residual) {
+          unpack8(*reinterpret_cast<const uint4*>(residual + t * H + idx * 8), a);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[c][i] = a[i];
+        }
+        if (shared) {
+          unpack8(*reinterpret_cast<const uint4*>(shared + t * H + idx * 8), a);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[c][i] += a[i];
+        }
+      }
+    }
+    for (int j = 0; j < k; ++j) {
+      const int32_t p = pos[t * k + j];
+      const int32_t e = ids[t * k + j];
+      if (p < 0 || e < 0 || e >= E) continue;
+      const int64_t row = (int64_t)row_base[e] + (p - own_offsets[e]);
+      if (row < 0 || row >= recv_cap) {
+        if (threadIdx.x == 0) raise_error(err, DEV_ERR_BAD_INDEX);
+        continue;
+      }
+      const uint4* y = reinterpret_cast<const uint4*>(pp.base[e / El] + off_results) + row * nch;
+      const float wj = w[t * k + j];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
+        if (idx < nch) {
+          float a[8];
+          unpack8(__ldcg(y + idx), a);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[c][i] = fmaf(wj, a[i], v[c][i]);
+        }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
+      if (idx < nch) {
+        const uint4 o = pack8(v[c]);
+        *reinterpret_cast<uint4*>(out + t * H + idx * 8) = o;
+        unpack8(o, v[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
+      }
+    }
+    if (norm_w) {
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        float s = threadIdx.x < kEpThreads / 32 ? red[threadIdx.x] : 0.f;
+        s = warp_sum(s);
+        if (threadIdx.x == 0) red[0] = s;
+      }
+      __syncthreads();
+      const float rstd = rsqrtf(red[0] / (float)H + eps);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
+        if (idx < nch) {
+          float g[8];
+          unpack8(*reinterpret_cast<const uint4*>(norm_w + idx * 8), g);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[i] *= v[c][i] * rstd;
+          *reinterpret_cast<uint4*>(normed + t * H + idx * 8) = pack8(g);
+        }
+      }
+      __syncthreads();
+    }
+  }
+  finish(epoch, done, ep_s);
+}
+
 }  // namespace
 
 struct b200_comm_s {
@@ -291,6 +511,13 @@ Peers peers_of(const b200_comm_s* c) {
 }
 int64_t half_bytes(const b200_comm_s* c) { return ((c->sym_bytes - kHeader) / 2) & ~int64_t(255); }
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? B200_OK : B200_ERROR_CUDA_BASE - (int)e; }
+// Offset of [p, p + bytes) inside this rank's symmetric region (every rank's
+// copy of it sits at the same offset), or -1 when it is not inside.
+int64_t sym_offset(const b200_comm_s* c, const void* p, int64_t bytes) {
+  const auto* q = static_cast<const uint8_t*>(p);
+  if (!p || q < c->sym + kHeader || bytes < 0 || q + bytes > c->sym + c->sym_bytes) return -1;
+  return q - c->sym;
+}
 }  // namespace
 
 extern "C" int b200_comm_unique_id(void* id_out) {
@@ -455,6 +682,64 @@ extern "C" int b200_comm_argmax(b200_comm_t c, const void* logits, int64_t rows,
   B200_CHECK_LAUNCH();
   launch_kernel(gather_argmax_kernel, dim3(1), 256, 0, stream, peers_of(c), rows, out, c->epoch, c->done,
                 b200::error_word(c->device));
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+extern "C" int b200_ep_dispatch(b200_comm_t c, const int32_t* send_offsets, const void* send_rows, int64_t send_cap,
+                                int64_t experts, int64_t H, void* recv_rows, int64_t recv_cap, int32_t* recv_offsets,
+                                int32_t* row_base, b200_stream_t stream) {
+  if (!c || !recv_rows || !recv_offsets || !row_base || experts <= 0 || H <= 0 || H % 8 || send_cap < 0 ||
+      recv_cap < 0 || send_cap > INT32_MAX || recv_cap > INT32_MAX)
+    return B200_ERROR_INVALID_PARAM;
+  if (!c->connected || experts % c->world || experts > kEpMaxExperts) return B200_ERROR_INVALID_PARAM;
+  const int64_t oo = sym_offset(c, send_offsets, (experts + 1) * 4);
+  const int64_t orow = sym_offset(c, send_rows, send_cap * H * 2);
+  if (oo < 0 || orow < 0 || (oo & 3) || (orow & 15) || (reinterpret_cast<uintptr_t>(recv_rows) & 15))
+    return B200_ERROR_INVALID_PARAM;
+  const int El = (int)(experts / c->world);
+  // enough warps to keep NVLink busy for the decode-sized batches, a full wave for prefill
+  const int64_t want = (recv_cap + kEpThreads / 32 - 1) / (kEpThreads / 32);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, 2 * 148));
+  launch_kernel(ep_dispatch_kernel, dim3(grid), kEpThreads, 0, stream, peers_of(c), oo, orow, (int)experts, El, H,
+                (int32_t)send_cap, static_cast<__nv_bfloat16*>(recv_rows), (int32_t)recv_cap, recv_offsets, row_base,
+                c->epoch, c->done, b200::error_word(c->device));
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+extern "C" int b200_ep_combine(b200_comm_t c, const void* results, int64_t recv_cap, const int32_t* row_base,
+                               const int32_t* send_offsets, const int32_t* topk_ids, const float* topk_weights,
+                               const int32_t* perm_pos, int64_t T, int top_k, int64_t experts, int64_t H,
+                               const void* residual, const void* shared, void* out, const void* norm_weight,
+                               void* normed, float eps, b200_stream_t stream) {
+  if (!c || !row_base || !send_offsets || !topk_ids || !topk_weights || !perm_pos || !out || T < 0 || top_k <= 0 ||
+      experts <= 0 || H <= 0 || H % 8 || recv_cap < 0 || recv_cap > INT32_MAX)
+    return B200_ERROR_INVALID_PARAM;
+  if (norm_weight && !normed) return B200_ERROR_INVALID_PARAM;
+  if (!c->connected || experts % c->world || experts > kEpMaxExperts) return B200_ERROR_INVALID_PARAM;
+  const int64_t ores = sym_offset(c, results, recv_cap * H * 2);
+  if (ores < 0 || (ores & 15)) return B200_ERROR_INVALID_PARAM;
+  for (const void* p : {(const void*)out, residual, shared, norm_weight, (const void*)normed})
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15)) return B200_ERROR_INVALID_PARAM;
+  const int64_t per = (H / 8 + kEpThreads - 1) / kEpThreads;
+  // every rank takes part in the exchange even with no tokens of its own
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(T, 1024));
+  const int El = (int)(experts / c->world);
+  auto rb = static_cast<const __nv_bfloat16*>(residual);
+  auto sb = static_cast<const __nv_bfloat16*>(shared);
+  auto ob = static_cast<__nv_bfloat16*>(out);
+  auto nw = static_cast<const __nv_bfloat16*>(norm_weight);
+  auto nb = static_cast<__nv_bfloat16*>(normed);
+  unsigned* err = b200::error_word(c->device);
+  const Peers pp = peers_of(c);
+  switch (per) {
+    case 1: launch_kernel(ep_combine_kernel<1>, dim3(grid), kEpThreads, 0, stream, pp, ores, (int32_t)recv_cap, row_base, send_offsets, topk_ids, topk_weights, perm_pos, T, top_k, (int)experts, El, H, rb, sb, ob, nw, nb, eps, c->epoch, c->done, err); break;
+    case 2: launch_kernel(ep_combine_kernel<2>, dim3(grid), kEpThreads, 0, stream, pp, ores, (int32_t)recv_cap, row_base, send_offsets, topk_ids, topk_weights, perm_pos, T, top_k, (int)experts, El, H, rb, sb, ob, nw, nb, eps, c->epoch, c->done, err); break;
+    case 3:
+    case 4: launch_kernel(ep_combine_kernel<4>, dim3(grid), kEpThreads, 0, stream, pp, ores, (int32_t)recv_cap, row_base, send_offsets, topk_ids, topk_weights, perm_pos, T, top_k, (int)experts, El, H, rb, sb, ob, nw, nb, eps, c->epoch, c->done, err); break;
+    default: return B200_ERROR_UNSUPPORTED;
+  }
   B200_CHECK_LAUNCH();
   return B200_OK;
 }

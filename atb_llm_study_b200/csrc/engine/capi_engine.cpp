@@ -118,7 +118,7 @@ extern "C" int b200_engine_config_check(const char* config_json, char* model_typ
   return STATUS_OK;
 }
 
-static int create_engine(const b200_engine_config* c, b200_comm_t comm, b200_engine_t* out) {
+static int create_engine(const b200_engine_config* c, b200_comm_t comm, bool expert_parallel, b200_engine_t* out) {
   if (!c || !out) return ERROR_INVALID_PARAM;
   *out = nullptr;
   JsonConfig cfg;
@@ -145,6 +145,7 @@ static int create_engine(const b200_engine_config* c, b200_comm_t comm, b200_eng
   o.seed = c->init_seed;
   o.init_std = c->init_std > 0 ? c->init_std : 0.02f;
   o.comm = comm;
+  o.expert_parallel = expert_parallel;
   auto* e = new (std::nothrow) b200_engine_s();
   if (!e) return ERROR_DEVICE_MEMORY;
   s = e->model.Init(mc, o);
@@ -194,12 +195,17 @@ static int create_engine(const b200_engine_config* c, b200_comm_t comm, b200_eng
 }
 
 extern "C" int b200_engine_create(const b200_engine_config* c, b200_engine_t* out) {
-  return create_engine(c, nullptr, out);
+  return create_engine(c, nullptr, false, out);
 }
 
 extern "C" int b200_engine_create_tp(const b200_engine_config* c, b200_comm_t comm, b200_engine_t* out) {
   if (!comm) return ERROR_INVALID_PARAM;
-  return create_engine(c, comm, out);
+  return create_engine(c, comm, false, out);
+}
+
+extern "C" int b200_engine_create_ep(const b200_engine_config* c, b200_comm_t comm, b200_engine_t* out) {
+  if (!comm) return ERROR_INVALID_PARAM;
+  return create_engine(c, comm, true, out);
 }
 
 extern "C" int b200_engine_destroy(b200_engine_t e) {

@@ -142,7 +142,11 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
   // heads), I/P of the MLP width and V/P of the vocabulary; everything below
   // sizes from that local view.
   ModelConfig cfg = whole;
-  if (opt.comm) {
+  if (opt.comm && opt.expert_parallel) {
+    // Expert parallel: whole replica of everything but the routed experts, which split into equal blocks
+    B200_RETURN_IF(b200_comm_info(opt.comm, &ep_, &ep_rank_, &ep_bufs_[0], &ep_bufs_[1], nullptr));
+    if (whole.experts <= 0 || whole.experts % ep_ || whole.experts > 256) return ERROR_UNSUPPORTED;
+  } else if (opt.comm) {
     B200_RETURN_IF(b200_comm_info(opt.comm, &tp_, &tp_rank_, &tp_buf_[0], &tp_buf_[1], nullptr));
     if (tp_ > 1) {
       // GQA attention (dense or mixture-of-experts MLPs; an expert's width is split like a dense MLP's)
@@ -180,6 +184,18 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
     int64_t bb = 0;
     B200_RETURN_IF(b200_comm_info(opt.comm, nullptr, nullptr, nullptr, nullptr, &bb));
     if (bb < max_t_ * H * 2) return ERROR_INVALID_PARAM;
+  }
+  if (ep_ > 1) {
+    // symmetric buffer 0: [E+1 send offsets | 64 KiB][send rows: max_t_*k x H];
+    // buffer 1: expert results for up to every rank's rows [P*max_t_*k x H]
+    int64_t bb = 0;
+    B200_RETURN_IF(b200_comm_info(opt.comm, nullptr, nullptr, nullptr, nullptr, &bb));
+    ep_send_cap_ = max_t_ * cfg.top_k;
+    ep_recv_cap_ = ep_ * ep_send_cap_;
+    if (bb < kEpRowsOffset + ep_send_cap_ * H * 2 || bb < ep_recv_cap_ * H * 2) return ERROR_INVALID_PARAM;
+    ep_send_off_ = static_cast<int32_t*>(ep_bufs_[0]);
+    ep_send_rows_ = static_cast<uint8_t*>(ep_bufs_[0]) + kEpRowsOffset;
+    ep_results_ = ep_bufs_[1];
   }
   max_blocks_ = (opt.max_context + opt.block_size - 1) / opt.block_size;
   num_blocks_ = (int64_t)opt.max_batch * max_blocks_;
@@ -230,11 +246,11 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
     B200_RETURN_IF(A(wgu_, DType::BF16, {n_dense, 2 * I, H}));
     B200_RETURN_IF(A(wdown_, DType::BF16, {n_dense, H, I}));
   }
-  const int64_t E = cfg.experts, Im = cfg.moe_intermediate, Is = cfg.shared_intermediate;
+  const int64_t E = cfg.experts, Im = cfg.moe_intermediate, Is = cfg.shared_intermediate, El = E / ep_;
   if (n_moe > 0) {
     B200_RETURN_IF(A(router_, DType::BF16, {n_moe, E, H}));
-    B200_RETURN_IF(A(egu_, DType::BF16, {n_moe, E, 2 * Im, H}));
-    B200_RETURN_IF(A(edown_, DType::BF16, {n_moe, E, H, Im}));
+    B200_RETURN_IF(A(egu_, DType::BF16, {n_moe, El, 2 * Im, H}));
+    B200_RETURN_IF(A(edown_, DType::BF16, {n_moe, El, H, Im}));
     if (Is > 0) {
       B200_RETURN_IF(A(sgu_, DType::BF16, {n_moe, 2 * Is, H}));
       B200_RETURN_IF(A(sdown_, DType::BF16, {n_moe, H, Is}));
@@ -302,10 +318,17 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
     B200_RETURN_IF(A(topk_ids_, DType::INT32, {R}));
     B200_RETURN_IF(A(topk_w_, DType::FP32, {R}));
     B200_RETURN_IF(A(rlogits_, DType::FP32, {max_t_, E}));
-    B200_RETURN_IF(A(xperm_, DType::BF16, {R, H}));
-    B200_RETURN_IF(A(eact_, DType::BF16, {R, Im}));
-    B200_RETURN_IF(A(ey_, DType::BF16, {R, H}));
-    B200_RETURN_IF(A(eoff_, DType::INT32, {E + 1}));
+    if (ep_ > 1) {  // rows received from every rank for this rank's experts
+      B200_RETURN_IF(A(ep_recv_, DType::BF16, {ep_recv_cap_, H}));
+      B200_RETURN_IF(A(ep_act_, DType::BF16, {ep_recv_cap_, Im}));
+      B200_RETURN_IF(A(ep_recv_off_, DType::INT32, {El + 1}));
+      B200_RETURN_IF(A(ep_row_base_, DType::INT32, {E}));
+    } else {
+      B200_RETURN_IF(A(xperm_, DType::BF16, {R, H}));
+      B200_RETURN_IF(A(eact_, DType::BF16, {R, Im}));
+      B200_RETURN_IF(A(ey_, DType::BF16, {R, H}));
+      B200_RETURN_IF(A(eoff_, DType::INT32, {E + 1}));
+    }
     B200_RETURN_IF(A(ppos_, DType::INT32, {R}));
     B200_RETURN_IF(A(psrc_, DType::INT32, {R}));
     pws_bytes_ = b200_moe_permute_workspace_bytes(max_t_, cfg.top_k, cfg.experts);
@@ -476,7 +499,13 @@ Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DTy
   const int e = std::atoi(m.substr(8, d2 - 8).c_str());
   if (e < 0 || e >= E) return ERROR_WEIGHT_LOAD;
   const std::string w = m.substr(d2 + 1);
-  const int64_t ge = (int64_t)mi * E + e;  // expert slot in the MoE stacks
+  const int64_t El = E / ep_, e0 = (int64_t)ep_rank_ * El;
+  if (e < e0 || e >= e0 + El) {  // another rank's expert (expert parallel)
+    const bool known = w == "w1.weight" || w == "w2.weight" || w == "w3.weight" || w == "gate_proj.weight" ||
+                       w == "up_proj.weight" || w == "down_proj.weight";
+    return known ? STATUS_OK : ERROR_WEIGHT_LOAD;
+  }
+  const int64_t ge = (int64_t)mi * El + (e - e0);  // expert slot in the MoE stacks
   if (w == "w2.weight" || w == "down_proj.weight") return put_cols(edown_, ge * H * Im, H, Im);
   if (w == "w1.weight" || w == "gate_proj.weight")
     return put_interleaved(egu_, ge * 2 * Im * H, Im, false, rk * Im, P);
@@ -785,10 +814,12 @@ Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm, bool deco
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
   // route (logits + selection when few tokens), permutation (count, scan,
   // scatter, gather), 2 grouped GEMMs, combine
-  launches_ += (T < 1024 ? 2 : 1) + 4 + 2 + 1;
+  launches_ += T < 1024 ? 2 : 1;
   B200_RETURN_IF(b200_moe_route(normed_.data, H, bf(router_, mi * E * H), T, H, (int)E, k, cfg_.norm_topk ? 1 : 0,
                                 cfg_.routed_scale, topk_ids_.as<int32_t>(), topk_w_.as<float>(),
                                 rlogits_.as<float>(), st));
+  if (ep_ > 1) return MoeBlockEp(l, T, next_norm, decode);
+  launches_ += 4 + 2 + 1;
   B200_RETURN_IF(b200_moe_permute(topk_ids_.as<int32_t>(), T, k, (int)E, normed_.data, H, H, xperm_.data,
                                   eoff_.as<int32_t>(), ppos_.as<int32_t>(), psrc_.as<int32_t>(), pws_.data,
                                   pws_bytes_, st));
@@ -797,24 +828,7 @@ Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm, bool deco
   B200_RETURN_IF(b200::grouped_gemm_launch(eact_.data, Im, bf(edown_, mi * E * H * Im), Im, ey_.data, H,
                                            eoff_.as<int32_t>(), (int)E, R, H, Im, B200_EPI_NONE, st));
   const void* shared = nullptr;
-  if (Is > 0) {
-    float* ws = gemm_ws_.as<float>();
-    int s1 = 1, s2 = 1;
-    launches_ += 2;
-    B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(sgu_, mi * 2 * Is * H), H, sact_.data, Is, T, 2 * Is, H,
-                                     B200_EPI_SWIGLU, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s1));
-    if (s1 > 1) {
-      ++launches_;
-      B200_RETURN_IF(b200::splitk_reduce(ws, s1, T, 2 * Is, B200_EPI_SWIGLU, nullptr, nullptr, 0, sact_.data, Is, st));
-    }
-    B200_RETURN_IF(b200::gemm_launch(sact_.data, Is, bf(sdown_, mi * H * Is), Is, sout_.data, H, T, H, Is,
-                                     B200_EPI_NONE, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s2));
-    if (s2 > 1) {
-      ++launches_;
-      B200_RETURN_IF(b200::splitk_reduce(ws, s2, T, H, B200_EPI_NONE, nullptr, nullptr, 0, sout_.data, H, st));
-    }
-    shared = sout_.data;
-  }
+  B200_RETURN_IF(SharedExpert(l, T, &shared));
   if (tp_ > 1) {  // this rank's share of every expert (and of the shared expert): all-reduce the combined sum
     B200_RETURN_IF(b200_moe_combine(ey_.data, ppos_.as<int32_t>(), topk_w_.as<float>(), T, k, H, nullptr, shared,
                                     tp_buf_[1], nullptr, nullptr, cfg_.eps, st));
@@ -822,6 +836,62 @@ Status DecoderModel::MoeBlock(int l, int64_t T, const void* next_norm, bool deco
   }
   return (Status)b200_moe_combine(ey_.data, ppos_.as<int32_t>(), topk_w_.as<float>(), T, k, H, hidden_.data, shared,
                                   hidden_.data, next_norm, next_norm ? normed_.data : nullptr, cfg_.eps, st);
+}
+
+// Always-on shared expert of MoE layer l on normed_ into sout_ (*out = null when the model has none).
+Status DecoderModel::SharedExpert(int l, int64_t T, const void** out) {
+  *out = nullptr;
+  const int64_t H = cfg_.hidden, Is = cfg_.shared_intermediate, mi = moe_idx_[l];
+  if (Is <= 0) return STATUS_OK;
+  cudaStream_t st = ctx_->GetStream();
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  float* ws = gemm_ws_.as<float>();
+  int s1 = 1, s2 = 1;
+  launches_ += 2;
+  B200_RETURN_IF(b200::gemm_launch(normed_.data, H, bf(sgu_, mi * 2 * Is * H), H, sact_.data, Is, T, 2 * Is, H,
+                                   B200_EPI_SWIGLU, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s1));
+  if (s1 > 1) {
+    ++launches_;
+    B200_RETURN_IF(b200::splitk_reduce(ws, s1, T, 2 * Is, B200_EPI_SWIGLU, nullptr, nullptr, 0, sact_.data, Is, st));
+  }
+  B200_RETURN_IF(b200::gemm_launch(sact_.data, Is, bf(sdown_, mi * H * Is), Is, sout_.data, H, T, H, Is,
+                                   B200_EPI_NONE, nullptr, nullptr, 0, ws, gemm_ws_bytes_, st, &s2));
+  if (s2 > 1) {
+    ++launches_;
+    B200_RETURN_IF(b200::splitk_reduce(ws, s2, T, H, B200_EPI_NONE, nullptr, nullptr, 0, sout_.data, H, st));
+  }
+  *out = sout_.data;
+  return STATUS_OK;
+}
+
+// Expert-parallel MoE layer (routing already done): group this rank's rows by
+// expert into the symmetric send area, pull every rank's rows of the local
+// experts (dispatch), run the local experts' grouped GEMMs into the symmetric
+// result area, then pull this rank's outputs back from the owners and combine
+// them with the residual, the shared expert and the next input norm.
+Status DecoderModel::MoeBlockEp(int l, int64_t T, const void* next_norm, bool decode) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden, E = cfg_.experts, Im = cfg_.moe_intermediate, El = E / ep_;
+  const int k = cfg_.top_k;
+  const int64_t mi = moe_idx_[l];
+  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
+  // every rank's batch is at most max_batch rows in decode, max_t_ in prefill
+  const int64_t cap = (int64_t)ep_ * (decode ? opt_.max_batch : max_t_) * k;
+  launches_ += 4 + 1 + 2 + 1;  // permutation, dispatch, 2 grouped GEMMs, combine
+  B200_RETURN_IF(b200_moe_permute(topk_ids_.as<int32_t>(), T, k, (int)E, normed_.data, H, H, ep_send_rows_,
+                                  ep_send_off_, ppos_.as<int32_t>(), psrc_.as<int32_t>(), pws_.data, pws_bytes_, st));
+  B200_RETURN_IF(b200_ep_dispatch(opt_.comm, ep_send_off_, ep_send_rows_, ep_send_cap_, E, H, ep_recv_.data, cap,
+                                  ep_recv_off_.as<int32_t>(), ep_row_base_.as<int32_t>(), st));
+  B200_RETURN_IF(b200::grouped_gemm_launch(ep_recv_.data, H, bf(egu_, mi * El * 2 * Im * H), H, ep_act_.data, Im,
+                                           ep_recv_off_.as<int32_t>(), (int)El, cap, 2 * Im, H, B200_EPI_SWIGLU, st));
+  B200_RETURN_IF(b200::grouped_gemm_launch(ep_act_.data, Im, bf(edown_, mi * El * H * Im), Im, ep_results_, H,
+                                           ep_recv_off_.as<int32_t>(), (int)El, cap, H, Im, B200_EPI_NONE, st));
+  const void* shared = nullptr;
+  B200_RETURN_IF(SharedExpert(l, T, &shared));
+  return (Status)b200_ep_combine(opt_.comm, ep_results_, cap, ep_row_base_.as<int32_t>(), ep_send_off_,
+                                 topk_ids_.as<int32_t>(), topk_w_.as<float>(), ppos_.as<int32_t>(), T, k, E, H,
+                                 hidden_.data, shared, hidden_.data, next_norm, next_norm ? normed_.data : nullptr,
+                                 cfg_.eps, st);
 }
 
 Status DecoderModel::Head(int64_t rows, bool gather, int64_t* next_tokens, bool next_on_device, void* logits) {

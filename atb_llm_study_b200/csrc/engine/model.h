@@ -64,7 +64,8 @@ struct EngineOptions {
   int block_size = 128;
   uint64_t seed = 0;
   float init_std = 0.02f;
-  b200_comm_t comm = nullptr;  // tensor-parallel group (null: one GPU)
+  b200_comm_t comm = nullptr;  // tensor- or expert-parallel group (null: one GPU)
+  bool expert_parallel = false;  // comm splits the routed experts (attention data-parallel) instead of every matrix
 };
 
 class DecoderModel {
@@ -128,6 +129,18 @@ class DecoderModel {
   void* tp_buf_[2] = {nullptr, nullptr};  // this rank's partial-sum buffers in the group's symmetric memory
   Status TpProject(const void* A, int64_t K, const void* W, int64_t T, bool decode, int parity, const void* norm_w);
   Status TpReduce(int64_t T, bool decode, int parity, const void* norm_w);
+  // Expert parallel: ep_ ranks, this rank owns routed experts [ep_rank_*El, (ep_rank_+1)*El);
+  // send rows / offsets and expert results live in the group's symmetric buffers
+  int ep_ = 1, ep_rank_ = 0;
+  int64_t ep_recv_cap_ = 0, ep_send_cap_ = 0;
+  int32_t* ep_send_off_ = nullptr;
+  void* ep_send_rows_ = nullptr;
+  void* ep_results_ = nullptr;
+  DeviceTensor ep_recv_, ep_act_, ep_recv_off_, ep_row_base_;
+  void* ep_bufs_[2] = {nullptr, nullptr};
+  static constexpr int64_t kEpRowsOffset = 64 << 10;  // send rows start after the offsets in buffer 0
+  Status MoeBlockEp(int l, int64_t T, const void* next_norm, bool decode);
+  Status SharedExpert(int l, int64_t T, const void** out);
   EngineOptions opt_;
   std::unique_ptr<ContextManager> ctx_;
   std::unique_ptr<TensorAllocator> alloc_;

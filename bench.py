@@ -619,11 +619,12 @@ def bench_deepseek(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
-def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
-    """Qwen3-8B tensor-parallel over all ranks: the same decode (batch 64 at
-    context 2048) and prefill (8 x 2048) as the replica headline, one model
-    sharded P ways; two all-reduces per layer (fused peer-memory kernel for
-    decode, NCCL for prefill).  Timed with CUDA events, max over ranks."""
+def bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, seqs, plen, batch, ctx, note):
+    """One model tensor-parallel over all ranks: prefill `seqs` x `plen` per
+    step, decode `batch` sequences at context `ctx` (slots filled by prefills of
+    whole `ctx`-token prompts); two all-reduces per layer (fused peer-memory
+    kernel for decode, NCCL for prefill).  Timed with CUDA events, max over
+    ranks."""
     import numpy as np
 
     uid = ctypes.create_string_buffer(128)
@@ -632,8 +633,8 @@ def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
     box = [uid.raw]
     dist.broadcast_object_list(box, src=0)
     uid = ctypes.create_string_buffer(box[0], 128)
-    T = PREFILL_SEQS * PREFILL_LEN
-    sym = 2 * T * QWEN3_8B["hidden_size"] * 2 + (16 << 20)
+    T = max(seqs * plen, ctx)
+    sym = 2 * T * C["hidden_size"] * 2 + (16 << 20)
     comm = ctypes.c_void_p()
     check(L.b200_comm_create(world, rank, dev.index, uid, sym, ctypes.byref(comm)), "comm_create")
     h = ctypes.create_string_buffer(64)
@@ -641,24 +642,23 @@ def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
     hs = [None] * world
     dist.all_gather_object(hs, h.raw)
     check(L.b200_comm_connect(comm, ctypes.create_string_buffer(b"".join(hs), 64 * world)), "comm_connect")
-    max_ctx = DECODE_CTX + warm + steps + 16
-    cfg = EngineConfig(None, json.dumps(QWEN3_8B).encode(), dev.index, DECODE_BATCH, max_ctx, T, BLOCK, 4321, 0.02)
+    max_ctx = ctx + warm + steps + 16
+    cfg = EngineConfig(None, json.dumps(C).encode(), dev.index, batch, max_ctx, T, BLOCK, 4321, 0.02)
     eng = ctypes.c_void_p()
     check(L.b200_engine_create_tp(ctypes.byref(cfg), comm, ctypes.byref(eng)), "engine_create_tp")
     est = stream_of(eng)
     try:
-        V = QWEN3_8B["vocab_size"]
+        V = C["vocab_size"]
         rng = np.random.default_rng(2)  # the same prompts on every rank
-        lens = np.full(PREFILL_SEQS, PREFILL_LEN, np.int32)
-        groups = DECODE_BATCH // PREFILL_SEQS
-        ids = [torch.from_numpy(rng.integers(0, V, T).astype(np.int64)).to(dev) for _ in range(groups)]
-        nxt = torch.empty(DECODE_BATCH, dtype=torch.int64, device=dev)
+        lens = np.full(seqs, plen, np.int32)
+        ids_pf = torch.from_numpy(rng.integers(0, V, seqs * plen).astype(np.int64)).to(dev)
+        nxt = torch.empty(max(batch, seqs), dtype=torch.int64, device=dev)
 
         def prefill(i):
-            g = i % groups
-            slots = np.arange(g * PREFILL_SEQS, (g + 1) * PREFILL_SEQS, dtype=np.int32)
-            check(L.b200_engine_prefill(eng, ids[g].data_ptr(), 1, lens.ctypes.data, slots.ctypes.data,
-                                        PREFILL_SEQS, None, nxt[g * PREFILL_SEQS:].data_ptr(), 1, None), "prefill")
+            g = i % max(1, batch // seqs)
+            slots = np.arange(g * seqs, (g + 1) * seqs, dtype=np.int32) % batch
+            check(L.b200_engine_prefill(eng, ids_pf.data_ptr(), 1, lens.ctypes.data, slots.ctypes.data,
+                                        seqs, None, nxt.data_ptr(), 1, None), "prefill")
 
         def timed(fn, n):
             for i in range(warm):
@@ -676,14 +676,26 @@ def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
             return float(t.item())
 
         pf_ms = timed(prefill, max(1, min(steps, 3)))
+        # fill every slot to `ctx` with distinct prompts, as many per call as fit one prefill
         check(L.b200_engine_reset(eng), "reset")
-        for g in range(groups):
-            prefill(g)
-        slots_all = np.arange(DECODE_BATCH, dtype=np.int32)
-        state = {"a": nxt.clone(), "b": torch.empty_like(nxt)}
+        per = max(1, T // ctx)
+        for g0 in range(0, batch, per):
+            n = min(per, batch - g0)
+            ids_ctx = torch.from_numpy(rng.integers(0, V, n * ctx).astype(np.int64)).to(dev)
+            sl = np.arange(g0, g0 + n, dtype=np.int32)
+            check(L.b200_engine_prefill(eng, ids_ctx.data_ptr(), 1, np.full(n, ctx, np.int32).ctypes.data,
+                                        sl.ctypes.data, n, None, nxt[g0:].data_ptr(), 1, None), "prefill ctx")
+        slots_all = np.arange(batch, dtype=np.int32)
+        state = {"a": nxt[:batch].clone(), "b": torch.empty(batch, dtype=torch.int64, device=dev)}
+        # mixture-of-experts models are fed fresh random tokens (the same on every rank) so that routing stays
+        # near-uniform; greedy feedback from random weights can collapse onto a few tokens and experts
+        feed = (torch.from_numpy(rng.integers(0, V, (warm + steps, batch)).astype(np.int64)).to(dev)
+                if C.get("num_local_experts") or C.get("n_routed_experts") else None)
 
         def decode(_):
-            check(L.b200_engine_decode(eng, state["a"].data_ptr(), 1, slots_all.ctypes.data, DECODE_BATCH,
+            state["n"] = state.get("n", -1) + 1
+            src = state["a"] if feed is None else feed[state["n"] % feed.shape[0]]
+            check(L.b200_engine_decode(eng, src.data_ptr(), 1, slots_all.ctypes.data, batch,
                                        state["b"].data_ptr(), 1, None), "decode")
             state["a"], state["b"] = state["b"], state["a"]
 
@@ -692,11 +704,10 @@ def bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of):
         check(L.b200_engine_query(eng, 2, ctypes.byref(v)), "query")
         errs = ctypes.c_uint(0)
         check(L.b200_device_error_read(ctypes.addressof(errs), 1, None), "device_error_read")
-        return {"tp": world, "decode_tok_s": DECODE_BATCH / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
-                "prefill_tok_s": T / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
-                "decode_launches_per_step": v.value, "device_errors": errs.value,
-                "note": "one Qwen3-8B sharded over all ranks (latency-oriented); the headline `value` is "
-                        "independent replicas (throughput-oriented)"}
+        return {"tp": world, "decode_batch": batch, "decode_ctx": ctx, "decode_tok_s": batch / (dec_ms / 1e3),
+                "decode_ms_per_step": dec_ms, "prefill": f"{seqs}x{plen}",
+                "prefill_tok_s": seqs * plen / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
+                "decode_launches_per_step": v.value, "device_errors": errs.value, "note": note}
     finally:
         torch.cuda.synchronize(dev)
         dist.barrier()
@@ -834,9 +845,15 @@ def run_b200(args, rank, world, local_rank):
         check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
         return torch.cuda.ExternalStream(s.value, device=dev)
 
-    tp = None
+    tp = tp_mx = None
     if dist and not args.no_tp:
-        tp = bench_tp_qwen3(L, torch, dev, dist, world, rank, steps, warm, stream_of)
+        tp = bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, QWEN3_8B, PREFILL_SEQS, PREFILL_LEN,
+                      DECODE_BATCH, DECODE_CTX, "one Qwen3-8B sharded over all ranks (latency-oriented); the headline "
+                      "`value` is independent replicas (throughput-oriented)")
+        if not args.no_mixtral:
+            tp_mx = bench_tp(L, torch, dev, dist, world, rank, max(3, min(steps, 10)), warm, stream_of, MIXTRAL_8X7B,
+                             MX_PREFILL_SEQS, MX_PREFILL_LEN, MX_BATCH, MX_CTX,
+                             "one Mixtral-8x7B sharded over all ranks: every expert's width split, router replicated")
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
@@ -900,6 +917,8 @@ def run_b200(args, rank, world, local_rank):
     }
     if tp:
         result["tensor_parallel"] = tp
+    if tp_mx:
+        result["tensor_parallel_mixtral"] = tp_mx
     if vl:
         result["qwen3vl_embedding"] = vl
     if mx:
@@ -955,7 +974,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-vl", action="store_true", help="skip the Qwen3-VL-2B embedding section")
-    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel Qwen3-8B section (N > 1)")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel sections (N > 1)")
     ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
     ap.add_argument("--no-mixtral", action="store_true", help="skip the Mixtral-8x7B section")
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")

@@ -390,6 +390,41 @@ B200_API int b200_comm_allreduce_rmsnorm(b200_comm_t comm, int parity, int64_t T
 B200_API int b200_comm_argmax(b200_comm_t comm, const void* logits, int64_t rows, int64_t vocab_local, int64_t ld,
                               int64_t* out, b200_stream_t stream);
 
+/* ---------------------------------------------------------- expert parallel */
+
+/* Expert-parallel token exchange over a connected b200_comm_t (experts split
+ * into equal blocks: rank d owns experts [d*E/P, (d+1)*E/P)).  Collective:
+ * every rank calls dispatch, then combine, once per MoE layer, in the same
+ * order, even with no tokens of its own.  No reference counterpart (the
+ * reference declares EP but runs one device: layer_desc.h:59-60).
+ *
+ * Dispatch: send_offsets [E+1] (int32) and send_rows [send_cap, H] (bf16) are
+ * this rank's rows grouped by expert (b200_moe_permute's output); both must
+ * lie in the communicator's symmetric buffers (b200_comm_info), at the same
+ * offsets on every rank.  After a bounded wait for every rank's rows, this
+ * rank copies the rows of its own experts from every source over NVLink into
+ * recv_rows [recv_cap, H] — expert-major, then source rank, then the source's
+ * row order — and writes recv_offsets [E/P + 1] (the grouped GEMM's group
+ * offsets) and row_base [E] (where this rank's first row of expert e sits in
+ * the owner's receive buffer; read by the combine).  recv_cap must cover the
+ * worst case (P * tokens * top_k) or rows are dropped and the device error
+ * word is set. */
+B200_API int b200_ep_dispatch(b200_comm_t comm, const int32_t* send_offsets, const void* send_rows, int64_t send_cap,
+                              int64_t experts, int64_t H, void* recv_rows, int64_t recv_cap, int32_t* recv_offsets,
+                              int32_t* row_base, b200_stream_t stream);
+/* Combine: results [recv_cap, H] (bf16, in the symmetric buffers) are this
+ * rank's expert outputs for its received rows.  After a bounded wait for every
+ * rank's results, out[t] = residual[t] + shared[t] + sum_j w[t,j] *
+ * y(t, j) (fp32, choices in order, one rounding), y read from the owner of
+ * expert topk_ids[t,j] at row row_base[e] + perm_pos[t*k+j] - send_offsets[e];
+ * normed[t] = RMSNorm(out[t]) * norm_weight when norm_weight is not NULL.
+ * residual / shared may be NULL; out may alias residual. */
+B200_API int b200_ep_combine(b200_comm_t comm, const void* results, int64_t recv_cap, const int32_t* row_base,
+                             const int32_t* send_offsets, const int32_t* topk_ids, const float* topk_weights,
+                             const int32_t* perm_pos, int64_t T, int top_k, int64_t experts, int64_t H,
+                             const void* residual, const void* shared, void* out, const void* norm_weight,
+                             void* normed, float eps, b200_stream_t stream);
+
 /* ----------------------------------------------------------------- engine */
 
 /* A decoder model on one GPU: weights, a paged KV cache of max_batch slots x
@@ -433,15 +468,26 @@ enum b200_engine_query_key {
  * (atb_cpp_llm/src/engine/model_registry.cpp:90-121). */
 B200_API int b200_engine_create(const b200_engine_config* config, b200_engine_t* out);
 
-/* Tensor-parallel engine over `comm` (dense GQA models): rank r holds heads
- * [r*nq/P, (r+1)*nq/P) (and the matching kv heads), rows r*I/P.. of gate/up,
- * the matching columns of o/down, vocabulary rows r*V/P.. of lm_head; two
- * all-reduces per layer (fused with residual + RMSNorm for decode-sized
- * batches, NCCL for prefill), a vocabulary-parallel argmax.  Weights are
- * given whole through b200_engine_set_weight and sliced on the host.  Every
- * rank must make the same prefill/decode calls in the same order; `logits`
- * outputs receive this rank's vocabulary shard [rows, V/P]. */
+/* Tensor-parallel engine over `comm` (GQA models, dense or mixture-of-experts):
+ * rank r holds heads [r*nq/P, (r+1)*nq/P) (and the matching kv heads), rows
+ * r*I/P.. of gate/up, the matching columns of o/down (of every expert and the
+ * shared expert too; the router is replicated), vocabulary rows r*V/P.. of
+ * lm_head; two all-reduces per layer (fused with residual + RMSNorm for
+ * decode-sized batches, NCCL for prefill), a vocabulary-parallel argmax.
+ * Weights are given whole through b200_engine_set_weight and sliced on the
+ * host.  Every rank must make the same prefill/decode calls in the same
+ * order; `logits` outputs receive this rank's vocabulary shard [rows, V/P]. */
 B200_API int b200_engine_create_tp(const b200_engine_config* config, b200_comm_t comm, b200_engine_t* out);
+
+/* Expert-parallel engine over `comm` (mixture-of-experts models, GQA or MLA):
+ * every rank is a whole replica of the attention, dense and shared-expert
+ * weights serving its OWN sequences (data-parallel attention, its own KV
+ * cache); rank r holds routed experts [r*E/P, (r+1)*E/P) and every MoE layer
+ * exchanges tokens with b200_ep_dispatch / b200_ep_combine.  Expert weights of
+ * other ranks given to b200_engine_set_weight are skipped.  Every rank must
+ * make the same sequence of prefill/decode calls (each with its own
+ * sequences, at least one); `logits` are whole rows. */
+B200_API int b200_engine_create_ep(const b200_engine_config* config, b200_comm_t comm, b200_engine_t* out);
 
 /* Host function (no GPU): resolve and validate a config.json text the way
  * b200_engine_create does, without allocating anything; the registry entry it

@@ -61,40 +61,41 @@ def make_weights(seed=31):
     return w
 
 
+def weight_items(w):
+    """(HF name, fp32 array) of every weight, in DeepSeek-V2 checkpoint naming."""
+    yield "model.embed_tokens.weight", w["embed"]
+    yield "lm_head.weight", w["lm_head"]
+    yield "model.norm.weight", w["norm"]
+    mlp3 = (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj"))
+    for i, lw in enumerate(w["layers"]):
+        p = f"model.layers.{i}."
+        yield p + "self_attn.q_proj.weight", lw["q_w"]
+        yield p + "self_attn.kv_a_proj_with_mqa.weight", lw["kva_w"]
+        yield p + "self_attn.kv_a_layernorm.weight", lw["kv_norm"]
+        yield p + "self_attn.kv_b_proj.weight", lw["kvb_w"]
+        yield p + "self_attn.o_proj.weight", lw["o_w"]
+        yield p + "input_layernorm.weight", lw["iln_w"]
+        yield p + "post_attention_layernorm.weight", lw["pln_w"]
+        if "gate_w" in lw:
+            for k, nm in mlp3:
+                yield p + f"mlp.{nm}.weight", lw[k]
+        else:
+            yield p + "mlp.gate.weight", lw["router"]
+            for e, ew in enumerate(lw["experts"]):
+                for k, nm in mlp3:
+                    yield p + f"mlp.experts.{e}.{nm}.weight", ew[k]
+            for k, nm in mlp3:
+                yield p + f"mlp.shared_experts.{nm}.weight", lw["shared"][k]
+
+
 def create(w, block):
     L = G.L()
     cfg = EngineConfig(None, json.dumps(DSV2).encode(), 0, 8, 256, 512, block, 5, 0.02)
     eng = ctypes.c_void_p()
     G.check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(eng)), "engine_create")
-    held = []
-
-    def put(name, a):
+    for name, a in weight_items(w):
         a = np.ascontiguousarray(a, np.float32)
-        held.append(a)
         G.check(L.b200_engine_set_weight(eng, name.encode(), a.ctypes.data, 2, a.size), name)
-
-    put("model.embed_tokens.weight", w["embed"])
-    put("lm_head.weight", w["lm_head"])
-    put("model.norm.weight", w["norm"])
-    for i, lw in enumerate(w["layers"]):
-        p = f"model.layers.{i}."
-        put(p + "self_attn.q_proj.weight", lw["q_w"])
-        put(p + "self_attn.kv_a_proj_with_mqa.weight", lw["kva_w"])
-        put(p + "self_attn.kv_a_layernorm.weight", lw["kv_norm"])
-        put(p + "self_attn.kv_b_proj.weight", lw["kvb_w"])
-        put(p + "self_attn.o_proj.weight", lw["o_w"])
-        put(p + "input_layernorm.weight", lw["iln_w"])
-        put(p + "post_attention_layernorm.weight", lw["pln_w"])
-        if "gate_w" in lw:
-            for k, nm in (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj")):
-                put(p + f"mlp.{nm}.weight", lw[k])
-        else:
-            put(p + "mlp.gate.weight", lw["router"])
-            for e, ew in enumerate(lw["experts"]):
-                for k, nm in (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj")):
-                    put(p + f"mlp.experts.{e}.{nm}.weight", ew[k])
-            for k, nm in (("gate_w", "gate_proj"), ("up_w", "up_proj"), ("down_w", "down_proj")):
-                put(p + f"mlp.shared_experts.{nm}.weight", lw["shared"][k])
     return eng
 
 

@@ -57,7 +57,7 @@ def _run_tp2(C, items, seqs, steps):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, items, seqs, steps, q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, items, seqs, steps, "tp", q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
