@@ -281,6 +281,7 @@ __global__ void gather_argmax_kernel(Peers pp, int64_t rows, int64_t* out, uint6
 
 constexpr int kEpThreads = 256;
 constexpr int kEpMaxExperts = 256;
+constexpr int kEpMaxTopK = 8;
 
 __device__ __forceinline__ int32_t clampi(int32_t v, int32_t lo, int32_t hi) { return v < lo ? lo : v > hi ? hi : v; }
 
@@ -366,7 +367,10 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(Peers pp, int64
     if (threadIdx.x == 0) raise_error(err, DEV_ERR_BAD_INDEX);
     total = recv_cap;
   }
-  // one warp per received row
+  // one warp per received row; every lane issues all its remote loads of a
+  // row (up to kCopyUnroll 16-byte chunks) before the first store, so a row
+  // costs one NVLink round trip rather than one per chunk
+  constexpr int kCopyUnroll = 8;
   const int64_t nch = H / 8;
   const int lane = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (kEpThreads / 32);
@@ -381,7 +385,15 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(Peers pp, int64
     const int64_t src = start[lo] + (i - ro[lo]);
     const uint4* sp = reinterpret_cast<const uint4*>(pp.base[s] + off_rows) + src * nch;
     uint4* dp = reinterpret_cast<uint4*>(recv) + i * nch;
-    for (int64_t c = lane; c < nch; c += 32) dp[c] = __ldcg(sp + c);
+    for (int64_t c0 = lane; c0 < nch; c0 += 32 * kCopyUnroll) {
+      uint4 r[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u)
+        if (c0 + u * 32 < nch) r[u] = __ldcg(sp + c0 + u * 32);
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u)
+        if (c0 + u * 32 < nch) dp[c0 + u * 32] = r[u];
+    }
   }
   finish(epoch, done, ep_s);
 }
@@ -424,25 +436,43 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(
         }
       }
     }
-    for (int j = 0; j < k; ++j) {
-      const int32_t p = pos[t * k + j];
-      const int32_t e = ids[t * k + j];
-      if (p < 0 || e < 0 || e >= E) continue;
-      const int64_t row = (int64_t)row_base[e] + (p - own_offsets[e]);
-      if (row < 0 || row >= recv_cap) {
-        if (threadIdx.x == 0) raise_error(err, DEV_ERR_BAD_INDEX);
-        continue;
+    // every choice's source row first, then all the remote loads, then the
+    // weighted sum in choice order (one NVLink round trip per token)
+    const uint4* yrow[kEpMaxTopK];
+    float wj[kEpMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kEpMaxTopK; ++j) {
+      yrow[j] = nullptr;
+      wj[j] = 0.f;
+      if (j < k) {
+        const int32_t p = pos[t * k + j];
+        const int32_t e = ids[t * k + j];
+        if (p >= 0 && e >= 0 && e < E) {
+          const int64_t row = (int64_t)row_base[e] + (p - own_offsets[e]);
+          if (row >= 0 && row < recv_cap) {
+            yrow[j] = reinterpret_cast<const uint4*>(pp.base[e / El] + off_results) + row * nch;
+            wj[j] = w[t * k + j];
+          } else if (threadIdx.x == 0) {
+            raise_error(err, DEV_ERR_BAD_INDEX);
+          }
+        }
       }
-      const uint4* y = reinterpret_cast<const uint4*>(pp.base[e / El] + off_results) + row * nch;
-      const float wj = w[t * k + j];
+    }
 #pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
-        if (idx < nch) {
+    for (int c = 0; c < CH; ++c) {
+      const int64_t idx = threadIdx.x + (int64_t)c * kEpThreads;
+      if (idx < nch) {
+        uint4 ys[kEpMaxTopK];
+#pragma unroll
+        for (int j = 0; j < kEpMaxTopK; ++j)
+          if (yrow[j]) ys[j] = __ldcg(yrow[j] + idx);
+#pragma unroll
+        for (int j = 0; j < kEpMaxTopK; ++j) {
+          if (!yrow[j]) continue;
           float a[8];
-          unpack8(__ldcg(y + idx), a);
+          unpack8(ys[j], a);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[c][i] = fmaf(wj, a[i], v[c][i]);
+          for (int i = 0; i < 8; ++i) v[c][i] = fmaf(wj[j], a[i], v[c][i]);
         }
       }
     }
@@ -714,7 +744,7 @@ extern "C" int b200_ep_combine(b200_comm_t c, const void* results, int64_t recv_
                                const void* residual, const void* shared, void* out, const void* norm_weight,
                                void* normed, float eps, b200_stream_t stream) {
   if (!c || !row_base || !send_offsets || !topk_ids || !topk_weights || !perm_pos || !out || T < 0 || top_k <= 0 ||
-      experts <= 0 || H <= 0 || H % 8 || recv_cap < 0 || recv_cap > INT32_MAX)
+      top_k > kEpMaxTopK || experts <= 0 || H <= 0 || H % 8 || recv_cap < 0 || recv_cap > INT32_MAX)
     return B200_ERROR_INVALID_PARAM;
   if (norm_weight && !normed) return B200_ERROR_INVALID_PARAM;
   if (!c->connected || experts % c->world || experts > kEpMaxExperts) return B200_ERROR_INVALID_PARAM;

@@ -295,18 +295,35 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
       }
     }
   }
-  for (int j = 0; j < k; ++j) {
-    const int p = pos[t * k + j];
-    if (p < 0) continue;
-    const float wj = w[t * k + j];
+  // up to 8 choices at a time: their rows' loads all issued before the
+  // weighted sum, which keeps choice order
+  constexpr int kInFlight = 8;
+  for (int j0 = 0; j0 < k; j0 += kInFlight) {
+    const uint4* yrow[kInFlight];
+    float wj[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int j = j0 + u;
+      const int p = j < k ? pos[t * k + j] : -1;
+      yrow[u] = p >= 0 ? reinterpret_cast<const uint4*>(y + (int64_t)p * H) : nullptr;
+      wj[u] = p >= 0 ? w[t * k + j] : 0.f;
+    }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int64_t idx = threadIdx.x + (int64_t)c * kCombineThreads;
       if (idx < nch) {
-        float a[8];
-        unpack8(*reinterpret_cast<const uint4*>(y + (int64_t)p * H + idx * 8), a);
+        uint4 ys[kInFlight];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[c][i] = fmaf(wj, a[i], v[c][i]);
+        for (int u = 0; u < kInFlight; ++u)
+          if (yrow[u]) ys[u] = yrow[u][idx];
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+          if (!yrow[u]) continue;
+          float a[8];
+          unpack8(ys[u], a);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[c][i] = fmaf(wj[u], a[i], v[c][i]);
+        }
       }
     }
   }

@@ -619,6 +619,143 @@ def bench_deepseek(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
+def make_comm(L, dist, world, rank, dev, sym_bytes):
+    """A connected b200_comm_t over all ranks (NCCL id and CUDA IPC handles exchanged through `dist`)."""
+    uid = ctypes.create_string_buffer(128)
+    if rank == 0:
+        check(L.b200_comm_unique_id(uid), "comm_unique_id")
+    box = [uid.raw]
+    dist.broadcast_object_list(box, src=0)
+    uid = ctypes.create_string_buffer(box[0], 128)
+    comm = ctypes.c_void_p()
+    check(L.b200_comm_create(world, rank, dev.index, uid, sym_bytes, ctypes.byref(comm)), "comm_create")
+    h = ctypes.create_string_buffer(64)
+    check(L.b200_comm_ipc_handle(comm, h), "comm_ipc_handle")
+    hs = [None] * world
+    dist.all_gather_object(hs, h.raw)
+    check(L.b200_comm_connect(comm, ctypes.create_string_buffer(b"".join(hs), 64 * world)), "comm_connect")
+    return comm
+
+
+def moe_decode_bytes(C, P, batch, ctx):
+    """Algorithmic bytes one rank streams in one decode step of a
+    mixture-of-experts model under P-way expert parallelism (P = 1: one GPU)
+    with data-parallel attention: every replicated weight once (attention —
+    plain, not absorbed, projections for MLA — dense layers, shared experts,
+    routers, lm_head), this rank's share of the routed experts the P * batch
+    tokens are expected to reach at uniform routing, and this rank's own KV
+    (latent) cache of batch x ctx tokens."""
+    H, Lyr, V = C["hidden_size"], C["num_hidden_layers"], C["vocab_size"]
+    if C.get("n_routed_experts"):
+        E, k, Im = C["n_routed_experts"], C["num_experts_per_tok"], C["moe_intermediate_size"]
+        nh, lora, rope, nope, vh = (C["num_attention_heads"], C["kv_lora_rank"], C["qk_rope_head_dim"],
+                                    C["qk_nope_head_dim"], C["v_head_dim"])
+        attn = H * nh * (nope + rope) + H * (lora + rope) + lora + nh * (nope + vh) * lora + H * nh * vh
+        fd = C["first_k_dense_replace"]
+        dense = fd * 3 * H * C["intermediate_size"]
+        shared = 3 * H * C["n_shared_experts"] * Im
+        cache = batch * ctx * Lyr * (lora + rope)
+    else:
+        E, k, Im = C["num_local_experts"], C["num_experts_per_tok"], C["intermediate_size"]
+        nq, nkv, hd = C["num_attention_heads"], C["num_key_value_heads"], H // C["num_attention_heads"]
+        attn = H * (nq + 2 * nkv) * hd + H * nq * hd
+        fd, dense, shared = 0, 0, 0
+        cache = batch * ctx * Lyr * 2 * nkv * hd
+    touched = (E / P) * (1 - ((E - k) / E) ** (P * batch))  # this rank's experts reached by P*batch tokens x k
+    weights = Lyr * attn + dense + (Lyr - fd) * (touched * 3 * H * Im + shared + E * H) + V * H
+    return 2 * (weights + cache)
+
+
+def bench_ep(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, batch, ctx, name):
+    """Expert parallel over all ranks: every rank serves its OWN `batch`
+    sequences at context `ctx` (data-parallel attention, whole replicas of the
+    non-expert weights) and holds E/P routed experts; every MoE layer exchanges
+    tokens through the peer-memory dispatch / combine kernels.  Whole-job
+    decode tok/s = P * batch / (max over ranks of the step time); fresh random
+    tokens each step (own seed per rank)."""
+    import numpy as np
+
+    H, k = C["hidden_size"], C["num_experts_per_tok"]
+    T = 2 * ctx  # prefill tokens per call (two whole prompts)
+    half = (64 << 10) + world * T * k * H * 2
+    comm = make_comm(L, dist, world, rank, dev, 2 * half + (1 << 20))
+    max_ctx = ctx + 2 * (warm + steps) + 16
+    cfg = EngineConfig(None, json.dumps(C).encode(), dev.index, batch, max_ctx, T, BLOCK, 99, 0.02)
+    eng = ctypes.c_void_p()
+    check(L.b200_engine_create_ep(ctypes.byref(cfg), comm, ctypes.byref(eng)), "engine_create_ep")
+    est = stream_of(eng)
+    try:
+        V = C["vocab_size"]
+        rng = np.random.default_rng(300 + rank)
+        nxt = torch.empty(batch, dtype=torch.int64, device=dev)
+        lens = np.full(2, ctx, np.int32)
+
+        def timed(fn, n):
+            for i in range(warm):
+                fn(i)
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(est)
+            for i in range(n):
+                fn(i)
+            e1.record(est)
+            torch.cuda.synchronize(dev)
+            t = torch.tensor([e0.elapsed_time(e1) / n], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        ids_pf = torch.from_numpy(rng.integers(0, V, T).astype(np.int64)).to(dev)
+
+        def prefill(i):
+            g = i % max(1, batch // 2)
+            sl = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, ids_pf.data_ptr(), 1, lens.ctypes.data, sl.ctypes.data, 2, None,
+                                        nxt[2 * g:].data_ptr(), 1, None), "prefill")
+
+        pf_ms = timed(prefill, 3)
+        check(L.b200_engine_reset(eng), "reset")
+        for g in range(batch // 2):
+            ids = torch.from_numpy(rng.integers(0, V, T).astype(np.int64)).to(dev)
+            sl = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, ids.data_ptr(), 1, lens.ctypes.data, sl.ctypes.data, 2, None,
+                                        nxt[2 * g:].data_ptr(), 1, None), "prefill ctx")
+        slots_all = np.arange(batch, dtype=np.int32)
+        feed = torch.from_numpy(rng.integers(0, V, (warm + steps + 1, batch)).astype(np.int64)).to(dev)
+        out_d = torch.empty(batch, dtype=torch.int64, device=dev)
+        counter = {"i": 0}
+
+        def decode(_):
+            i = counter["i"] % feed.shape[0]
+            counter["i"] += 1
+            check(L.b200_engine_decode(eng, feed[i].data_ptr(), 1, slots_all.ctypes.data, batch, out_d.data_ptr(),
+                                       1, None), "decode")
+
+        dec_ms = timed(decode, steps)
+        v = ctypes.c_int64()
+        check(L.b200_engine_query(eng, 2, ctypes.byref(v)), "query")
+        errs = ctypes.c_uint(0)
+        check(L.b200_device_error_read(ctypes.addressof(errs), 1, None), "device_error_read")
+        hbm, _, _, src = peaks()
+        nbytes = moe_decode_bytes(C, world, batch, ctx)
+        return {"ep": world, "workload": f"{name}: {world} ranks x own decode batch {batch} at context {ctx}, "
+                                         f"{C.get('n_routed_experts') or C['num_local_experts']} experts split "
+                                         f"{world} ways, attention data-parallel",
+                "decode_tok_s": world * batch / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+                "decode_roofline_per_rank": {"bound": "hbm", "bytes_per_step": nbytes,
+                                             "achieved": nbytes / (dec_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                                             "frac": nbytes / (dec_ms / 1e3) / 1e9 / hbm,
+                                             "peak_source": f"{src} copy"},
+                "prefill_tok_s": world * T / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
+                "prefill": f"{world} ranks x 2x{ctx}",
+                "decode_launches_per_step": v.value, "device_errors": errs.value}
+    finally:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        L.b200_engine_destroy(eng)
+        L.b200_comm_destroy(comm)
+
+
 def bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, seqs, plen, batch, ctx, note):
     """One model tensor-parallel over all ranks: prefill `seqs` x `plen` per
     step, decode `batch` sequences at context `ctx` (slots filled by prefills of
@@ -627,21 +764,8 @@ def bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, seqs, 
     ranks."""
     import numpy as np
 
-    uid = ctypes.create_string_buffer(128)
-    if rank == 0:
-        check(L.b200_comm_unique_id(uid), "comm_unique_id")
-    box = [uid.raw]
-    dist.broadcast_object_list(box, src=0)
-    uid = ctypes.create_string_buffer(box[0], 128)
     T = max(seqs * plen, ctx)
-    sym = 2 * T * C["hidden_size"] * 2 + (16 << 20)
-    comm = ctypes.c_void_p()
-    check(L.b200_comm_create(world, rank, dev.index, uid, sym, ctypes.byref(comm)), "comm_create")
-    h = ctypes.create_string_buffer(64)
-    check(L.b200_comm_ipc_handle(comm, h), "comm_ipc_handle")
-    hs = [None] * world
-    dist.all_gather_object(hs, h.raw)
-    check(L.b200_comm_connect(comm, ctypes.create_string_buffer(b"".join(hs), 64 * world)), "comm_connect")
+    comm = make_comm(L, dist, world, rank, dev, 2 * T * C["hidden_size"] * 2 + (16 << 20))
     max_ctx = ctx + warm + steps + 16
     cfg = EngineConfig(None, json.dumps(C).encode(), dev.index, batch, max_ctx, T, BLOCK, 4321, 0.02)
     eng = ctypes.c_void_p()
@@ -845,7 +969,12 @@ def run_b200(args, rank, world, local_rank):
         check(L.b200_engine_stream(e, ctypes.byref(s)), "engine_stream")
         return torch.cuda.ExternalStream(s.value, device=dev)
 
-    tp = tp_mx = None
+    tp = tp_mx = ep_ds = ep_mx = None
+    if dist and not args.no_ep:
+        ep_ds = bench_ep(L, torch, dev, dist, world, rank, max(3, min(steps, 10)), warm, stream_of,
+                         DEEPSEEK_V2_LITE, DS_BATCH, DS_CTX, "DeepSeek-V2-Lite")
+        ep_mx = bench_ep(L, torch, dev, dist, world, rank, max(3, min(steps, 10)), warm, stream_of, MIXTRAL_8X7B,
+                         MX_BATCH, MX_CTX, "Mixtral-8x7B")
     if dist and not args.no_tp:
         tp = bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, QWEN3_8B, PREFILL_SEQS, PREFILL_LEN,
                       DECODE_BATCH, DECODE_CTX, "one Qwen3-8B sharded over all ranks (latency-oriented); the headline "
@@ -919,6 +1048,10 @@ def run_b200(args, rank, world, local_rank):
         result["tensor_parallel"] = tp
     if tp_mx:
         result["tensor_parallel_mixtral"] = tp_mx
+    if ep_ds:
+        result["expert_parallel_deepseek"] = ep_ds
+    if ep_mx:
+        result["expert_parallel_mixtral"] = ep_mx
     if vl:
         result["qwen3vl_embedding"] = vl
     if mx:
@@ -975,6 +1108,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-vl", action="store_true", help="skip the Qwen3-VL-2B embedding section")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel sections (N > 1)")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel sections (N > 1)")
     ap.add_argument("--vl-only", action="store_true", help="only the Qwen3-VL-2B embedding section")
     ap.add_argument("--no-mixtral", action="store_true", help="skip the Mixtral-8x7B section")
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")

@@ -413,7 +413,7 @@ B200_API int b200_ep_dispatch(b200_comm_t comm, const int32_t* send_offsets, con
                               int64_t experts, int64_t H, void* recv_rows, int64_t recv_cap, int32_t* recv_offsets,
                               int32_t* row_base, b200_stream_t stream);
 /* Combine: results [recv_cap, H] (bf16, in the symmetric buffers) are this
- * rank's expert outputs for its received rows.  After a bounded wait for every
+ * rank's expert outputs for its received rows; top_k <= 8.  After a bounded wait for every
  * rank's results, out[t] = residual[t] + shared[t] + sum_j w[t,j] *
  * y(t, j) (fp32, choices in order, one rounding), y read from the owner of
  * expert topk_ids[t,j] at row row_base[e] + perm_pos[t*k+j] - send_offsets[e];
