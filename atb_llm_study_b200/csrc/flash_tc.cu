@@ -1,0 +1,422 @@
+// Prefill attention on the 5th-generation tensor cores (128-wide heads).
+//
+// One CTA = 128 query rows of one head of one sequence, 192 threads:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
+//               (two 64-column boxes each, 128-byte swizzle) through a
+//               2-stage ring guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM; one thread issues tcgen05.mma:
+//               S_j = Q K_j^T into one of two TMEM score buffers (M=128,
+//               N=128, K=128), and O += P_j V_j into the TMEM output
+//               accumulator (P from shared memory, V read MN-major so no
+//               transpose is ever materialised).  S_{j+1} is issued before
+//               waiting for P_j, so the tensor core computes the next scores
+//               while the softmax warps work on the current ones.
+//   warps 2-5   softmax, one query row per thread (TMEM lane = row): load the
+//               row's 128 scores, mask (causal rule j > i and the sequence
+//               end), online max / sum in the log2 domain, write P (bf16) into
+//               shared memory in the swizzled K-major layout the MMA reads.
+//               The running max only moves when it grows by more than 2^8, so
+//               the O rows in TMEM are rescaled rarely; the final 1/l scaling
+//               and the bf16 store happen once, from TMEM.
+// Every mbarrier wait is bounded and sets the device error word on timeout.
+// No TMA multicast (the library also runs in multi-GPU jobs).
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+using namespace b200;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kTile = 128;                    // query rows per CTA = keys per tile
+constexpr int kBoxBytes = kTile * 128;        // 128 rows x 64 bf16 (one 128-byte swizzle span)
+constexpr int kTileBytes = 2 * kBoxBytes;     // 128 rows x 128 dims
+constexpr int kSmem = 6 * kTileBytes + 1024 + 256;  // Q, K x2, V x2, P + alignment + barriers
+constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256,384)
+constexpr float kRescaleLog2 = 8.f;           // move the running max only when it grows by > 2^8
+constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128);
+constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128) | (1u << 16);  // B operand (V) MN-major
+
+// MN-major operand, 128-byte swizzle: 64-element rows of the MN dimension,
+// 8-row groups of the K dimension 1024 bytes apart (SBO), the next 64
+// MN elements `lbo` bytes away (LBO).
+__device__ __forceinline__ uint64_t smem_desc_mn128(uint32_t addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t r[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 2^x on the special-function unit (PTX ex2.approx, relative error ~2^-22)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, int64_t os,
+                            int64_t ohs, const int32_t* __restrict__ cu, int nq, int nkv, int64_t qhs, int64_t khs,
+                            int64_t vhs, float scale_log2, int mblocks, unsigned* err) {
+  pdl_trigger();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kTileBytes;
+  uint8_t* sV = smem + 3 * kTileBytes;
+  uint8_t* sP = smem + 5 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  // heavier (later) query tiles first: causal tiles see more keys
+  const int m = mblocks - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, sq = blockIdx.z;
+  pdl_wait();  // q / k / v and the sequence offsets come from earlier kernels
+  const int start = cu[sq];
+  const int len = cu[sq + 1] - start;
+  const int m0 = m * kTile;
+  if (m0 >= len) return;  // whole CTA: no barrier or TMEM touched yet
+  const int ntiles = CAUSAL ? min((len + kTile - 1) / kTile, m + 1) : (len + kTile - 1) / kTile;
+  const int kvh = h / (nq / nkv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const int qc = (int)(h * qhs), kc = (int)(kvh * khs), vc = (int)(kvh * vhs);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tmQ, q_full, qc, start + m0);
+      tma_load_2d(sQ + kBoxBytes, &tmQ, q_full, qc + 64, start + m0);
+      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int row = start + j * kTile;
+        if (j >= 2 && !mbar_wait(&k_empty[st], ph ^ 1, err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+        tma_load_2d(sK + st * kTileBytes, &tmK, &k_full[st], kc, row);
+        tma_load_2d(sK + st * kTileBytes + kBoxBytes, &tmK, &k_full[st], kc + 64, row);
+        if (j >= 2 && !mbar_wait(&v_empty[st], ph ^ 1, err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+        tma_load_2d(sV + st * kTileBytes, &tmV, &v_full[st], vc, row);
+        tma_load_2d(sV + st * kTileBytes + kBoxBytes, &tmV, &v_full[st], vc + 64, row);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t tO = tmem + 256;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_full[st], ph, err)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[st], ph ^ 1, err)) return false;
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
+          umma_bf16(tmem + st * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, err);
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
+        if (j + 1 < ntiles && !(ok = issue_s(j + 1))) break;
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(p_full, j & 1, err) || !mbar_wait(&v_full[st], ph, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
+                    smem_desc_mn128(v0 + ks * 2048, kBoxBytes), kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(o_done);
+        umma_commit(&v_empty[st]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax (warps 2..5, one query row per thread) ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;
+    const int qpos = m0 + row;     // query position within the sequence
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    float mref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (*abort_flag || !mbar_wait(&s_full[st], ph, err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lanes + st * 128 + c * 32, sr + c * 32);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+      const int kv0 = j * kTile;
+      const bool full_tile = kv0 + kTile <= len && (!CAUSAL || kv0 + kTile - 1 <= m0);
+      // raw-score max (scale > 0), masked keys set to -inf
+      float mx = -INFINITY;
+      if (full_tile) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const int col = kv0 + c;
+          if (col >= len || (CAUSAL && col > qpos)) sr[c] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(sr[c]));
+        }
+      }
+      mx *= scale_log2;
+      // running max (log2 domain): moved only when it grows by more than 2^kRescaleLog2
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > mref + kRescaleLog2 || (mref == -INFINITY && mx > -INFINITY)) {
+        rescale = mref != -INFINITY;
+        alpha = rescale ? ex2(mref - mx) : 0.f;
+        l *= alpha;
+        mref = mx;
+      }
+      // P = 2^(s * scale - ref), packed to bf16 pairs in place, before waiting
+      // for the previous P.V product (this overlaps the exponentials with it)
+      const float ref = mref == -INFINITY ? 0.f : mref;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -ref));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -ref));
+        rs += p0 + p1;
+        sr[c] = pack2(p0, p1);
+      }
+      if (j > 0) {  // P_{j-1} consumed and O up to date
+        if (!mbar_wait(o_done, (j - 1) & 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * (rescale ? alpha : 1.f));
+            tmem_st_32x32b_x32(tmem + lanes + 256 + c * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      uint8_t* prow = sP + row * 128;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)  // 16-byte chunk k = keys 8k..8k+7
+        *reinterpret_cast<uint4*>(prow + (k >> 3) * kBoxBytes + (((k & 7) ^ (row & 7)) << 4)) =
+            make_uint4(sr[4 * k], sr[4 * k + 1], sr[4 * k + 2], sr[4 * k + 3]);
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && !*abort_flag && mbar_wait(o_done, (ntiles - 1) & 1, err)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool valid = qpos < len;
+      __nv_bfloat16* orow = out + (int64_t)(start + (valid ? qpos : 0)) * os + (int64_t)h * ohs;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * g + i]) * inv;
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = pack8(f);
+          }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// Row-major bf16 [rows, cols] with row stride ld (elements); box = 128 rows x
+// 64 columns, 128-byte swizzle; rows past `rows` read as zeros.
+bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)kTile};
+  cuuint32_t estr[2] = {1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool CAUSAL>
+int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* out, int64_t os,
+              int64_t ohs, const int32_t* cu, int num_seqs, int mblocks, int nq, int nkv, int64_t qhs, int64_t khs,
+              int64_t vhs, float scale_log2, cudaStream_t st) {
+  auto k = flash_prefill_tc_kernel<CAUSAL>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return B200_ERROR_UNSUPPORTED;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return B200_ERROR_UNSUPPORTED;
+    attr_set[dev] = true;
+  }
+  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, kSmem, st, mq, mk, mv, static_cast<__nv_bfloat16*>(out),
+                os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks, b200::error_word(dev));
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_t q_head_stride, const void* k,
+                                         int64_t k_stride, int64_t k_head_stride, const void* v, int64_t v_stride,
+                                         int64_t v_head_stride, void* out, int64_t out_stride,
+                                         int64_t out_head_stride, const int32_t* cu_seqlens, int num_seqs,
+                                         int max_seqlen, int64_t total_tokens, int nq, int nkv, int head_dim_qk,
+                                         int head_dim_v, float scale, int causal, b200_stream_t stream) {
+  if (head_dim_qk != 128 || head_dim_v != 128 || total_tokens <= 0)
+    return b200_flash_prefill_ex(q, q_stride, q_head_stride, k, k_stride, k_head_stride, v, v_stride, v_head_stride,
+                                 out, out_stride, out_head_stride, cu_seqlens, num_seqs, max_seqlen, nq, nkv,
+                                 head_dim_qk, head_dim_v, scale, causal, stream);
+  if (!q || !k || !v || !out || !cu_seqlens || num_seqs < 0 || max_seqlen < 0 || nq <= 0 || nkv <= 0 || nq % nkv)
+    return B200_ERROR_INVALID_PARAM;
+  for (int64_t s : {q_stride, q_head_stride, k_stride, k_head_stride, v_stride, v_head_stride, out_stride,
+                    out_head_stride})
+    if (s < 0 || s % 8) return B200_ERROR_INVALID_PARAM;
+  for (const void* p : {q, k, v, (const void*)out})
+    if (reinterpret_cast<uintptr_t>(p) & 15u) return B200_ERROR_INVALID_PARAM;
+  const int64_t qcols = (int64_t)(nq - 1) * q_head_stride + 128, kcols = (int64_t)(nkv - 1) * k_head_stride + 128,
+                vcols = (int64_t)(nkv - 1) * v_head_stride + 128;
+  if (q_stride < qcols || k_stride < kcols || v_stride < vcols ||
+      out_stride < (int64_t)(nq - 1) * out_head_stride + 128)
+    return B200_ERROR_INVALID_PARAM;
+  if (num_seqs == 0 || max_seqlen == 0) return B200_OK;
+  if (num_seqs > 65535 || nq > 65535 || total_tokens > INT32_MAX || qcols > INT32_MAX || kcols > INT32_MAX ||
+      vcols > INT32_MAX)
+    return B200_ERROR_UNSUPPORTED;
+  // the maps end at the last packed row and at each operand's last head, so
+  // no tile reads past the buffers: rows beyond total_tokens read as zeros
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, q, total_tokens, qcols, q_stride) || !make_map(&mk, k, total_tokens, kcols, k_stride) ||
+      !make_map(&mv, v, total_tokens, vcols, v_stride))
+    return B200_ERROR_UNSUPPORTED;
+  const int mblocks = (max_seqlen + kTile - 1) / kTile;
+  const float sl2 = scale * 1.4426950408889634f;
+  return causal ? launch_tc<true>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq,
+                                  nkv, q_head_stride, k_head_stride, v_head_stride, sl2, stream)
+                : launch_tc<false>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq,
+                                   nkv, q_head_stride, k_head_stride, v_head_stride, sl2, stream);
+}

@@ -243,6 +243,20 @@ B200_API int b200_flash_prefill_ex(const void* q, int64_t q_stride, int64_t q_he
                                    const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int nq, int nkv,
                                    int head_dim_qk, int head_dim_v, float scale, int causal, b200_stream_t stream);
 
+/* b200_flash_prefill_ex for callers that know the packed row count on the
+ * host (total_tokens = cu_seqlens[num_seqs]).  128-wide heads run on the
+ * tcgen05 tensor cores: 128 query rows per CTA, K/V tiles of 128 keys by TMA
+ * (tile reads stop at total_tokens and at each operand's last head), scores
+ * and the output accumulator in TMEM, the running max moved only when it grows
+ * by more than 2^8 (exact rescaling, rarely needed).  Other head widths, or
+ * total_tokens <= 0, run b200_flash_prefill_ex.  Same causal rule. */
+B200_API int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_t q_head_stride, const void* k,
+                                       int64_t k_stride, int64_t k_head_stride, const void* v, int64_t v_stride,
+                                       int64_t v_head_stride, void* out, int64_t out_stride, int64_t out_head_stride,
+                                       const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int64_t total_tokens,
+                                       int nq, int nkv, int head_dim_qk, int head_dim_v, float scale, int causal,
+                                       b200_stream_t stream);
+
 /* ---- multi-head latent attention (DeepSeek-V2): fills the reference's stubs
  * MlaAttentionBuilder (atb_cpp_llm/src/components/common/attention_builder.h:60-69)
  * and AttnConfig.kv_lora_rank / q_lora_rank (atb_cpp_llm/include/atb_llm/layer_desc.h:47-49).
