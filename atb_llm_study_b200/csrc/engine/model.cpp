@@ -579,9 +579,9 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     uint16_t* q = static_cast<uint16_t*>(qkv_.data);
     if (!decode) {
       ++launches_;
-      B200_RETURN_IF(b200_flash_prefill(q, QKV, q + nq * hd, q + (nq + nkv) * hd, QKV, attn_.data, AO,
-                                        cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, nq, nkv, (int)hd, scale, 1,
-                                        st));
+      B200_RETURN_IF(b200_flash_prefill_packed(q, QKV, hd, q + nq * hd, QKV, hd, q + (nq + nkv) * hd, QKV, hd,
+                                               attn_.data, AO, hd, cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, T,
+                                               nq, nkv, (int)hd, (int)hd, scale, 1, st));
     } else {
       launches_ += attn_ws_bytes_ > 0 ? 2 : 1;
       B200_RETURN_IF(b200_paged_decode(q, QKV, kc, vc, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(),
