@@ -292,6 +292,30 @@ def kernel_roofline_moe_gemm(L, torch, dev, reps=10):
     return ms, E * N * K * 2 + rows * K * 2 + rows * N // 2 * 2
 
 
+def kernel_roofline_prefill_attention(L, torch, dev, reps=10):
+    """tcgen05 causal prefill attention alone at the Qwen3-8B prefill shape (8
+    sequences x 2048, 32 query / 8 kv heads of 128, the engine's packed q|k|v
+    rows): 2*S^2*d*nq flops per sequence (the causal half of QK^T and PV)."""
+    import numpy as np
+
+    S, B, nq, nkv, hd = PREFILL_LEN, PREFILL_SEQS, 32, 8, 128
+    T, W = S * B, (nq + 2 * nkv) * hd
+    g = torch.Generator(device=dev).manual_seed(5)
+    d = torch.randn(T, W, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device=dev)
+    cu = torch.from_numpy(np.arange(0, T + 1, S, dtype=np.int32)).to(dev)
+
+    def run(st):
+        check(L.b200_flash_prefill_packed(d.data_ptr(), W, hd, d.data_ptr() + nq * hd * 2, W, hd,
+                                          d.data_ptr() + (nq + nkv) * hd * 2, W, hd, out.data_ptr(), nq * hd, hd,
+                                          cu.data_ptr(), B, S, T, nq, nkv, hd, hd, 1.0 / hd ** 0.5, 1, st.cuda_stream),
+              "flash_prefill_packed")
+
+    ms = _time_launches(torch, dev, run, reps)
+    del d, out
+    return ms, 2.0 * S * S * hd * nq * B
+
+
 def kernel_roofline_prefill_gemm(L, torch, dev, reps=10):
     """gate/up projection with the fused SwiGLU epilogue at the prefill shape
     (M 16384, N 2 x 12288, K 4096): 2*M*N*K flops per launch."""
@@ -962,6 +986,7 @@ def run_b200(args, rank, world, local_rank):
     hbm, tf_burst, tf_sus, src = peaks()
     att_ms, att_bytes = kernel_roofline_decode_attention(L, torch, dev)
     gemm_ms, gemm_flops = kernel_roofline_prefill_gemm(L, torch, dev)
+    fa_ms, fa_flops = kernel_roofline_prefill_attention(L, torch, dev)
     L.b200_engine_destroy(eng)
 
     def stream_of(e):
@@ -1030,6 +1055,10 @@ def run_b200(args, rank, world, local_rank):
                          "bound": "tensor", "achieved": gemm_flops / (gemm_ms / 1e3) / 1e12, "peak": tf_burst,
                          "unit": "TFLOP/s", "frac": gemm_flops / (gemm_ms / 1e3) / 1e12 / tf_burst,
                          "peak_source": f"{src} bf16 burst", "ms": gemm_ms},
+            "attention_roofline": {"kernel": "flash_prefill_tc_kernel (tcgen05), causal 8x2048, 32q/8kv, d128",
+                                   "bound": "tensor", "achieved": fa_flops / (fa_ms / 1e3) / 1e12, "peak": tf_burst,
+                                   "unit": "TFLOP/s", "frac": fa_flops / (fa_ms / 1e3) / 1e12 / tf_burst,
+                                   "peak_source": f"{src} bf16 burst", "ms": fa_ms},
         },
         "roofline": {"kernel": "paged_decode_kernel (+combine), B64 ctx2048 32q/8kv", "bound": "hbm",
                      "achieved": att_bytes / (att_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
@@ -1114,7 +1143,8 @@ def main():
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
     ap.add_argument("--no-deepseek", action="store_true", help="skip the DeepSeek-V2-Lite section")
     ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
-    ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "mla_decode", "moe_gemm"],
+    ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "prefill_attention", "mla_decode",
+                                                 "moe_gemm"],
                     help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1129,7 +1159,8 @@ def main():
 
         dev = torch.device("cuda", local_rank)
         fn = {"decode_attention": kernel_roofline_decode_attention, "prefill_gemm": kernel_roofline_prefill_gemm,
-              "mla_decode": kernel_roofline_mla_decode, "moe_gemm": kernel_roofline_moe_gemm}[args.profile_kernel]
+              "prefill_attention": kernel_roofline_prefill_attention, "mla_decode": kernel_roofline_mla_decode,
+              "moe_gemm": kernel_roofline_moe_gemm}[args.profile_kernel]
         ms, work = fn(capi.lib(), torch, dev, reps=3)
         print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
         return
