@@ -365,6 +365,43 @@ B200_API int b200_scatter_add_rows(void* hidden, int64_t rows, int64_t dim, cons
 /* out[r] = argmax_j logits[r, j] (lowest index on ties), logits [rows, vocab] bf16. */
 B200_API int b200_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t ld, int64_t* out, b200_stream_t stream);
 
+/* -------------------------------------------------------- image preprocess */
+
+/* Qwen3-VL SmartResize (host, no GPU): the nearest multiple of factor per
+ * side (size / factor rounded half to even in float32), scaled down to
+ * max_pixels or up to min_pixels when outside (factor = patch * merge).
+ * Same result as SmartResize (atb_cpp_llm/src/adapters/qwen3vl_embedding/
+ * qwen3vl_preprocess.cpp:219-243). */
+B200_API int b200_smart_resize(int height, int width, int factor, int min_pixels, int max_pixels, int* new_height,
+                               int* new_width);
+/* Device scratch for one resize of a [C, H, W] image to (new_h, new_w):
+ * both axes' fixed-point coefficients and the horizontal-pass image. */
+B200_API int64_t b200_preprocess_workspace_bytes(int channels, int height, int width, int new_height,
+                                                 int new_width);
+/* Pillow's BICUBIC Image.resize on 8-bit planes, bit-exact: image [C, H, W]
+ * uint8 (device) -> out [C, out_h, out_w] uint8 (device).  Antialiased
+ * (support 2 x max(1, in/out)), coefficients quantised to 22 fractional bits,
+ * horizontal then vertical pass each clipped to [0, 255], an unchanged axis
+ * not resampled.  Replaces BicubicResize / ResampleCore8bpc
+ * (qwen3vl_preprocess.cpp:52-207) and the device path of PreprocessImageNpu
+ * (qwen3vl_preprocess.cpp:369-824). */
+B200_API int b200_bicubic_resize_u8(const uint8_t* image, int channels, int height, int width, int out_h, int out_w,
+                                    uint8_t* out, void* workspace, int64_t workspace_bytes, b200_stream_t stream);
+/* The whole Qwen3-VL processor on the GPU: SmartResize, the bicubic resample,
+ * (v/255 - mean[c]) / std[c] in float32 (mean / std NULL: 0.5), and the
+ * patchify in merge-block order with the frame duplicated over the temporal
+ * patch, written as pixel_values [num_patches, C*tp*ps*ps] (out_dtype 1:
+ * fp16 as the reference, 0: bf16) on the device.  num_patches and grid_thw
+ * [3] = (1, new_h/ps, new_w/ps) are host outputs, known before the kernels
+ * run.  Replaces PreprocessImage (qwen3vl_preprocess.cpp:245-366); fp16
+ * output equals the reference's bit for bit.  workspace: at least
+ * b200_preprocess_workspace_bytes(C, H, W, new_h, new_w) (256-byte aligned). */
+B200_API int b200_preprocess_image(const uint8_t* image, int channels, int height, int width, int patch_size,
+                                   int temporal_patch_size, int merge_size, int min_pixels, int max_pixels,
+                                   const float* mean, const float* stdv, int out_dtype, void* pixel_values,
+                                   int64_t pixel_capacity, int64_t* num_patches, int64_t* grid_thw, void* workspace,
+                                   int64_t workspace_bytes, b200_stream_t stream);
+
 /* --------------------------------------------------------- tensor parallel */
 
 /* A tensor-parallel group of `world` (<= 8) processes, one GPU each: an NCCL
