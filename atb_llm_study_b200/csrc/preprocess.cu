@@ -10,18 +10,20 @@
 // fixed-point arithmetic (coefficients quantised to 22 fractional bits,
 // int32 accumulation from 2^21, clip of >> 22), so results equal PIL's.
 //
-// Work per image: one horizontal-pass kernel (one thread per output sample,
-// uint8 intermediate [C, H, out_w]) and one vertical-pass kernel that also
+// Work per image: the fixed-point coefficients of both axes (one small
+// kernel, FMA-free double arithmetic identical to the host's), one
+// horizontal-pass kernel (one thread per output sample, uint8 intermediate
+// [C, H, out_w]) and one vertical-pass kernel that also
 // normalises and scatters each value to its patch positions (frame 0 and the
 // duplicated frames).  An axis whose size does not change is not resampled
 // (the horizontal pass is skipped; the vertical pass runs with one unit tap,
-// which reproduces the input byte exactly).  HBM-bound byte work: no tensor
-// cores; grids are sized in whole waves of 256-thread blocks.
+// which reproduces the input byte exactly).  HBM-bound byte work, no tensor
+// cores: 2-D grids (256 samples of one row per block) keep the index math in
+// 32-bit and the row reads coalesced.
 #include <cuda_fp16.h>
 #include <math.h>
 
 #include <algorithm>
-#include <vector>
 
 #include "common.cuh"
 
@@ -31,131 +33,202 @@ namespace {
 
 constexpr int kPrecisionBits = 22;
 constexpr int kThreads = 256;
+constexpr int kRowsPerBlock = 8;  // image rows one block walks through
 
 __device__ __forceinline__ uint8_t clip8(int v) {
   const int s = v >> kPrecisionBits;  // arithmetic shift
   return (uint8_t)(s < 0 ? 0 : (s > 255 ? 255 : s));
 }
 
-// out[c][y][xx] = clip8(2^21 + sum_x in[c][y][xmin + x] * k[xx][x])
-__global__ void __launch_bounds__(kThreads) resample_h_kernel(const uint8_t* __restrict__ in, int C, int H, int W,
+// out[c][y][xx] = clip8(2^21 + sum_x in[c][y][xmin + x] * k[xx][x]);
+// grid (out_w / 256, C*H): 256 consecutive output samples of one row per
+// block; the input bytes their windows cover (monotone in xx) are staged in
+// shared memory once.
+template <int KMAX>
+__global__ void __launch_bounds__(kThreads) resample_h_kernel(const uint8_t* __restrict__ in, int rows, int W,
                                                                int out_w, int ksize, const int* __restrict__ bounds,
-                                                               const int* __restrict__ coef, uint8_t* __restrict__ out) {
+                                                               const int* __restrict__ coef, uint8_t* __restrict__ out,
+                                                               int span_cap) {
   pdl_trigger();
   pdl_wait();
-  const int64_t n = (int64_t)C * H * out_w;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int xx = (int)(i % out_w);
-    const int64_t row = i / out_w;  // c * H + y
-    const int x0 = bounds[2 * xx], taps = bounds[2 * xx + 1];
-    const uint8_t* src = in + row * W + x0;
-    const int* k = coef + (int64_t)xx * ksize;
-    int ss = 1 << (kPrecisionBits - 1);
-    for (int x = 0; x < taps; ++x) ss += (int)src[x] * k[x];
-    out[i] = clip8(ss);
+  extern __shared__ uint8_t span[];
+  const int xx0 = blockIdx.x * kThreads;
+  const int last = min(xx0 + kThreads, out_w) - 1;
+  const int lo = bounds[2 * xx0];
+  const int hi = min(bounds[2 * last] + bounds[2 * last + 1], lo + span_cap);
+  const int xx = xx0 + threadIdx.x;
+  const bool active = xx <= last;
+  const int x0 = active ? bounds[2 * xx] - lo : 0;
+  const int taps = active ? min(bounds[2 * xx + 1], hi - lo - x0) : 0;
+  // this sample's taps stay in registers for all the block's rows
+  int kr[KMAX];
+#pragma unroll
+  for (int x = 0; x < KMAX; ++x) kr[x] = x < taps ? coef[(int64_t)xx * ksize + x] : 0;
+  const int r1 = min(rows, (int)(blockIdx.y + 1) * kRowsPerBlock);
+  for (int r = blockIdx.y * kRowsPerBlock; r < r1; ++r) {
+    const uint8_t* row = in + (int64_t)r * W;
+    for (int i = threadIdx.x; i < hi - lo; i += kThreads) span[i] = row[lo + i];
+    __syncthreads();
+    if (active) {
+      int ss = 1 << (kPrecisionBits - 1);
+#pragma unroll
+      for (int x = 0; x < KMAX; ++x)
+        if (x < taps) ss += (int)span[x0 + x] * kr[x];
+      out[(int64_t)r * out_w + xx] = clip8(ss);
+    }
+    __syncthreads();
   }
 }
 
 // Vertical pass over in [C, H, out_w] to rows of out_h; MODE 0 writes the
 // uint8 image [C, out_h, out_w]; MODE 1 / 2 write (v/255 - mean)/std as fp16 /
 // bf16 into the patch layout (merge-block order, frame duplicated over tp).
-template <int MODE>
-__global__ void __launch_bounds__(kThreads) resample_v_kernel(const uint8_t* __restrict__ in, int C, int H, int out_h,
-                                                               int out_w, int ksize, const int* __restrict__ bounds,
+// grid (out_w / (256 VEC), C*out_h): VEC consecutive samples of one row per
+// thread (4-byte loads of each tap row); the 256 normalised values of the
+// block's channel are precomputed once per block (same float32 arithmetic,
+// so the table holds exactly the values the formula gives).
+template <int MODE, int VEC, int KMAX>
+__global__ void __launch_bounds__(kThreads) resample_v_kernel(const uint8_t* __restrict__ in, int C, int H,
+                                                               int out_h, int out_w, int ksize,
+                                                               const int* __restrict__ bounds,
                                                                const int* __restrict__ coef, void* __restrict__ out,
                                                                float3 mean, float3 stdv, int ps, int tp, int ms) {
   pdl_trigger();
+  __shared__ uint16_t lut[256];
+  const int row_blocks = (out_h + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int c = blockIdx.y / row_blocks;
+  const int yy0 = (blockIdx.y - c * row_blocks) * kRowsPerBlock, yy1 = min(out_h, yy0 + kRowsPerBlock);
+  if (MODE != 0) {
+    // the reference's order of operations: (u / 255 - mean) / std in float32
+    const float m = c == 0 ? mean.x : (c == 1 ? mean.y : mean.z);
+    const float sd = c == 0 ? stdv.x : (c == 1 ? stdv.y : stdv.z);
+    const float v = ((float)threadIdx.x / 255.0f - m) / sd;
+    if (MODE == 1) lut[threadIdx.x] = __half_as_ushort(__float2half_rn(v));
+    else lut[threadIdx.x] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
   pdl_wait();
-  const int64_t n = (int64_t)C * out_h * out_w;
-  const int gw = out_w / ps;
+  __syncthreads();
+  const int xx = (blockIdx.x * kThreads + threadIdx.x) * VEC;
+  if (xx >= out_w) return;
+  const int gx = xx / ps, px = xx - gx * ps;
+  const int gwm = out_w / ps / ms;
   const int64_t pdim = (int64_t)C * tp * ps * ps;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int xx = (int)(i % out_w);
-    const int64_t r = i / out_w;
-    const int yy = (int)(r % out_h);
-    const int c = (int)(r / out_h);
+  for (int yy = yy0; yy < yy1; ++yy) {
     const int y0 = bounds[2 * yy], taps = bounds[2 * yy + 1];
     const uint8_t* src = in + ((int64_t)c * H + y0) * out_w + xx;
-    const int* k = coef + (int64_t)yy * ksize;
-    int ss = 1 << (kPrecisionBits - 1);
-    for (int y = 0; y < taps; ++y) ss += (int)src[(int64_t)y * out_w] * k[y];
-    const uint8_t u = clip8(ss);
-    if (MODE == 0) {
-      static_cast<uint8_t*>(out)[i] = u;
-    } else {
-      // the reference's order of operations: (u / 255 - mean) / std, float32
-      const float m = c == 0 ? mean.x : (c == 1 ? mean.y : mean.z);
-      const float s = c == 0 ? stdv.x : (c == 1 ? stdv.y : stdv.z);
-      const float v = ((float)u / 255.0f - m) / s;
-      // patch (gy, gx) in merge-block order, element (c, f, py, px)
-      const int gy = yy / ps, py = yy % ps, gx = xx / ps, px = xx % ps;
-      const int64_t patch = (((int64_t)(gy / ms) * (gw / ms) + gx / ms) * ms + gy % ms) * ms + gx % ms;
-      const int64_t base = patch * pdim + (int64_t)c * tp * ps * ps + (int64_t)py * ps + px;
-      for (int f = 0; f < tp; ++f) {
-        if (MODE == 1) static_cast<__half*>(out)[base + (int64_t)f * ps * ps] = __float2half_rn(v);
-        else static_cast<__nv_bfloat16*>(out)[base + (int64_t)f * ps * ps] = __float2bfloat16_rn(v);
+    const int* k = coef + yy * ksize;
+    int ss[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) ss[e] = 1 << (kPrecisionBits - 1);
+#pragma unroll
+    for (int y = 0; y < KMAX; ++y) {
+      if (y >= taps) break;
+      const int ky = k[y];
+      if (VEC == 4) {
+        const uchar4 q = *reinterpret_cast<const uchar4*>(src + (int64_t)y * out_w);
+        ss[0] += (int)q.x * ky;
+        ss[1] += (int)q.y * ky;
+        ss[2] += (int)q.z * ky;
+        ss[3] += (int)q.w * ky;
+      } else {
+        ss[0] += (int)src[(int64_t)y * out_w] * ky;
       }
+    }
+    if (MODE == 0) {
+      uint8_t* o = static_cast<uint8_t*>(out) + ((int64_t)c * out_h + yy) * out_w + xx;
+      if (VEC == 4) *reinterpret_cast<uchar4*>(o) = make_uchar4(clip8(ss[0]), clip8(ss[1]), clip8(ss[2]), clip8(ss[3]));
+      else o[0] = clip8(ss[0]);
+      continue;
+    }
+    // patch (gy, gx) in merge-block order, element (c, f, py, px); the VEC
+    // samples stay inside one patch row (ps % VEC == 0)
+    const int gy = yy / ps, py = yy - gy * ps;
+    const int64_t patch = ((int64_t)((gy / ms) * gwm + gx / ms) * ms + gy % ms) * ms + gx % ms;
+    uint16_t* o = static_cast<uint16_t*>(out) + patch * pdim + ((int64_t)c * tp * ps + py) * ps + px;
+    if (VEC == 4) {
+      const uint2 w = make_uint2((uint32_t)lut[clip8(ss[0])] | ((uint32_t)lut[clip8(ss[1])] << 16),
+                                 (uint32_t)lut[clip8(ss[2])] | ((uint32_t)lut[clip8(ss[3])] << 16));
+      for (int f = 0; f < tp; ++f) *reinterpret_cast<uint2*>(o + (int64_t)f * ps * ps) = w;
+    } else {
+      const uint16_t w = lut[clip8(ss[0])];
+      for (int f = 0; f < tp; ++f) o[(int64_t)f * ps * ps] = w;
     }
   }
 }
 
-// ---- host: Pillow's coefficient computation for one axis ----
-double bicubic(double x) {
+// ---- Pillow's coefficients for one axis, computed on the device ----
+// Every double operation is an explicit round-to-nearest intrinsic, so none
+// is fused into an FMA and the values equal the host computation (Pillow's
+// precompute_coeffs + normalize_coeffs_8bpc as the reference ports it,
+// qwen3vl_preprocess.cpp:38-99) bit for bit.
+__device__ __forceinline__ double bicubic_d(double x) {
   const double a = -0.5;
   x = fabs(x);
-  if (x < 1.0) return ((a + 2.0) * x - (a + 3.0)) * x * x + 1.0;
-  if (x < 2.0) return (((x - 5.0) * x + 8.0) * x - 4.0) * a;
+  if (x < 1.0)  // ((a + 2) x - (a + 3)) x x + 1
+    return __dadd_rn(__dmul_rn(__dmul_rn(__dsub_rn(__dmul_rn(__dadd_rn(a, 2.0), x), __dadd_rn(a, 3.0)), x), x), 1.0);
+  if (x < 2.0)  // (((x - 5) x + 8) x - 4) a
+    return __dmul_rn(__dsub_rn(__dmul_rn(__dadd_rn(__dmul_rn(__dsub_rn(x, 5.0), x), 8.0), x), 4.0), a);
   return 0.0;
+}
+
+constexpr int kMaxTaps = 256;  // downscale factors up to 63x per axis
+
+// blockIdx.y = axis (0: vertical, 1: horizontal); one thread per output sample.
+// bounds[2*o] = first tap, bounds[2*o+1] = taps; coef[o*ksize + t] in 22-bit
+// fixed point.  An axis that keeps its size gets one unit tap per sample.
+__global__ void __launch_bounds__(kThreads) coeffs_kernel(int in_v, int out_v, int ks_v, int* bounds_v, int* coef_v,
+                                                           int in_h, int out_h, int ks_h, int* bounds_h,
+                                                           int* coef_h) {
+  pdl_trigger();
+  pdl_wait();
+  const bool horiz = blockIdx.y == 1;
+  const int in = horiz ? in_h : in_v, out = horiz ? out_h : out_v, ks = horiz ? ks_h : ks_v;
+  int* bounds = horiz ? bounds_h : bounds_v;
+  int* coef = horiz ? coef_h : coef_v;
+  if (!bounds || !coef) return;
+  for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < out; o += gridDim.x * blockDim.x) {
+    int* k = coef + (int64_t)o * ks;
+    if (in == out) {
+      bounds[2 * o] = o;
+      bounds[2 * o + 1] = 1;
+      k[0] = 1 << kPrecisionBits;
+      continue;
+    }
+    const double scale = __ddiv_rn((double)in, (double)out);
+    const double filterscale = scale < 1.0 ? 1.0 : scale;
+    const double support = __dmul_rn(2.0, filterscale);
+    const double center = __dmul_rn(__dadd_rn((double)o, 0.5), scale);
+    const double rss = __ddiv_rn(1.0, filterscale);
+    int xmin = __double2int_rz(__dadd_rn(__dsub_rn(center, support), 0.5));
+    if (xmin < 0) xmin = 0;
+    int xmax = __double2int_rz(__dadd_rn(__dadd_rn(center, support), 0.5));
+    if (xmax > in) xmax = in;
+    xmax -= xmin;
+    if (xmax > ks) xmax = ks;  // never taken: ks = 2 ceil(support) + 1 covers every window
+    double w[kMaxTaps];
+    double ww = 0.0;
+    for (int x = 0; x < xmax; ++x) {
+      w[x] = bicubic_d(__dmul_rn(__dadd_rn(__dsub_rn((double)(x + xmin), center), 0.5), rss));
+      ww = __dadd_rn(ww, w[x]);
+    }
+    for (int x = 0; x < ks; ++x) {
+      int q = 0;
+      if (x < xmax) {
+        const double v = ww != 0.0 ? __ddiv_rn(w[x], ww) : w[x];
+        const double f = __dmul_rn(v, (double)(1 << kPrecisionBits));
+        q = v < 0 ? __double2int_rz(__dadd_rn(-0.5, f)) : __double2int_rz(__dadd_rn(0.5, f));
+      }
+      k[x] = q;
+    }
+    bounds[2 * o] = xmin;
+    bounds[2 * o + 1] = xmax;
+  }
 }
 
 int ksize_of(int in_size, int out_size) {
   const double scale = (double)in_size / out_size;
   const double support = 2.0 * (scale < 1.0 ? 1.0 : scale);
   return (int)ceil(support) * 2 + 1;
-}
-
-// bounds[2*o] = first tap, bounds[2*o+1] = taps; coef[o*ksize + t] in 22-bit fixed point
-int axis_coeffs(int in_size, int out_size, std::vector<int>& bounds, std::vector<int>& coef) {
-  const double scale = (double)in_size / out_size;
-  const double filterscale = scale < 1.0 ? 1.0 : scale;
-  const double support = 2.0 * filterscale;
-  const int ksize = (int)ceil(support) * 2 + 1;
-  bounds.assign((size_t)out_size * 2, 0);
-  coef.assign((size_t)out_size * ksize, 0);
-  std::vector<double> w(ksize);
-  for (int o = 0; o < out_size; ++o) {
-    const double center = (o + 0.5) * scale;
-    const double rss = 1.0 / filterscale;
-    int xmin = (int)(center - support + 0.5);  // C cast: truncation toward zero
-    if (xmin < 0) xmin = 0;
-    int xmax = (int)(center + support + 0.5);
-    if (xmax > in_size) xmax = in_size;
-    xmax -= xmin;
-    double ww = 0.0;
-    for (int x = 0; x < xmax; ++x) {
-      w[x] = bicubic((x + xmin - center + 0.5) * rss);
-      ww += w[x];
-    }
-    for (int x = 0; x < xmax; ++x) {
-      const double v = ww != 0.0 ? w[x] / ww : w[x];
-      coef[(size_t)o * ksize + x] = v < 0 ? (int)(-0.5 + v * (1 << kPrecisionBits))
-                                          : (int)(0.5 + v * (1 << kPrecisionBits));
-    }
-    bounds[(size_t)o * 2] = xmin;
-    bounds[(size_t)o * 2 + 1] = xmax;
-  }
-  return ksize;
-}
-
-// one unit tap per output row: the vertical pass then reproduces its input
-int identity_coeffs(int n, std::vector<int>& bounds, std::vector<int>& coef) {
-  bounds.resize((size_t)n * 2);
-  coef.assign((size_t)n, 1 << kPrecisionBits);
-  for (int i = 0; i < n; ++i) {
-    bounds[(size_t)i * 2] = i;
-    bounds[(size_t)i * 2 + 1] = 1;
-  }
-  return 1;
 }
 
 int64_t align256(int64_t b) { return (b + 255) & ~int64_t(255); }
@@ -185,14 +258,6 @@ Layout layout(int C, int H, int W, int oh, int ow) {
   return L;
 }
 
-unsigned grid_for(int64_t n) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t blocks = (n + kThreads - 1) / kThreads;
-  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * 8));
-}
-
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? B200_OK : B200_ERROR_CUDA_BASE - (int)e; }
 
 // Resample image [C,H,W] (device) to (oh, ow); MODE as resample_v_kernel.
@@ -201,44 +266,62 @@ int run_resample(int mode, const uint8_t* image, int C, int H, int W, int oh, in
   const Layout L = layout(C, H, W, oh, ow);
   if (!ws || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255)) return B200_ERROR_INVALID_PARAM;
   uint8_t* w8 = static_cast<uint8_t*>(ws);
-  std::vector<int> bh, ch, bv, cv;
-  const bool need_h = ow != W, need_v = oh != H;
-  int ksv = need_v ? axis_coeffs(H, oh, bv, cv) : identity_coeffs(oh, bv, cv);
-  if (need_h) {
-    axis_coeffs(W, ow, bh, ch);
-    int rc = cuda_rc(cudaMemcpyAsync(w8 + L.off_bh, bh.data(), bh.size() * 4, cudaMemcpyHostToDevice, st));
-    if (rc == B200_OK)
-      rc = cuda_rc(cudaMemcpyAsync(w8 + L.off_ch, ch.data(), ch.size() * 4, cudaMemcpyHostToDevice, st));
-    if (rc != B200_OK) return rc;
-  }
-  int rc = cuda_rc(cudaMemcpyAsync(w8 + L.off_bv, bv.data(), bv.size() * 4, cudaMemcpyHostToDevice, st));
-  if (rc == B200_OK) rc = cuda_rc(cudaMemcpyAsync(w8 + L.off_cv, cv.data(), cv.size() * 4, cudaMemcpyHostToDevice, st));
-  if (rc != B200_OK) return rc;
+  const bool need_h = ow != W;
+  if (L.ksh > kMaxTaps || L.ksv > kMaxTaps) return B200_ERROR_UNSUPPORTED;
+  // grid rows: kRowsPerBlock image rows each
+  if ((int64_t)C * (std::max(H, oh) / kRowsPerBlock + 1) > 65535) return B200_ERROR_UNSUPPORTED;
+  int* bv = reinterpret_cast<int*>(w8 + L.off_bv);
+  int* cv = reinterpret_cast<int*>(w8 + L.off_cv);
+  int* bh = need_h ? reinterpret_cast<int*>(w8 + L.off_bh) : nullptr;
+  int* ch = need_h ? reinterpret_cast<int*>(w8 + L.off_ch) : nullptr;
+  const int most = std::max(oh, ow);
+  launch_kernel(coeffs_kernel, dim3((unsigned)((most + kThreads - 1) / kThreads), 2), kThreads, 0, st, H, oh, L.ksv,
+                bv, cv, W, ow, L.ksh, bh, ch);
+  B200_CHECK_LAUNCH();
   const uint8_t* vin = image;
   if (need_h) {
-    const int64_t n = (int64_t)C * H * ow;
-    launch_kernel(resample_h_kernel, dim3(grid_for(n)), kThreads, 0, st, image, C, H, W, ow, L.ksh,
-                  reinterpret_cast<const int*>(w8 + L.off_bh), reinterpret_cast<const int*>(w8 + L.off_ch),
-                  w8 + L.off_tmp);
+    // bytes the widest block's windows span: 256 samples x the scale + one window
+    const int span_cap = (int)ceil((double)W / ow * kThreads) + L.ksh + 8;
+    if (span_cap > 160 * 1024) return B200_ERROR_UNSUPPORTED;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (span_cap > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
+      for (auto f : {resample_h_kernel<8>, resample_h_kernel<16>, resample_h_kernel<32>, resample_h_kernel<64>})
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) != cudaSuccess)
+          return B200_ERROR_UNSUPPORTED;
+      attr[dev] = true;
+    }
+    const dim3 gh((unsigned)((ow + kThreads - 1) / kThreads), (unsigned)((C * H + kRowsPerBlock - 1) / kRowsPerBlock));
+#define B200_RH(K) \
+  launch_kernel(resample_h_kernel<K>, gh, kThreads, (size_t)span_cap, st, image, C * H, W, ow, L.ksh, bh, ch, \
+                w8 + L.off_tmp, span_cap)
+    if (L.ksh <= 8) B200_RH(8);
+    else if (L.ksh <= 16) B200_RH(16);
+    else if (L.ksh <= 32) B200_RH(32);
+    else if (L.ksh <= 64) B200_RH(64);
+    else return B200_ERROR_UNSUPPORTED;
+#undef B200_RH
     B200_CHECK_LAUNCH();
     vin = w8 + L.off_tmp;
   }
-  const int64_t n = (int64_t)C * oh * ow;
-  const dim3 g(grid_for(n));
-  const int* vb = reinterpret_cast<const int*>(w8 + L.off_bv);
-  const int* vc = reinterpret_cast<const int*>(w8 + L.off_cv);
-  if (mode == 0)
-    launch_kernel(resample_v_kernel<0>, g, kThreads, 0, st, vin, C, H, oh, ow, ksv, vb, vc, out, mean, stdv, ps, tp,
-                  ms);
-  else if (mode == 1)
-    launch_kernel(resample_v_kernel<1>, g, kThreads, 0, st, vin, C, H, oh, ow, ksv, vb, vc, out, mean, stdv, ps, tp,
-                  ms);
-  else
-    launch_kernel(resample_v_kernel<2>, g, kThreads, 0, st, vin, C, H, oh, ow, ksv, vb, vc, out, mean, stdv, ps, tp,
-                  ms);
+  const bool vec = ow % 4 == 0 && (reinterpret_cast<uintptr_t>(vin) & 3) == 0 && (mode == 0 || ps % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(out) & (mode == 0 ? 3 : 7)) == 0;
+  const int per = vec ? 4 : 1;
+  const dim3 g((unsigned)((ow + kThreads * per - 1) / (kThreads * per)),
+               (unsigned)(C * ((oh + kRowsPerBlock - 1) / kRowsPerBlock)));
+  const int ksv = L.ksv;
+#define B200_RVK(M, V, K)                                                                                     \
+  launch_kernel(resample_v_kernel<M, V, K>, g, kThreads, 0, st, vin, C, H, oh, ow, ksv, bv, cv, out, mean, stdv, ps, \
+                tp, ms)
+#define B200_RV(M, V) \
+  (ksv <= 16 ? B200_RVK(M, V, 16) : ksv <= 64 ? B200_RVK(M, V, 64) : B200_RVK(M, V, 256))
+  if (mode == 0) vec ? B200_RV(0, 4) : B200_RV(0, 1);
+  else if (mode == 1) vec ? B200_RV(1, 4) : B200_RV(1, 1);
+  else vec ? B200_RV(2, 4) : B200_RV(2, 1);
+#undef B200_RVK
+#undef B200_RV
   B200_CHECK_LAUNCH();
-  // the host coefficient vectors were copied from pageable memory: the copies
-  // have completed when cudaMemcpyAsync returned, so they may be freed now
   return B200_OK;
 }
 

@@ -436,6 +436,84 @@ def bench_qwen3vl(L, torch, dev, steps, warm, stream_of):
         L.b200_engine_destroy(eng)
 
 
+PP_H, PP_W = 1080, 1920  # a 1080p RGB frame, resized to 992 x 1792 (3472 patches)
+
+
+def bench_preprocess(L, torch, dev, steps, warm, cpu_baseline=True):
+    """Qwen3-VL image preprocessing of one 1080x1920 RGB frame on the GPU
+    (SmartResize to 992x1792, Pillow-exact bicubic, normalise, patchify into
+    fp16 pixel values [3472, 1536]).  value: image resident in HBM; e2e: the
+    uint8 frame copied from pinned host memory every step (the pixel values
+    stay on the device for the vision tower).  Algorithmic bytes = the uint8
+    frame read + the fp16 pixel values written.  cpu_baseline: the oracle
+    port of the reference's CPU PreprocessImage on the same frame."""
+    import numpy as np
+
+    C = 3
+    rng = np.random.default_rng(11)
+    img = rng.integers(0, 256, (C, PP_H, PP_W), dtype=np.uint8)
+    nh, nw = ctypes.c_int(), ctypes.c_int()
+    check(L.b200_smart_resize(PP_H, PP_W, 32, 4096, 1843200, ctypes.byref(nh), ctypes.byref(nw)), "smart_resize")
+    n = (nh.value // 16) * (nw.value // 16)
+    pdim = C * 2 * 16 * 16
+    pv = torch.empty(n, pdim, dtype=torch.float16, device=dev)
+    wsb = L.b200_preprocess_workspace_bytes(C, PP_H, PP_W, nh.value, nw.value)
+    ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
+    img_dev = torch.from_numpy(img).to(dev)
+    img_pinned = torch.from_numpy(img).pin_memory()
+    npatch = ctypes.c_int64()
+    grid = (ctypes.c_int64 * 3)()
+
+    def run(src):
+        check(L.b200_preprocess_image(src.data_ptr(), C, PP_H, PP_W, 16, 2, 2, 4096, 1843200, None, None, 1,
+                                      pv.data_ptr(), pv.numel(), ctypes.byref(npatch), grid, ws.data_ptr(), wsb,
+                                      torch.cuda.current_stream(dev).cuda_stream), "preprocess_image")
+
+    staging = torch.empty_like(img_dev)
+
+    def e2e_step():
+        staging.copy_(img_pinned, non_blocking=True)
+        run(staging)
+
+    def timed(fn, reps):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    reps = max(20, steps)
+    ms = timed(lambda: run(img_dev), reps)
+    e2e_ms = timed(e2e_step, reps)
+    nbytes = img.nbytes + n * pdim * 2
+    hbm, _, _, src = peaks()
+    out = {"workload": f"Qwen3-VL image preprocessing: {C}x{PP_H}x{PP_W} uint8 -> {nh.value}x{nw.value} "
+                       f"-> fp16 pixel values [{n}, {pdim}]",
+           "images_per_s": 1e3 / ms, "ms_per_image": ms, "e2e_images_per_s": 1e3 / e2e_ms,
+           "e2e_h2d_bytes": img.nbytes, "gpu_launches_per_image": 3,
+           "roofline": {"bound": "hbm", "bytes_per_image": nbytes, "achieved": nbytes / (ms / 1e3) / 1e9,
+                        "peak": hbm, "unit": "GB/s", "frac": nbytes / (ms / 1e3) / 1e9 / hbm,
+                        "peak_source": f"{src} copy"}}
+    if cpu_baseline:
+        import time
+
+        from oracle.preprocess import preprocess_image
+
+        t0 = time.perf_counter()
+        preprocess_image(img)
+        cpu_s = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": 1.0 / cpu_s, "unit": "images/s", "cores": 1, "kind": "port",
+                               "sample": "one 1080x1920 frame through the numpy port of the reference's "
+                                         "CPU PreprocessImage"}
+    del pv, ws, img_dev, staging
+    return out
+
+
 MIXTRAL_8X7B = dict(model_type="mixtral", hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
                     num_key_value_heads=8, intermediate_size=14336, num_local_experts=8, num_experts_per_tok=2,
                     vocab_size=32000, rms_norm_eps=1e-5, rope_theta=1e6, tie_word_embeddings=False)
@@ -1009,6 +1087,8 @@ def run_b200(args, rank, world, local_rank):
                              MX_PREFILL_SEQS, MX_PREFILL_LEN, MX_BATCH, MX_CTX,
                              "one Mixtral-8x7B sharded over all ranks: every expert's width split, router replicated")
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+    pp = None if args.no_vl else bench_preprocess(L, torch, dev, steps, warm,
+                                                  cpu_baseline=rank == 0 and not args.no_cpu_baseline)
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
 
@@ -1083,6 +1163,8 @@ def run_b200(args, rank, world, local_rank):
         result["expert_parallel_mixtral"] = ep_mx
     if vl:
         result["qwen3vl_embedding"] = vl
+    if pp:
+        result["image_preprocess"] = pp
     if mx:
         result["mixtral_8x7b"] = mx
     if ds:
@@ -1182,7 +1264,10 @@ def main():
             return torch.cuda.ExternalStream(s.value, device=dev)
 
         fn = bench_qwen3vl if args.vl_only else bench_mixtral if args.mixtral_only else bench_deepseek
-        print(json.dumps(fn(L, torch, dev, args.steps, args.warmup, stream_of)), flush=True)
+        res = fn(L, torch, dev, args.steps, args.warmup, stream_of)
+        if args.vl_only:
+            res["image_preprocess"] = bench_preprocess(L, torch, dev, args.steps, args.warmup)
+        print(json.dumps(res), flush=True)
         return
     run_b200(args, rank, world, local_rank)
 
