@@ -92,6 +92,19 @@ B200_API int b200_get_rope_index(const int64_t* input_ids, int64_t batch, int64_
                                  int64_t image_token_id, int64_t vision_start_token_id, int64_t spatial_merge_size,
                                  int64_t* position_ids);
 
+/* b200_get_rope_index on the GPU: input_ids, attention_mask (or NULL),
+ * image_grid_thw and position_ids are device arrays; the same positions,
+ * bit for bit (one CTA walks the rows; block scans compact the mask and find
+ * the image runs).  workspace: b200_rope_index_workspace_bytes(seq_len).
+ * Grids with a zero or negative dimension (which the host call rejects) set
+ * the device error word and end that row's image layout. */
+B200_API int64_t b200_rope_index_workspace_bytes(int64_t seq_len);
+B200_API int b200_get_rope_index_device(const int64_t* input_ids, int64_t batch, int64_t seq_len,
+                                        const int64_t* attention_mask, const int64_t* image_grid_thw,
+                                        int64_t num_images, int64_t image_token_id, int64_t vision_start_token_id,
+                                        int64_t spatial_merge_size, int64_t* position_ids, void* workspace,
+                                        int64_t workspace_bytes, b200_stream_t stream);
+
 /* cos/sin tables [T, head_dim] (fp32) for standard 1-D rope from positions [T].
  * Replaces Rope1D::Compute (atb_cpp_llm/src/components/common/rope_1d.h:23-167). */
 B200_API int b200_rope_table_1d(const int64_t* positions, int64_t T, int head_dim, float theta, float* cos_out,
