@@ -349,8 +349,9 @@ Status VisionModel::RunTower(int64_t N, const int64_t* grid_thw, int num_images,
                         bf(qkv_b_, l * 3 * H), nullptr, 0));
     launches_ += 2;
     B200_RETURN_IF(b200_rope_apply(qkv, N, 2 * nh, (int)hd, 3 * H, cos_.as<float>(), sin_.as<float>(), st));
-    B200_RETURN_IF(b200_flash_prefill(qkv, 3 * H, qkv + H, qkv + 2 * H, 3 * H, attn_.data, H, cu_.as<int32_t>(),
-                                      (int)frames, max_len, nh, nh, (int)hd, scale, 0, st));
+    B200_RETURN_IF(b200_flash_prefill_packed(qkv, 3 * H, hd, qkv + H, 3 * H, hd, qkv + 2 * H, 3 * H, hd, attn_.data,
+                                             H, hd, cu_.as<int32_t>(), (int)frames, max_len, N, nh, nh, (int)hd,
+                                             (int)hd, scale, 0, st));
     B200_RETURN_IF(Gemm(attn_.data, H, bf(proj_w_, l * H * H), h_.data, H, N, H, H, B200_EPI_BIAS_RESIDUAL,
                         bf(proj_b_, l * H), h_.data, H));
     ++launches_;

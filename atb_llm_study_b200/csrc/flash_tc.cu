@@ -1,4 +1,4 @@
-// Prefill attention on the 5th-generation tensor cores (128-wide heads).
+// Prefill attention on the 5th-generation tensor cores (64- or 128-wide heads).
 //
 // One CTA = 128 query rows of one head of one sequence, 192 threads:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
@@ -34,12 +34,18 @@ namespace {
 constexpr int kThreads = 192;
 constexpr int kTile = 128;                    // query rows per CTA = keys per tile
 constexpr int kBoxBytes = kTile * 128;        // 128 rows x 64 bf16 (one 128-byte swizzle span)
-constexpr int kTileBytes = 2 * kBoxBytes;     // 128 rows x 128 dims
-constexpr int kSmem = 6 * kTileBytes + 1024 + 256;  // Q, K x2, V x2, P + alignment + barriers
+constexpr int kPBytes = 2 * kBoxBytes;        // P: 128 rows x 128 keys
+// head width HD (64 or 128): Q, K and V tiles are HD / 64 boxes of 128 rows
+template <int HD>
+struct TcCfg {
+  static constexpr int BOXES = HD / 64;
+  static constexpr int TILE = BOXES * kBoxBytes;
+  static constexpr int SMEM = 5 * TILE + kPBytes + 1024 + 256;  // Q, K x2, V x2, P + alignment + barriers
+  static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD) | (1u << 16);  // B operand (V) MN-major
+};
 constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256,384)
 constexpr float kRescaleLog2 = 8.f;           // move the running max only when it grows by > 2^8
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128);
-constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128) | (1u << 16);  // B operand (V) MN-major
 
 // MN-major operand, 128-byte swizzle: 64-element rows of the MN dimension,
 // 8-row groups of the K dimension 1024 bytes apart (SBO), the next 64
@@ -74,7 +80,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <bool CAUSAL>
+template <int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, int64_t os,
@@ -84,10 +90,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
+  using Cf = TcCfg<HD>;
+  constexpr int kTileBytes = Cf::TILE;
   uint8_t* sK = smem + kTileBytes;
   uint8_t* sV = smem + 3 * kTileBytes;
   uint8_t* sP = smem + 5 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes + kPBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 3;
@@ -144,8 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const int qc = (int)(h * qhs), kc = (int)(kvh * khs), vc = (int)(kvh * vhs);
       mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tmQ, q_full, qc, start + m0);
-      tma_load_2d(sQ + kBoxBytes, &tmQ, q_full, qc + 64, start + m0);
+      for (int bx = 0; bx < Cf::BOXES; ++bx) tma_load_2d(sQ + bx * kBoxBytes, &tmQ, q_full, qc + 64 * bx, start + m0);
       for (int j = 0; j < ntiles && !*abort_flag; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -155,15 +162,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        tma_load_2d(sK + st * kTileBytes, &tmK, &k_full[st], kc, row);
-        tma_load_2d(sK + st * kTileBytes + kBoxBytes, &tmK, &k_full[st], kc + 64, row);
+        for (int bx = 0; bx < Cf::BOXES; ++bx)
+          tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
         if (j >= 2 && !mbar_wait(&v_empty[st], ph ^ 1, err)) {
           *abort_flag = 1;
           break;
         }
         mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        tma_load_2d(sV + st * kTileBytes, &tmV, &v_full[st], vc, row);
-        tma_load_2d(sV + st * kTileBytes + kBoxBytes, &tmV, &v_full[st], vc + 64, row);
+        for (int bx = 0; bx < Cf::BOXES; ++bx)
+          tma_load_2d(sV + st * kTileBytes + bx * kBoxBytes, &tmV, &v_full[st], vc + 64 * bx, row);
       }
     }
     __syncwarp();
@@ -179,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
+        for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
           umma_bf16(tmem + st * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
         }
@@ -202,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
-                    smem_desc_mn128(v0 + ks * 2048, kBoxBytes), kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                    smem_desc_mn128(v0 + ks * 2048, kBoxBytes), Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
         umma_commit(&v_empty[st]);
       }
@@ -275,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
             tmem_ld_wait();
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = qpos < len;
       __nv_bfloat16* orow = out + (int64_t)(start + (valid ? qpos : 0)) * os + (int64_t)h * ohs;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
         tmem_ld_wait();
@@ -359,22 +366,23 @@ bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool CAUSAL>
+template <int HD, bool CAUSAL>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* out, int64_t os,
               int64_t ohs, const int32_t* cu, int num_seqs, int mblocks, int nq, int nkv, int64_t qhs, int64_t khs,
               int64_t vhs, float scale_log2, cudaStream_t st) {
-  auto k = flash_prefill_tc_kernel<CAUSAL>;
+  auto k = flash_prefill_tc_kernel<HD, CAUSAL>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return B200_ERROR_UNSUPPORTED;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<HD>::SMEM) != cudaSuccess)
       return B200_ERROR_UNSUPPORTED;
     attr_set[dev] = true;
   }
-  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, kSmem, st, mq, mk, mv, static_cast<__nv_bfloat16*>(out),
-                os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks, b200::error_word(dev));
+  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, TcCfg<HD>::SMEM, st, mq, mk, mv,
+                static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks,
+                b200::error_word(dev));
   B200_CHECK_LAUNCH();
   return B200_OK;
 }
@@ -387,7 +395,7 @@ extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_
                                          int64_t out_head_stride, const int32_t* cu_seqlens, int num_seqs,
                                          int max_seqlen, int64_t total_tokens, int nq, int nkv, int head_dim_qk,
                                          int head_dim_v, float scale, int causal, b200_stream_t stream) {
-  if (head_dim_qk != 128 || head_dim_v != 128 || total_tokens <= 0)
+  if (head_dim_qk != head_dim_v || (head_dim_qk != 128 && head_dim_qk != 64) || total_tokens <= 0)
     return b200_flash_prefill_ex(q, q_stride, q_head_stride, k, k_stride, k_head_stride, v, v_stride, v_head_stride,
                                  out, out_stride, out_head_stride, cu_seqlens, num_seqs, max_seqlen, nq, nkv,
                                  head_dim_qk, head_dim_v, scale, causal, stream);
@@ -398,10 +406,11 @@ extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_
     if (s < 0 || s % 8) return B200_ERROR_INVALID_PARAM;
   for (const void* p : {q, k, v, (const void*)out})
     if (reinterpret_cast<uintptr_t>(p) & 15u) return B200_ERROR_INVALID_PARAM;
-  const int64_t qcols = (int64_t)(nq - 1) * q_head_stride + 128, kcols = (int64_t)(nkv - 1) * k_head_stride + 128,
-                vcols = (int64_t)(nkv - 1) * v_head_stride + 128;
+  const int hd = head_dim_qk;
+  const int64_t qcols = (int64_t)(nq - 1) * q_head_stride + hd, kcols = (int64_t)(nkv - 1) * k_head_stride + hd,
+                vcols = (int64_t)(nkv - 1) * v_head_stride + hd;
   if (q_stride < qcols || k_stride < kcols || v_stride < vcols ||
-      out_stride < (int64_t)(nq - 1) * out_head_stride + 128)
+      out_stride < (int64_t)(nq - 1) * out_head_stride + hd)
     return B200_ERROR_INVALID_PARAM;
   if (num_seqs == 0 || max_seqlen == 0) return B200_OK;
   if (num_seqs > 65535 || nq > 65535 || total_tokens > INT32_MAX || qcols > INT32_MAX || kcols > INT32_MAX ||
@@ -415,8 +424,10 @@ extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_
     return B200_ERROR_UNSUPPORTED;
   const int mblocks = (max_seqlen + kTile - 1) / kTile;
   const float sl2 = scale * 1.4426950408889634f;
-  return causal ? launch_tc<true>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq,
-                                  nkv, q_head_stride, k_head_stride, v_head_stride, sl2, stream)
-                : launch_tc<false>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq,
-                                   nkv, q_head_stride, k_head_stride, v_head_stride, sl2, stream);
+#define B200_TC(HD, C)                                                                                          \
+  launch_tc<HD, C>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq, nkv,         \
+                   q_head_stride, k_head_stride, v_head_stride, sl2, stream)
+  if (hd == 128) return causal ? B200_TC(128, true) : B200_TC(128, false);
+  return causal ? B200_TC(64, true) : B200_TC(64, false);
+#undef B200_TC
 }

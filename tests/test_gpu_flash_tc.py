@@ -1,8 +1,9 @@
-"""tcgen05 prefill attention (b200_flash_prefill_packed, 128-wide heads)
+"""tcgen05 prefill attention (b200_flash_prefill_packed, 64- and 128-wide heads)
 against the numpy oracle and a torch fp32 reference.
 
 Cases: packed variable-length sequences around the 128-row tile edges, causal
-and bidirectional, GQA, the packed q|k|v layout of the engine; the Qwen3-8B
+and bidirectional, 64- and 128-wide heads, GQA, the packed q|k|v layout of the
+engine; the Qwen3-8B
 prefill shape (8 x 2048, 32 query / 8 kv heads) against torch fp32 SDPA; and
 scores that keep growing along the keys so the running max moves (the rescale
 of the TMEM output rows) many times.
@@ -32,12 +33,12 @@ def _run(d, W, nq, nkv, hd, cu, lens, causal, T, out=None):
     return out
 
 
-@pytest.mark.parametrize("causal", [1, 0])
-def test_varlen_tile_edges(causal):
-    rng = np.random.default_rng(7 + causal)
+@pytest.mark.parametrize("causal,hd", [(1, 128), (0, 128), (1, 64), (0, 64)])
+def test_varlen_tile_edges(causal, hd):
+    rng = np.random.default_rng(7 + causal + hd)
     lens = [1, 63, 127, 128, 129, 300, 17, 1000]
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
-    T, nq, nkv, hd = int(cu[-1]), 8, 2, 128
+    T, nq, nkv = int(cu[-1]), 8, 2
     W = (nq + 2 * nkv) * hd
     qkv = rng.standard_normal((T, W)).astype(np.float32)
     d = G.bf16(qkv)
