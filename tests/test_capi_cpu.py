@@ -53,3 +53,33 @@ def test_gemm_plan_split_heuristic():
     # decode-shaped projections want split-K workspace on 148 SMs; prefill shapes do not
     assert L.b200_gemm_workspace_bytes(64, 4096, 4096, 0) > 0
     assert L.b200_gemm_workspace_bytes(16384, 6144, 4096, 0) == 0
+
+
+def test_newer_entry_points_reject_invalid_params_without_gpu():
+    if not os.path.exists(capi.LIB_PATH):
+        pytest.skip("library not built")
+    L = capi.lib()
+    INVALID = -1
+    # tcgen05 prefill attention: nq % nkv, unaligned stride (checked before any tensor map is built)
+    assert L.b200_flash_prefill_packed(16, 128, 128, 16, 128, 128, 16, 128, 128, 16, 128, 128, 16, 1, 8, 8, 3, 2,
+                                       128, 128, 0.1, 1, None) == INVALID
+    assert L.b200_flash_prefill_packed(16, 130, 128, 16, 128, 128, 16, 128, 128, 16, 128, 128, 16, 1, 8, 8, 2, 2,
+                                       128, 128, 0.1, 1, None) == INVALID
+    # expert-parallel exchange without a communicator
+    assert L.b200_ep_dispatch(None, 16, 16, 8, 8, 64, 16, 64, 16, 16, None) == INVALID
+    assert L.b200_ep_combine(None, 16, 64, 16, 16, 16, 16, 16, 4, 2, 8, 64, None, None, 16, None, None, 1e-6,
+                             None) == INVALID
+    # image preprocessing: zero-sized image, more than 3 channels, unknown output dtype
+    grid = (ctypes.c_int64 * 3)()
+    n = ctypes.c_int64()
+    assert L.b200_preprocess_image(16, 3, 0, 32, 16, 2, 2, 4096, 1843200, None, None, 1, 16, 1 << 20,
+                                   ctypes.byref(n), grid, 16, 1 << 20, None) == INVALID
+    assert L.b200_preprocess_image(16, 4, 32, 32, 16, 2, 2, 4096, 1843200, None, None, 1, 16, 1 << 20,
+                                   ctypes.byref(n), grid, 16, 1 << 20, None) == INVALID
+    assert L.b200_preprocess_image(16, 3, 32, 32, 16, 2, 2, 4096, 1843200, None, None, 5, 16, 1 << 20,
+                                   ctypes.byref(n), grid, 16, 1 << 20, None) == INVALID
+    assert L.b200_bicubic_resize_u8(None, 3, 8, 8, 4, 4, None, None, 0, None) == INVALID
+    assert L.b200_preprocess_workspace_bytes(3, 0, 8, 4, 4) == 0
+    # device position ids: missing workspace
+    assert L.b200_get_rope_index_device(16, 1, 8, None, None, 0, 1, 2, 2, 16, None, 0, None) == INVALID
+    assert L.b200_rope_index_workspace_bytes(100) == 800
