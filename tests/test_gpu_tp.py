@@ -103,3 +103,28 @@ def test_tp2_prefill_and_decode(kind):
         np.testing.assert_array_equal(o0, o1)
         prefixes = [np.append(p, t) for p, t in zip(prefixes, fed0)]
         check([a0, a1], o0, prefixes)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_wait_times_out_without_hanging(monkeypatch):
+    """Failure detection without a GPU fault: one rank enters the fused
+    all-reduce, its peer never does.  The bounded flag wait gives up after about
+    two seconds, sets DEV_ERR_WAIT_TIMEOUT (bit 0) in the device error word and
+    the kernel returns; the context keeps running kernels."""
+    import tp_worker
+
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=tp_worker.wait_timeout, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+    assert res[0]["timeout_bits"] & 1, res[0]
+    assert 1.0 < res[0]["seconds"] < 30.0, res[0]
+    assert res[0]["context_ok"]

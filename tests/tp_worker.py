@@ -156,3 +156,45 @@ def ep_kernels(rank, world, port, E, k, H, T, skip_expert, queue):
         queue.put((rank, result))
     except Exception:
         queue.put((rank, traceback.format_exc()))
+
+
+def wait_timeout(rank, world, port, queue):
+    """Rank 0 enters the fused all-reduce; rank 1 never does (it waits on the
+    host).  Rank 0's bounded flag wait must give up after ~2 s, set the
+    device error word's timeout bit and return, leaving its context usable;
+    then both ranks tear down."""
+    try:
+        import time
+
+        import torch
+
+        L, capi, dist, comm = _bootstrap(rank, world, port, 16 << 20)
+        dev = f"cuda:{rank}"
+        out = {"errors": 0}
+        if rank == 0:
+            H, T = 512, 4
+            hidden = torch.ones(T, H, dtype=torch.bfloat16, device=dev)
+            bits = ctypes.c_uint(0)
+            capi.check(L.b200_device_error_read(ctypes.addressof(bits), 1, None), "error_read")  # clear
+            t0 = time.time()
+            capi.check(L.b200_comm_allreduce_rmsnorm(comm, 0, T, H, hidden.data_ptr(), None, None, 1e-6,
+                                                     torch.cuda.current_stream().cuda_stream), "allreduce_rmsnorm")
+            torch.cuda.synchronize()
+            out["seconds"] = time.time() - t0
+            capi.check(L.b200_device_error_read(ctypes.addressof(bits), 1, None), "error_read")
+            out["timeout_bits"] = bits.value
+            # the context still runs work
+            x = torch.randn(8, 64, device=dev).to(torch.bfloat16)
+            w = torch.ones(64, dtype=torch.bfloat16, device=dev)
+            y = torch.empty_like(x)
+            capi.check(L.b200_rmsnorm(x.data_ptr(), None, w.data_ptr(), y.data_ptr(), None, 8, 64, 64, 1e-6,
+                                      torch.cuda.current_stream().cuda_stream), "rmsnorm")
+            torch.cuda.synchronize()
+            ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+            out["context_ok"] = bool(torch.allclose(y.float(), ref.float(), atol=2e-2, rtol=2e-2))
+        dist.barrier()  # rank 1 waits here, on the host, while rank 0's kernel times out
+        L.b200_comm_destroy(comm)
+        dist.destroy_process_group()
+        queue.put((rank, out))
+    except Exception:
+        queue.put((rank, traceback.format_exc()))
