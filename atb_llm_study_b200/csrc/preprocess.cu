@@ -11,7 +11,11 @@
 // int32 accumulation from 2^21, clip of >> 22), so results equal PIL's.
 //
 // Work per image: the fixed-point coefficients of both axes (one small
-// kernel, FMA-free double arithmetic identical to the host's), one
+// kernel, FMA-free double arithmetic identical to the host's).  Then, when
+// every window has at most 16 taps (downscales up to about 3.5x, every
+// upscale) and a block's input rows fit in shared memory, one
+// preprocess_fused_kernel that runs the horizontal pass into shared memory
+// and the vertical pass plus normalise/patchify from there.  Otherwise one
 // horizontal-pass kernel (one thread per output sample, uint8 intermediate
 // [C, H, out_w]) and one vertical-pass kernel that also
 // normalises and scatters each value to its patch positions (frame 0 and the
@@ -225,6 +229,165 @@ __global__ void __launch_bounds__(kThreads) coeffs_kernel(int in_v, int out_v, i
   }
 }
 
+// ---- the resample (+ normalise + patchify) in one launch after the coefficients ----
+// Block (x, y, c) produces output columns [256x, 256x + 256) of output rows
+// [32y, 32y + 32) of channel c.  It reads its coefficients from the tables
+// coeffs_kernel wrote, stages the input tile its windows cover (every row at
+// once, so all the loads are in flight together: 16-byte cp.async when the
+// rows are 16-byte aligned, batched byte loads otherwise), runs the
+// horizontal pass into shared memory (a few halo rows are computed by both
+// neighbouring blocks), then the vertical pass from there: the uint8
+// intermediate never goes to global memory.  Same integer arithmetic as the
+// two-pass kernels, so the same bytes.
+constexpr int kFRows = 32;  // output rows per block
+constexpr int kFK = 16;     // taps per axis the fused kernel handles (downscale up to ~3.5x)
+constexpr int kFusedSmemCap = 96 * 1024;
+
+// Dynamic shared memory: the input tile [rows_cap][tile_w] and the horizontal
+// results [rows_cap + K][256].  The tap loops run all K taps without a branch:
+// weights past a window are zero, and the K spare rows / the tile's slack
+// keep every read in bounds (what they hold is multiplied by zero).
+// bh/ch = nullptr: the width does not change (one unit tap per column).
+template <int MODE, bool VEC16, int K>
+__global__ void __launch_bounds__(kThreads) preprocess_fused_kernel(
+    const uint8_t* __restrict__ in, int C, int H, int W, int out_h, int out_w, const int* __restrict__ bv,
+    const int* __restrict__ cv, int ksv, const int* __restrict__ bh, const int* __restrict__ ch, int ksh,
+    void* __restrict__ out, float3 mean, float3 stdv, int ps, int tp, int ms, int rows_cap, int span_cap, int tile_w,
+    unsigned* err) {
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t fsm[];
+  uint8_t* tile = fsm;
+  uint8_t* hrow = fsm + (int64_t)rows_cap * tile_w;
+  __shared__ __align__(16) int vk[kFRows * K];  // vertical taps of the block's output rows
+  __shared__ int vb[kFRows * 2];                // first input row, taps
+  __shared__ int64_t ro[kFRows];                // output offset of each row's first element
+  __shared__ uint16_t lut[256];
+  __shared__ int lo_s, hi_s;
+  const int c = blockIdx.z;
+  const int xx0 = blockIdx.x * kThreads, yy0 = blockIdx.y * kFRows;
+  const int nrows = min(kFRows, out_h - yy0);
+  const int last = min(xx0 + kThreads, out_w) - 1;
+  const int64_t pdim = (int64_t)C * tp * ps * ps;
+  if (MODE != 0) {  // (u / 255 - mean) / std in float32, the reference's order of operations
+    const float m = c == 0 ? mean.x : (c == 1 ? mean.y : mean.z);
+    const float sd = c == 0 ? stdv.x : (c == 1 ? stdv.y : stdv.z);
+    const float v = ((float)threadIdx.x / 255.0f - m) / sd;
+    if (MODE == 1) lut[threadIdx.x] = __half_as_ushort(__float2half_rn(v));
+    else lut[threadIdx.x] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+  const int xx = xx0 + threadIdx.x;
+  const bool active = xx <= last;
+  int64_t col;  // output offset of this column inside a row
+  {
+    const int gx = xx / ps, px = xx - gx * ps;
+    col = MODE == 0 ? (int64_t)xx : ((int64_t)(gx / ms) * ms * ms + gx % ms) * pdim + px;
+  }
+  if ((int)threadIdx.x < nrows && MODE != 0) {
+    // patch ((gy/ms) gw/ms + gx/ms) ms^2 + (gy%ms) ms + gx%ms, element (c, f, py, px): the row part
+    const int yy = yy0 + threadIdx.x;
+    const int gy = yy / ps, py = yy - gy * ps;
+    const int gwm = out_w / ps / ms;
+    ro[threadIdx.x] = ((int64_t)(gy / ms) * gwm * ms * ms + (gy % ms) * ms) * pdim + ((int64_t)c * tp * ps + py) * ps;
+  } else if ((int)threadIdx.x < nrows) {
+    ro[threadIdx.x] = ((int64_t)c * out_h + yy0 + threadIdx.x) * out_w;
+  }
+  pdl_wait();  // the coefficient tables and the image come from earlier kernels / copies
+  if ((int)threadIdx.x < nrows) {
+    const int yy = yy0 + threadIdx.x;
+#pragma unroll
+    for (int y = 0; y < K; ++y) vk[threadIdx.x * K + y] = y < ksv ? cv[(int64_t)yy * ksv + y] : 0;
+    vb[2 * threadIdx.x] = bv[2 * yy];
+    vb[2 * threadIdx.x + 1] = bv[2 * yy + 1];
+  }
+  const int sx = active ? xx : last;
+  int kr[K], hx0, htaps;
+  if (bh) {
+    hx0 = bh[2 * sx];
+    htaps = bh[2 * sx + 1];
+#pragma unroll
+    for (int x = 0; x < K; ++x) kr[x] = x < ksh ? ch[(int64_t)sx * ksh + x] : 0;
+  } else {
+    hx0 = sx;
+    htaps = 1;
+#pragma unroll
+    for (int x = 0; x < K; ++x) kr[x] = x == 0 ? (1 << kPrecisionBits) : 0;
+  }
+  if (threadIdx.x == 0) lo_s = hx0;
+  if (xx == last) hi_s = hx0 + htaps;
+  __syncthreads();
+  // input columns [lo, hi) (lo rounded down to 16 bytes on the aligned path), rows [ylo, yhi)
+  const int lo = VEC16 ? (lo_s & ~15) : lo_s;
+  const int hi = min(hi_s, lo_s + span_cap);
+  const int ylo = vb[0];
+  int yhi = vb[2 * (nrows - 1)] + vb[2 * (nrows - 1) + 1];
+  if (yhi - ylo > rows_cap) {  // the host's bound makes this unreachable
+    if (threadIdx.x == 0) raise_error(err, DEV_ERR_BAD_INDEX);
+    yhi = ylo + rows_cap;
+  }
+  const int nr = yhi - ylo;
+  // this column's window inside the tile; taps past the staged bytes get weight zero
+  const int hx = min(hx0 - lo, tile_w - K);
+#pragma unroll
+  for (int x = 0; x < K; ++x)
+    if (hx + x >= hi - lo) kr[x] = 0;
+  const uint8_t* src = in + ((int64_t)c * H + ylo) * W + lo;
+  if (VEC16) {
+    // chunks of 16 bytes: hi - lo rounded up stays inside the row (W % 16 == 0) and inside tile_w
+    const int cw = (hi - lo + 15) >> 4;
+    for (int i = threadIdx.x; i < nr * cw; i += kThreads) {
+      const int r = i / cw, q = i - r * cw;
+      cp_async_16(smem_u32(tile + r * tile_w + q * 16), src + (int64_t)r * W + q * 16, true);
+    }
+    cp_async_commit();
+  } else {
+    const int sw = hi - lo, total = nr * sw;
+    for (int base = threadIdx.x; base < total; base += kThreads * 8) {
+      uint8_t v[8];
+      int at[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kThreads;
+        const int r = i / sw, q = i - r * sw;
+        at[j] = i < total ? r * tile_w + q : -1;
+        v[j] = i < total ? src[(int64_t)r * W + q] : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (at[j] >= 0) tile[at[j]] = v[j];
+    }
+  }
+  // the K spare result rows past nr read as zero-weighted taps: give them defined bytes
+#pragma unroll
+  for (int y = 0; y < K; ++y) hrow[(nr + y) * kThreads + threadIdx.x] = 0;
+  if (VEC16) cp_async_wait<0>();
+  __syncthreads();
+  // horizontal pass over the staged rows
+  const uint8_t* t = tile + hx;
+  for (int r = 0; r < nr; ++r, t += tile_w) {
+    int ss = 1 << (kPrecisionBits - 1);
+#pragma unroll
+    for (int x = 0; x < K; ++x) ss += (int)t[x] * kr[x];
+    hrow[r * kThreads + threadIdx.x] = clip8(ss);
+  }
+  __syncthreads();
+  if (!active) return;
+  for (int i = 0; i < nrows; ++i) {
+    const uint8_t* h = hrow + min(vb[2 * i] - ylo, nr) * kThreads + threadIdx.x;  // rows < nr + K
+    const int* k = vk + i * K;
+    int ss = 1 << (kPrecisionBits - 1);
+#pragma unroll
+    for (int y = 0; y < K; ++y) ss += (int)h[y * kThreads] * k[y];
+    const uint8_t u = clip8(ss);
+    if (MODE == 0) {
+      static_cast<uint8_t*>(out)[ro[i] + col] = u;
+    } else {
+      uint16_t* o = static_cast<uint16_t*>(out) + ro[i] + col;
+      const uint16_t wv = lut[u];
+      for (int f = 0; f < tp; ++f) o[(int64_t)f * ps * ps] = wv;
+    }
+  }
+}
+
 int ksize_of(int in_size, int out_size) {
   const double scale = (double)in_size / out_size;
   const double support = 2.0 * (scale < 1.0 ? 1.0 : scale);
@@ -265,6 +428,63 @@ int run_resample(int mode, const uint8_t* image, int C, int H, int W, int oh, in
                  float3 stdv, int ps, int tp, int ms, void* ws, int64_t ws_bytes, cudaStream_t st) {
   const Layout L = layout(C, H, W, oh, ow);
   if (!ws || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255)) return B200_ERROR_INVALID_PARAM;
+  // coefficients + one fused launch when every window fits its tap budget and a block's tile fits in
+  // shared memory; the horizontal intermediate in the workspace serves only the two-pass path below
+  {
+    const int ksh = ow != W ? ksize_of(W, ow) : 1, ksv = oh != H ? ksize_of(H, oh) : 1;
+    const int K = std::max(ksh, ksv) <= 8 ? 8 : kFK;
+    // input rows of 32 output rows' windows / input bytes of 256 output columns' windows, with slack
+    const int rows_cap = (int)ceil((double)H / oh * kFRows) + ksv + 2;
+    const int span_cap = (int)ceil((double)W / ow * kThreads) + ksh + 8;
+    const int tile_w = ((span_cap + 15) & ~15) + 32;  // room for the 16-byte round-down and round-up
+    const int64_t smem = (int64_t)rows_cap * tile_w + (int64_t)(rows_cap + K) * kThreads;
+    const int64_t gy = (oh + kFRows - 1) / kFRows;
+    if (ksh <= kFK && ksv <= kFK && smem <= kFusedSmemCap && gy <= 65535 && C <= 65535) {
+      const bool vec16 = W % 16 == 0 && (reinterpret_cast<uintptr_t>(image) & 15) == 0;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      static bool attr[64] = {false};
+      if (dev >= 0 && dev < 64 && !attr[dev]) {
+#define B200_PF_ATTR(V, KK)                                                                                        \
+  for (auto f : {preprocess_fused_kernel<0, V, KK>, preprocess_fused_kernel<1, V, KK>,                             \
+                 preprocess_fused_kernel<2, V, KK>})                                                                \
+    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmemCap) != cudaSuccess) \
+      return B200_ERROR_UNSUPPORTED;
+        B200_PF_ATTR(true, 8)
+        B200_PF_ATTR(false, 8)
+        B200_PF_ATTR(true, kFK)
+        B200_PF_ATTR(false, kFK)
+#undef B200_PF_ATTR
+        attr[dev] = true;
+      }
+      uint8_t* w8 = static_cast<uint8_t*>(ws);
+      int* bv = reinterpret_cast<int*>(w8 + L.off_bv);
+      int* cv = reinterpret_cast<int*>(w8 + L.off_cv);
+      int* bh = ow != W ? reinterpret_cast<int*>(w8 + L.off_bh) : nullptr;
+      int* ch = ow != W ? reinterpret_cast<int*>(w8 + L.off_ch) : nullptr;
+      launch_kernel(coeffs_kernel, dim3((unsigned)((std::max(oh, ow) + kThreads - 1) / kThreads), 2), kThreads, 0,
+                    st, H, oh, L.ksv, bv, cv, W, ow, L.ksh, bh, ch);
+      B200_CHECK_LAUNCH();
+      const dim3 g((unsigned)((ow + kThreads - 1) / kThreads), (unsigned)gy, (unsigned)C);
+      unsigned* err = b200::error_word(dev);
+#define B200_PF(M, V, KK)                                                                                     \
+  launch_kernel(preprocess_fused_kernel<M, V, KK>, g, kThreads, (size_t)smem, st, image, C, H, W, oh, ow, bv, cv, \
+                L.ksv, bh, ch, L.ksh, out, mean, stdv, ps, tp, ms, rows_cap, span_cap, tile_w, err)
+#define B200_PF_MODE(V, KK)          \
+  if (mode == 0) B200_PF(0, V, KK);  \
+  else if (mode == 1) B200_PF(1, V, KK); \
+  else B200_PF(2, V, KK);
+      if (K == 8) {
+        if (vec16) { B200_PF_MODE(true, 8) } else { B200_PF_MODE(false, 8) }
+      } else {
+        if (vec16) { B200_PF_MODE(true, kFK) } else { B200_PF_MODE(false, kFK) }
+      }
+#undef B200_PF_MODE
+#undef B200_PF
+      B200_CHECK_LAUNCH();
+      return B200_OK;
+    }
+  }
   uint8_t* w8 = static_cast<uint8_t*>(ws);
   const bool need_h = ow != W;
   if (L.ksh > kMaxTaps || L.ksv > kMaxTaps) return B200_ERROR_UNSUPPORTED;
