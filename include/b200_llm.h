@@ -424,7 +424,7 @@ B200_API int b200_preprocess_image(const uint8_t* image, int channels, int heigh
  * every rank calls b200_comm_create (collective), shares its 64-byte
  * b200_comm_ipc_handle, then calls b200_comm_connect with all ranks' handles
  * concatenated in rank order.  No reference counterpart: the reference runs
- * on one device (SURVEY's TP rows for Qwen3-8B are new). */
+ * on one device (tensor and expert parallelism are new here). */
 typedef struct b200_comm_s* b200_comm_t;
 B200_API int b200_comm_unique_id(void* nccl_id_out);
 B200_API int b200_comm_create(int world, int rank, int device, const void* nccl_id, int64_t symmetric_bytes,

@@ -13,7 +13,7 @@ path into compact ``.npz`` fixtures next to this script:
 The inputs of the ``GetRopeIndex`` cases are not written by the generator,
 so ``get_rope_index`` is wrapped while the stages run to record its arguments.
 
-Usage (in a container that has the reference; the GPU box does not need it):
+Usage (where a reference checkout exists; the tests read only the fixtures):
     python tests/golden/make_golden.py [--reference /root/reference]
 """
 

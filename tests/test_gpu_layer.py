@@ -7,7 +7,7 @@ RMSNorm -> fused QKV GEMM -> QK-norm + rope -> causal flash attention ->
 O GEMM (+residual epilogue) -> fused residual RMSNorm -> gate/up GEMM with the
 SwiGLU epilogue -> down GEMM (+residual epilogue).
 
-Bar (BASELINE): cosine >= 0.999 per layer output; max |err| / max |ref| < 2 %.
+Bar: cosine >= 0.999 per layer output; max |err| / max |ref| < 2 %.
 """
 
 import numpy as np

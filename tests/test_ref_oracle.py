@@ -1,7 +1,7 @@
 """Pin the numpy oracle against the reference's own compiled CPU functions
 (oracle/_ref, built from atb_cpp_llm/src/components/common/mrope.cpp and
 atb_cpp_llm/src/components/vision/pos_embed_interp.cpp by oracle/Makefile).
-Skipped where the reference checkout is absent (the GPU box)."""
+Skipped where the reference checkout or oracle/_ref is absent."""
 
 import numpy as np
 import pytest
