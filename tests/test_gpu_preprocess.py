@@ -7,7 +7,9 @@ generator's golden data) and the oracle.
   output), plus odd up/down sizes against the oracle.
 * b200_preprocess_image: the three PreprocessImage cases, fp16 pixel values
   bit-exact with the PIL chain, grid and patch count; bf16 output equal to
-  the oracle's float32 values rounded to bf16.
+  the oracle's float32 values rounded to bf16; and frames that take each
+  variant of the fused kernel (rows not a multiple of 16 bytes, so byte-load
+  staging; 8- and 16-tap windows; a >2x downscale) bit-exact with the oracle.
 """
 
 import ctypes
@@ -109,4 +111,16 @@ def test_preprocess_bf16_and_large_image():
     norm = ((r.astype(np.float32) / np.float32(255.0)) - np.float32(0.5)) / np.float32(0.5)
     want = torch.from_numpy(P.patchify(norm)).to(torch.bfloat16)
     assert torch.equal(pv.cpu(), want)
+    assert G.device_errors() == 0
+
+
+@pytest.mark.parametrize("h,w", [(37, 53), (500, 333), (2400, 3000), (2400, 3008)])
+def test_preprocess_chain_fused_variants_vs_oracle(h, w):
+    # 37x53 -> 64x96 and 500x333 -> 512x320: unaligned rows, up to 7 taps;
+    # 2400x3000 / 2400x3008 -> 1184x1504: 9 / 11 taps (the 16-tap kernel), unaligned / aligned rows
+    x = np.random.default_rng(h * 7 + w).integers(0, 256, (3, h, w), dtype=np.uint8)
+    pv, n, grid = preprocess(x)
+    ref, rgrid = P.preprocess_image(x)
+    assert grid == rgrid and n == ref.shape[0]
+    np.testing.assert_array_equal(pv.cpu().numpy().view(np.uint16), ref.view(np.uint16))
     assert G.device_errors() == 0
