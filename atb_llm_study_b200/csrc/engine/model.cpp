@@ -15,11 +15,19 @@ void set_pdl(bool on);
 }
 
 namespace {
-// Prefill launches without programmatic dependent launch: its grids fill the
-// GPU on their own, and early-launched successors measured slower there.
+// Long prefill / encode passes launch without programmatic dependent launch:
+// their grids fill the GPU on their own, and early-launched successors
+// measured slower there (16384-token Qwen3-8B prefill).  Short passes (a few
+// hundred tokens: grids of tens of CTAs) keep it, like decode.
+constexpr int64_t kPdlMaxTokens = 1024;
 struct NoPdlScope {
-  NoPdlScope() { b200::set_pdl(false); }
-  ~NoPdlScope() { b200::set_pdl(true); }
+  explicit NoPdlScope(bool active) : active_(active) {
+    if (active_) b200::set_pdl(false);
+  }
+  ~NoPdlScope() {
+    if (active_) b200::set_pdl(true);
+  }
+  bool active_;
 };
 }  // namespace
 
@@ -942,7 +950,7 @@ Status DecoderModel::Prefill(const int64_t* ids, bool ids_on_device, const int32
     max_len = std::max(max_len, seq_lens[i]);
   }
   if (T > max_t_) return ERROR_INVALID_PARAM;
-  NoPdlScope no_pdl;
+  NoPdlScope no_pdl(T > kPdlMaxTokens);
   cudaStream_t st = ctx_->GetStream();
   // host-side metadata staged in pinned memory
   uint8_t* pin = static_cast<uint8_t*>(pinned_);
@@ -1081,7 +1089,7 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
       seen[vis_rows[i]] = 1;
     }
   }
-  NoPdlScope no_pdl;
+  NoPdlScope no_pdl(S > kPdlMaxTokens);
   cudaStream_t st = ctx_->GetStream();
   const int64_t H = cfg_.hidden;
   uint8_t* pin = static_cast<uint8_t*>(pinned_);
