@@ -5,6 +5,7 @@
 
 #include "engine/engine_kernels.h"
 #include "engine/safetensors.h"
+#include "fused.h"
 #include "gemm.h"
 
 namespace b200llm {
@@ -241,6 +242,28 @@ Status VisionModel::Gemm(const void* A, int64_t lda, const void* W, void* C, int
   return STATUS_OK;
 }
 
+Status VisionModel::GemmResidualNorm(const void* A, int64_t lda, const void* W, int64_t M, int64_t K,
+                                     const void* bias, const void* gamma, const void* beta, bool* normed) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden;
+  int splits = 1;
+  *normed = false;
+  ++launches_;
+  B200_RETURN_IF(b200::gemm_launch(A, lda, W, K, h_.data, H, M, H, K, B200_EPI_BIAS_RESIDUAL, bias, h_.data, H,
+                                   ws_.data, ws_bytes_, st, &splits));
+  if (splits <= 1) return STATUS_OK;
+  ++launches_;
+  const int rc = b200::splitk_bias_residual_layernorm(ws_.as<float>(), splits, M, H, bias, h_.data, gamma, beta,
+                                                      normed_.data, cfg_.eps, st);
+  if (rc == B200_OK) {
+    *normed = true;
+    return STATUS_OK;
+  }
+  if (rc != B200_ERROR_UNSUPPORTED) return (Status)rc;
+  return (Status)b200::splitk_reduce(ws_.as<float>(), splits, M, H, B200_EPI_BIAS_RESIDUAL, bias, h_.data, H,
+                                     h_.data, H, st);
+}
+
 // LayerNorm -> fc1 (+bias, GELU-tanh) -> fc2 (+bias).  The main merger
 // normalises each token over `hidden` before grouping; a deepstack merger
 // groups merge^2 tokens first and normalises over the grouped width
@@ -342,9 +365,12 @@ Status VisionModel::RunTower(int64_t N, const int64_t* grid_thw, int num_images,
   const float scale = 1.0f / std::sqrt((float)hd);
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<const uint16_t*>(t.data) + off; };
   uint16_t* qkv = qkv_.as<uint16_t>();
+  bool n1_ready = false;  // normed_ already holds this block's first LayerNorm (fused into fc2's reduce)
   for (int l = 0; l < cfg_.depth; ++l) {
-    ++launches_;
-    B200_RETURN_IF(b200_layernorm(h_.data, bf(n1_w_, l * H), bf(n1_b_, l * H), normed_.data, N, H, cfg_.eps, st));
+    if (!n1_ready) {
+      ++launches_;
+      B200_RETURN_IF(b200_layernorm(h_.data, bf(n1_w_, l * H), bf(n1_b_, l * H), normed_.data, N, H, cfg_.eps, st));
+    }
     B200_RETURN_IF(Gemm(normed_.data, H, bf(qkv_w_, l * 3 * H * H), qkv, 3 * H, N, 3 * H, H, B200_EPI_BIAS,
                         bf(qkv_b_, l * 3 * H), nullptr, 0));
     launches_ += 2;
@@ -352,15 +378,26 @@ Status VisionModel::RunTower(int64_t N, const int64_t* grid_thw, int num_images,
     B200_RETURN_IF(b200_flash_prefill_packed(qkv, 3 * H, hd, qkv + H, 3 * H, hd, qkv + 2 * H, 3 * H, hd, attn_.data,
                                              H, hd, cu_.as<int32_t>(), (int)frames, max_len, N, nh, nh, (int)hd,
                                              (int)hd, scale, 0, st));
-    B200_RETURN_IF(Gemm(attn_.data, H, bf(proj_w_, l * H * H), h_.data, H, N, H, H, B200_EPI_BIAS_RESIDUAL,
-                        bf(proj_b_, l * H), h_.data, H));
-    ++launches_;
-    B200_RETURN_IF(b200_layernorm(h_.data, bf(n2_w_, l * H), bf(n2_b_, l * H), normed_.data, N, H, cfg_.eps, st));
+    bool n2_ready = false;
+    B200_RETURN_IF(GemmResidualNorm(attn_.data, H, bf(proj_w_, l * H * H), N, H, bf(proj_b_, l * H),
+                                    bf(n2_w_, l * H), bf(n2_b_, l * H), &n2_ready));
+    if (!n2_ready) {
+      ++launches_;
+      B200_RETURN_IF(b200_layernorm(h_.data, bf(n2_w_, l * H), bf(n2_b_, l * H), normed_.data, N, H, cfg_.eps, st));
+    }
     B200_RETURN_IF(Gemm(normed_.data, H, bf(fc1_w_, l * I * H), act_.data, I, N, I, H, B200_EPI_BIAS_GELU,
                         bf(fc1_b_, l * I), nullptr, 0));
-    B200_RETURN_IF(Gemm(act_.data, I, bf(fc2_w_, l * H * I), h_.data, H, N, H, I, B200_EPI_BIAS_RESIDUAL,
-                        bf(fc2_b_, l * H), h_.data, H));
     const int ds = DeepstackSlot(l);
+    if (ds < 0 && l + 1 < cfg_.depth) {
+      // the next block's first LayerNorm rides on fc2's split-K reduce (a merger
+      // after this block would use normed_ itself, so those blocks normalise later)
+      B200_RETURN_IF(GemmResidualNorm(act_.data, I, bf(fc2_w_, l * H * I), N, I, bf(fc2_b_, l * H),
+                                      bf(n1_w_, (l + 1) * H), bf(n1_b_, (l + 1) * H), &n1_ready));
+    } else {
+      B200_RETURN_IF(Gemm(act_.data, I, bf(fc2_w_, l * H * I), h_.data, H, N, H, I, B200_EPI_BIAS_RESIDUAL,
+                          bf(fc2_b_, l * H), h_.data, H));
+      n1_ready = false;
+    }
     if (ds >= 0)
       B200_RETURN_IF(Merger(h_.data, N, 1 + ds,
                             static_cast<uint16_t*>(ds_.data) + (int64_t)ds * merged_tokens_ * cfg_.out_hidden));

@@ -75,6 +75,11 @@ class VisionModel {
   void DropGraphs();
   Status Gemm(const void* A, int64_t lda, const void* W, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi,
               const void* bias, const void* R, int64_t ldr);
+  // h_ += A W^T + bias (K may split).  When it splits, the reduce and the
+  // LayerNorm (gamma, beta) of h_ into normed_ run as one kernel and *normed
+  // is set; otherwise the caller normalises.
+  Status GemmResidualNorm(const void* A, int64_t lda, const void* W, int64_t M, int64_t K, const void* bias,
+                          const void* gamma, const void* beta, bool* normed);
   Status Merger(const void* x, int64_t N, int which, void* out);
   int DeepstackSlot(int block) const;
 

@@ -18,4 +18,13 @@ int qk_norm_rope_launch(void* qkv, int64_t T, int nq, int nkv, int head_dim, int
 int splitk_residual_rmsnorm(const float* partials, int splits, int64_t rows, int64_t dim, void* hidden,
                             const void* weight, void* normed, float eps, cudaStream_t stream);
 
+// hidden[rows, dim] = bf16(sum_s partials[s] + bias + hidden) (the split-K
+// reduce of a bias + residual projection, same order of additions);
+// normed = layernorm(hidden) * gamma + beta, the arithmetic of b200_layernorm.
+// B200_ERROR_UNSUPPORTED for dim > 4096 (the caller reduces and normalises
+// separately).
+int splitk_bias_residual_layernorm(const float* partials, int splits, int64_t rows, int64_t dim, const void* bias,
+                                   void* hidden, const void* gamma, const void* beta, void* normed, float eps,
+                                   cudaStream_t stream);
+
 }  // namespace b200

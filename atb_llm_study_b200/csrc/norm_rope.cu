@@ -180,6 +180,77 @@ __global__ void __launch_bounds__(kNormThreads) layernorm_kernel(const __nv_bflo
   }
 }
 
+// One CTA of kNormThreads per row, the thread / chunk mapping of
+// layernorm_kernel: h = bf16(sum_s partials[s][row] + bias + hidden[row])
+// (the additions in splitk_reduce_kernel's order), hidden[row] = h, then
+// layernorm_kernel's arithmetic on h.  Replaces a split-K reduce launch and a
+// LayerNorm launch with one.
+template <int CH>
+__global__ void __launch_bounds__(kNormThreads) splitk_bias_residual_layernorm_kernel(
+    const float* __restrict__ partials, int splits, int64_t rows, const __nv_bfloat16* __restrict__ bias,
+    __nv_bfloat16* hidden, const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ b,
+    __nv_bfloat16* __restrict__ out, int64_t dim, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  pdl_trigger();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const int64_t nchunk = dim / 8;
+  float v[CH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4* src = reinterpret_cast<const float4*>(partials + ((int64_t)sp * rows + row) * dim + idx * 8);
+        const float4 a = src[0], q = src[1];
+        v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
+        v[c][4] += q.x; v[c][5] += q.y; v[c][6] += q.z; v[c][7] += q.w;
+      }
+      float t[8];
+      unpack8(*reinterpret_cast<const uint4*>(bias + idx * 8), t);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] += t[i];
+      unpack8(*reinterpret_cast<const uint4*>(hidden + row * dim + idx * 8), t);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] += t[i];
+      const uint4 hb = pack8(v[c]);
+      *reinterpret_cast<uint4*>(hidden + row * dim + idx * 8) = hb;
+      unpack8(hb, v[c]);  // normalise the stored (bf16) residual stream
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[c][i];
+    }
+  }
+  const float mean = block_sum<kNormThreads>(s, red) / (float)dim;
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[c][i] - mean;
+        ss += d * d;
+      }
+    }
+  }
+  const float inv = rsqrtf(block_sum<kNormThreads>(ss, red) / (float)dim + eps);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) {
+      float gg[8], bb[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(g + idx * 8), gg);
+      unpack8(*reinterpret_cast<const uint4*>(b + idx * 8), bb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[c][i] - mean) * inv * gg[i] + bb[i];
+      *reinterpret_cast<uint4*>(out + row * dim + idx * 8) = pack8(o);
+    }
+  }
+}
+
 // cos/sin table: one thread per (token, frequency index i < d/2).
 // plane(i) selects which position-id plane feeds frequency i: 0 for 1-D rope;
 // for interleaved mrope, 1 when i%3==1 && i<3*sec_h, 2 when i%3==2 && i<3*sec_w.
@@ -600,6 +671,33 @@ int splitk_residual_rmsnorm(const float* partials, int splits, int64_t rows, int
     case 2: launch_kernel(splitk_residual_rmsnorm_kernel<2>, g, kRowThreads, 0, stream, partials, splits, rows, h, w, o, dim, eps); break;
     case 3:
     case 4: launch_kernel(splitk_residual_rmsnorm_kernel<4>, g, kRowThreads, 0, stream, partials, splits, rows, h, w, o, dim, eps); break;
+    default: return B200_ERROR_UNSUPPORTED;
+  }
+  B200_CHECK_LAUNCH();
+  return B200_OK;
+}
+
+int splitk_bias_residual_layernorm(const float* partials, int splits, int64_t rows, int64_t dim, const void* bias,
+                                   void* hidden, const void* gamma, const void* beta, void* normed, float eps,
+                                   cudaStream_t stream) {
+  if (!partials || splits <= 0 || !bias || !hidden || !gamma || !beta || !normed || rows < 0 || dim <= 0 || dim % 8)
+    return B200_ERROR_INVALID_PARAM;
+  if (!aligned16(partials) || !aligned16(bias) || !aligned16(hidden) || !aligned16(gamma) || !aligned16(beta) ||
+      !aligned16(normed))
+    return B200_ERROR_INVALID_PARAM;
+  if (rows == 0) return B200_OK;
+  const int64_t per = (dim / 8 + kNormThreads - 1) / kNormThreads;
+  auto bs = static_cast<const __nv_bfloat16*>(bias);
+  auto h = static_cast<__nv_bfloat16*>(hidden);
+  auto gb = static_cast<const __nv_bfloat16*>(gamma);
+  auto bb = static_cast<const __nv_bfloat16*>(beta);
+  auto o = static_cast<__nv_bfloat16*>(normed);
+  dim3 g((unsigned)rows);
+  switch (per) {
+    case 1: launch_kernel(splitk_bias_residual_layernorm_kernel<1>, g, kNormThreads, 0, stream, partials, splits, rows, bs, h, gb, bb, o, dim, eps); break;
+    case 2: launch_kernel(splitk_bias_residual_layernorm_kernel<2>, g, kNormThreads, 0, stream, partials, splits, rows, bs, h, gb, bb, o, dim, eps); break;
+    case 3:
+    case 4: launch_kernel(splitk_bias_residual_layernorm_kernel<4>, g, kNormThreads, 0, stream, partials, splits, rows, bs, h, gb, bb, o, dim, eps); break;
     default: return B200_ERROR_UNSUPPORTED;
   }
   B200_CHECK_LAUNCH();
