@@ -103,6 +103,49 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+class RegionClock:
+    """Median SM clock over a short timed region: NVML clock reads (read only)
+    every 5 ms from a thread; None where NVML is unavailable."""
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.mhz = []
+        self.stop = None
+        self.thread = None
+
+    def __enter__(self):
+        import threading
+
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+        except Exception:
+            return self
+        self.stop = threading.Event()
+
+        def run():
+            while not self.stop.is_set():
+                try:
+                    self.mhz.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                except Exception:
+                    return
+                time.sleep(0.005)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.thread:
+            self.stop.set()
+            self.thread.join(1.0)
+
+    def median(self):
+        return statistics.median(self.mhz) if self.mhz else None
+
+
 # --------------------------------------------------------------------- CPU leg
 
 def cpu_decode_layer_seconds(threads_note):
@@ -1052,11 +1095,14 @@ def run_b200(args, rank, world, local_rank):
 
     for i in range(warm):
         decode_dev(i)
-    dec_ms = timed(decode_dev, steps, 0)
+    with RegionClock(local_rank) as dec_clk:
+        dec_ms = timed(decode_dev, steps, 0)
     clk.__exit__(None, None, None)
     clocks = clk.summary()
+    clocks["decode_region_sm_mhz"] = dec_clk.median()
     host_ids[:] = ids_d.cpu().numpy()
-    dec_e2e_ms = timed(decode_host, steps, 0)
+    with RegionClock(local_rank) as e2e_clk:
+        dec_e2e_ms = timed(decode_host, steps, 0)
     launches_per_step = q(2)
     prefill_launches = q(3)
 
@@ -1147,7 +1193,10 @@ def run_b200(args, rank, world, local_rank):
                                        "shape (profiles/paged_decode_b64_ctx2048.md)",
                      "peak_source": f"{src} copy bandwidth", "ms": att_ms, "bytes_per_launch": att_bytes},
         "e2e": {"value": world * DECODE_BATCH * steps / (dec_e2e_ms / 1e3), "unit": "tok/s",
-                "h2d_bytes_per_step": DECODE_BATCH * 8 + DECODE_BATCH * 4, "d2h_bytes_per_step": DECODE_BATCH * 8},
+                "h2d_bytes_per_step": DECODE_BATCH * 8 + DECODE_BATCH * 4, "d2h_bytes_per_step": DECODE_BATCH * 8,
+                # the e2e steps run after the device-resident ones, with a host sync each step; under
+                # sw_power_cap their SM clock can differ from the decode region's (clocks.decode_region_sm_mhz)
+                "sm_mhz": e2e_clk.median()},
         "gpu_launches": launches_per_step * steps,
         "gpu_launches_note": f"{launches_per_step} kernels per decode step (CUDA graph); prefill step "
                              f"{prefill_launches}",
