@@ -134,6 +134,8 @@ DecoderModel::~DecoderModel() {
   if (ctx_) cudaSetDevice(ctx_->GetDeviceId());
   for (auto& g : graphs_) cudaGraphExecDestroy(g.second);
   graphs_.clear();
+  for (auto& g : enc_graphs_) cudaGraphExecDestroy(g.second.exec);
+  enc_graphs_.clear();
   if (ctx_) ctx_->Synchronize();
   if (pinned_) cudaFreeHost(pinned_);
   alloc_.reset();
@@ -1114,6 +1116,53 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
   cur_num_seqs_ = 1;
   cur_max_len_ = (int)S;
 
+  // Every per-call input now sits in the engine's device buffers (ids, positions,
+  // image rows, pooled row), so a pass of the same shape over the same feature
+  // buffers replays one captured graph.
+  std::string key = std::to_string(S) + "/" + std::to_string(n_vis) + "/" +
+                    std::to_string(reinterpret_cast<uintptr_t>(vis_embeds)) + "/" + std::to_string(normalize) + "/" +
+                    std::to_string(reinterpret_cast<uintptr_t>(hidden_out));
+  for (int i = 0; i < n_ds; ++i) key += "/" + std::to_string(reinterpret_cast<uintptr_t>(deepstack[i]));
+  static const bool no_graph = EnvInt("B200_DISABLE_GRAPHS", 0) != 0;
+  auto it = enc_graphs_.find(key);
+  if (it != enc_graphs_.end()) {
+    B200_RETURN_IF(FromCuda(cudaGraphLaunch(it->second.exec, st)));
+    launches_ = it->second.launches;
+  } else if (!no_graph && enc_graphs_.size() < kMaxEncodeGraphs && ++enc_calls_[key] >= 2) {
+    B200_RETURN_IF(FromCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed)));
+    Status s = EncodeDevice(S, n_vis, vis_embeds, deepstack, n_ds, normalize, hidden_out);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    cudaGraphExec_t ex = nullptr;
+    if (s == STATUS_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (s == STATUS_OK && e == cudaSuccess) {
+      enc_graphs_[key] = EncodeGraph{ex, launches_};
+      enc_calls_.erase(key);
+      B200_RETURN_IF(FromCuda(cudaGraphLaunch(ex, st)));
+    } else {
+      // nothing of the capture ran: clear its error, never capture this key again, run the pass eagerly
+      (void)cudaGetLastError();
+      enc_calls_[key] = -(1 << 30);
+      B200_RETURN_IF(EncodeDevice(S, n_vis, vis_embeds, deepstack, n_ds, normalize, hidden_out));
+    }
+  } else {
+    B200_RETURN_IF(EncodeDevice(S, n_vis, vis_embeds, deepstack, n_ds, normalize, hidden_out));
+  }
+  last_encode_launches_ = launches_;
+  float* h_out = reinterpret_cast<float*>(pin);
+  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(h_out, pooled_.data, (size_t)H * 4, cudaMemcpyDeviceToHost, st)));
+  B200_RETURN_IF(ctx_->Synchronize());
+  std::memcpy(out, h_out, (size_t)H * 4);
+  return FromCuda(cudaGetLastError());
+}
+
+// The device part of Encode: rope tables, embedding (+ image rows), the
+// layers, final RMSNorm of the pooled row and L2 pooling into pooled_.
+Status DecoderModel::EncodeDevice(int64_t S, int64_t n_vis, const void* vis_embeds, const void* const* deepstack,
+                                  int n_ds, bool normalize, void* hidden_out) {
+  cudaStream_t st = ctx_->GetStream();
+  const int64_t H = cfg_.hidden;
   B200_RETURN_IF(RopeTables(S));
   B200_RETURN_IF(b200_embedding(ids_.as<int64_t>(), S, embed_.data, gcfg_.vocab, H, hidden_.data, st));
   launches_ = 2;
@@ -1140,12 +1189,7 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
     ++launches_;
     B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, final_norm_.data, hidden_out, nullptr, S, H, H, cfg_.eps, st));
   }
-  last_encode_launches_ = launches_;
-  float* h_out = reinterpret_cast<float*>(pin);
-  B200_RETURN_IF(FromCuda(cudaMemcpyAsync(h_out, pooled_.data, (size_t)H * 4, cudaMemcpyDeviceToHost, st)));
-  B200_RETURN_IF(ctx_->Synchronize());
-  std::memcpy(out, h_out, (size_t)H * 4);
-  return FromCuda(cudaGetLastError());
+  return STATUS_OK;
 }
 
 int DecoderModel::DecodeLaunches() const { return last_decode_launches_; }

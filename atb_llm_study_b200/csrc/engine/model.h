@@ -198,6 +198,17 @@ class DecoderModel {
   // second call (the first runs eagerly and initialises lazy state)
   std::map<int, cudaGraphExec_t> graphs_;
   std::map<int, int> decode_calls_;
+  // text encode passes as CUDA graphs, keyed by the shape and the buffers the
+  // pass reads (a key is captured on its second call; at most kMaxEncodeGraphs)
+  struct EncodeGraph {
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+  };
+  static constexpr size_t kMaxEncodeGraphs = 16;
+  std::map<std::string, EncodeGraph> enc_graphs_;
+  std::map<std::string, int> enc_calls_;
+  Status EncodeDevice(int64_t S, int64_t n_vis, const void* vis_embeds, const void* const* deepstack, int n_ds,
+                      bool normalize, void* hidden_out);
   unsigned* err_ = nullptr;
 };
 

@@ -211,6 +211,33 @@ def test_embed_with_image(engine, grid):
     close(out, ref)
 
 
+def test_embed_repeated_shapes_replay_graph(engine):
+    """A repeated request shape runs eagerly, is captured as a CUDA graph on its
+    second call and replayed after: every call, with fresh ids (and pixels),
+    matches the oracle."""
+    eng, vis, txt = engine
+    rng = np.random.default_rng(21)
+    for _ in range(4):
+        ids = rng.integers(0, 1000, 29)
+        rc, out, _ = _embed(eng, ids, hidden=False)
+        assert rc == 0
+        ref, _ = embed_forward(ids, txt, TCFG)
+        close(out, ref)
+    grid = [[1, 8, 8]]
+    g = np.array(grid, np.int64)
+    for i in range(3):
+        ids = np.array(list(rng.integers(0, 1000, 5)) + [VS] + [IMG] * 16 + list(rng.integers(0, 1000, 4)), np.int64)
+        px = _pixels(grid, 30 + i)
+        rc, out, _ = _embed(eng, ids, px=px, grid=g, hidden=False)
+        assert rc == 0
+        merged, ds = vision_tower(G.rounded(px), g, vis, VCFG)
+        pid = oracle.get_rope_index(ids[None], g, image_token_id=IMG, vision_start_token_id=VS)[:, 0]
+        rows = np.nonzero(ids == IMG)[0]
+        ref, _ = embed_forward(ids, txt, TCFG, pid, rows, merged, ds)
+        close(out, ref)
+    assert G.device_errors() == 0
+
+
 def test_embed_pools_last_unmasked_token(engine):
     eng, _, txt = engine
     ids = np.random.default_rng(6).integers(0, 1000, 24)
