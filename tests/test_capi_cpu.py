@@ -83,3 +83,26 @@ def test_newer_entry_points_reject_invalid_params_without_gpu():
     # device position ids: missing workspace
     assert L.b200_get_rope_index_device(16, 1, 8, None, None, 0, 1, 2, 2, 16, None, 0, None) == INVALID
     assert L.b200_rope_index_workspace_bytes(100) == 800
+
+
+def test_gemm_split_plan_for_the_measured_shapes():
+    """Host-side split-K plan of the shapes the benchmarks run (split count =
+    workspace bytes / (M x N x 4)): decode projections split until their
+    128-row weight tiles cover the 148 SMs; the 16384-token prefill GEMM and
+    the lm_head (1187 tiles) never split; the few-hundred-token vision / text
+    projections split only where their output tiles leave SMs idle."""
+    L = capi.lib()
+    want = {
+        (64, 6144, 4096): 3,      # Qwen3-8B decode qkv: 48 tiles x 3
+        (64, 4096, 4096): 4,      # o
+        (64, 24576, 4096): 3,     # gate/up: 192 tiles x 3
+        (64, 4096, 12288): 4,     # down
+        (64, 151936, 4096): 0,    # lm_head
+        (16384, 24576, 4096): 0,  # prefill gate/up
+        (784, 1024, 1024): 2,     # vision proj
+        (784, 1024, 4096): 5,     # vision fc2
+        (784, 4096, 1024): 0,     # vision fc1
+        (256, 2048, 6144): 9,     # Qwen3-VL text down
+    }
+    for (M, N, K), splits in want.items():
+        assert L.b200_gemm_workspace_bytes(M, N, K, 0) == splits * M * N * 4, (M, N, K)
