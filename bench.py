@@ -335,6 +335,34 @@ def kernel_roofline_moe_gemm(L, torch, dev, reps=10):
     return ms, E * N * K * 2 + rows * K * 2 + rows * N // 2 * 2
 
 
+def kernel_roofline_image_preprocess(L, torch, dev, reps=20):
+    """Image preprocessing of the bench_preprocess frame (seeded 3x1080x1920
+    uint8, resident on the device) into fp16 pixel values: the coefficient
+    kernel + preprocess_fused_kernel per image.  Algorithmic bytes = the uint8
+    frame read + the fp16 pixel values written."""
+    import numpy as np
+
+    C = 3
+    img = np.random.default_rng(11).integers(0, 256, (C, PP_H, PP_W), dtype=np.uint8)
+    nh, nw = ctypes.c_int(), ctypes.c_int()
+    check(L.b200_smart_resize(PP_H, PP_W, 32, 4096, 1843200, ctypes.byref(nh), ctypes.byref(nw)), "smart_resize")
+    n = (nh.value // 16) * (nw.value // 16)
+    pv = torch.empty(n, C * 2 * 16 * 16, dtype=torch.float16, device=dev)
+    wsb = L.b200_preprocess_workspace_bytes(C, PP_H, PP_W, nh.value, nw.value)
+    ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
+    src = torch.from_numpy(img).to(dev)
+    npatch = ctypes.c_int64()
+    grid = (ctypes.c_int64 * 3)()
+
+    def run(st):
+        check(L.b200_preprocess_image(src.data_ptr(), C, PP_H, PP_W, 16, 2, 2, 4096, 1843200, None, None, 1,
+                                      pv.data_ptr(), pv.numel(), ctypes.byref(npatch), grid, ws.data_ptr(), wsb,
+                                      st.cuda_stream), "preprocess_image")
+
+    ms = _time_launches(torch, dev, run, reps)
+    return ms, img.nbytes + pv.numel() * 2
+
+
 def kernel_roofline_prefill_attention(L, torch, dev, reps=10):
     """tcgen05 causal prefill attention alone at the Qwen3-8B prefill shape (8
     sequences x 2048, 32 query / 8 kv heads of 128, the engine's packed q|k|v
@@ -1275,8 +1303,8 @@ def main():
     ap.add_argument("--no-deepseek", action="store_true", help="skip the DeepSeek-V2-Lite section")
     ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "prefill_attention", "mla_decode",
-                                                 "moe_gemm"],
-                    help="run only this kernel at its bench shape (2 warm-up + 3 launches), for ncu")
+                                                 "moe_gemm", "image_preprocess"],
+                    help="run only this kernel at its bench shape (3 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1291,7 +1319,7 @@ def main():
         dev = torch.device("cuda", local_rank)
         fn = {"decode_attention": kernel_roofline_decode_attention, "prefill_gemm": kernel_roofline_prefill_gemm,
               "prefill_attention": kernel_roofline_prefill_attention, "mla_decode": kernel_roofline_mla_decode,
-              "moe_gemm": kernel_roofline_moe_gemm}[args.profile_kernel]
+              "moe_gemm": kernel_roofline_moe_gemm, "image_preprocess": kernel_roofline_image_preprocess}[args.profile_kernel]
         ms, work = fn(capi.lib(), torch, dev, reps=3)
         print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
         return
