@@ -16,6 +16,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -574,6 +575,29 @@ int decode_splits(int batch, int nkv, int max_context) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(want, decode_max_splits(max_context)));
 }
 
+// The split-KV plan of one decode launch: the split count decode_splits picks,
+// rounded so every split covers whole K/V tiles, the tokens each split covers
+// and the fp32 scratch the splits need (per query head and split: 128 partial
+// outputs + one log-sum-exp).  b200_paged_decode, its allocation-free variant
+// and the workspace query all size from this one plan.
+struct DecodePlan {
+  int splits;
+  int tokens_per_split;
+  int64_t scratch_bytes;  // 0 when unsplit
+};
+
+DecodePlan decode_plan(int batch, int nq, int nkv, int max_context) {
+  DecodePlan d;
+  const int ctx = std::max(1, max_context);
+  const int want = decode_splits(batch, nkv, ctx);
+  const int tiles_total = (ctx + kDecTile - 1) / kDecTile;
+  const int tiles_per_split = (tiles_total + want - 1) / want;
+  d.splits = (tiles_total + tiles_per_split - 1) / tiles_per_split;
+  d.tokens_per_split = tiles_per_split * kDecTile;
+  d.scratch_bytes = d.splits > 1 ? (int64_t)batch * nq * d.splits * (kDecHD + 1) * (int64_t)sizeof(float) : 0;
+  return d;
+}
+
 // Opt one kernel (a distinct template argument per kernel) into large dynamic
 // shared memory, once per device.
 template <auto Kernel>
@@ -670,9 +694,12 @@ static __device__ __align__(256) unsigned char g_paged_decode_scratch[kNoAllocSc
 
 namespace {
 
-// Device address of g_paged_decode_scratch on the current device (nullptr on failure).
+// Device address of g_paged_decode_scratch on the current device (nullptr on
+// failure).  Entries are atomics: host threads that race on a device's first
+// call each look the address up and store the same value.  A cached address
+// does not survive cudaDeviceReset (the array is re-created with the context).
 void* noalloc_scratch(cudaError_t* err) {
-  static void* ptrs[64] = {nullptr};
+  static std::atomic<void*> ptrs[64];
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -680,13 +707,13 @@ void* noalloc_scratch(cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    *err = cudaGetSymbolAddress(&p, g_paged_decode_scratch);
+  void* cached = ptrs[dev].load(std::memory_order_acquire);
+  if (!cached) {
+    *err = cudaGetSymbolAddress(&cached, g_paged_decode_scratch);
     if (*err != cudaSuccess) return nullptr;
-    ptrs[dev] = p;
+    ptrs[dev].store(cached, std::memory_order_release);
   }
-  return ptrs[dev];
+  return cached;
 }
 
 }  // namespace
@@ -698,20 +725,17 @@ extern "C" int b200_paged_decode_noalloc(const void* q, int64_t q_stride, const 
                                          const int32_t* context_lens, int batch, int nq, int nkv, int head_dim,
                                          int block_size, int64_t num_blocks, float scale, void* out,
                                          int64_t out_stride, int max_context, b200_stream_t stream) {
+  // The argument checks b200_paged_decode makes before its plan, in the same
+  // order, so both entry points return the same code for the same bad call.
+  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out || batch < 0 || nq <= 0 || nkv <= 0 ||
+      nq % nkv || max_blocks_per_seq <= 0 || num_blocks <= 0 || max_context < 0)
+    return B200_ERROR_INVALID_PARAM;
+  if (head_dim != kDecHD || (block_size != 64 && block_size != 128) || nq / nkv > 16) return B200_ERROR_UNSUPPORTED;
   // Reject, before any launch, a problem whose split-KV scratch exceeds the
-  // array: the split count b200_paged_decode picks for this shape, times
-  // batch x nq x (head_dim + 1) fp32 values.
-  if (batch < 0 || nq <= 0 || nkv <= 0 || max_context < 0) return B200_ERROR_INVALID_PARAM;
-  if (batch > 0) {
-    const int ctx = std::max(1, max_context);
-    int splits = decode_splits(batch, nkv, ctx);
-    const int tiles_total = (ctx + kDecTile - 1) / kDecTile;
-    const int tiles_per_split = (tiles_total + splits - 1) / splits;
-    splits = (tiles_total + tiles_per_split - 1) / tiles_per_split;
-    const int64_t need =
-        splits > 1 ? (int64_t)batch * nq * splits * (kDecHD + 1) * (int64_t)sizeof(float) : 0;
-    if (need > kNoAllocScratchBytes) return B200_ERROR_INVALID_PARAM;
-  }
+  // array: the same plan b200_paged_decode runs, so a call that passes here
+  // is never silently run unsplit for want of scratch.
+  if (batch > 0 && decode_plan(batch, nq, nkv, max_context).scratch_bytes > kNoAllocScratchBytes)
+    return B200_ERROR_INVALID_PARAM;
   cudaError_t e = cudaSuccess;
   void* scratch = noalloc_scratch(&e);
   if (!scratch) return B200_ERROR_CUDA_BASE - (int)e;
@@ -758,15 +782,16 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_
   p.block_size = block_size;
   p.num_blocks = num_blocks;
   p.scale_log2 = scale * kLog2e;
-  int splits = decode_splits(batch, nkv, std::max(1, max_context));
-  const int64_t need = (int64_t)batch * nq * splits * (kDecHD + 1) * (int64_t)sizeof(float);
-  if (splits > 1 && (!workspace || workspace_bytes < need || !al16(workspace))) splits = 1;
-  // tokens per split: a multiple of the tile so tiles never straddle splits
-  int tiles_total = (std::max(1, max_context) + kDecTile - 1) / kDecTile;
-  int tiles_per_split = (tiles_total + splits - 1) / splits;
-  splits = (tiles_total + tiles_per_split - 1) / tiles_per_split;
+  // tokens per split: a multiple of the tile so tiles never straddle splits;
+  // without a workspace that holds the plan's scratch the context runs unsplit
+  const DecodePlan plan = decode_plan(batch, nq, nkv, max_context);
+  int splits = plan.splits;
+  p.tokens_per_split = plan.tokens_per_split;
+  if (splits > 1 && (!workspace || workspace_bytes < plan.scratch_bytes || !al16(workspace))) {
+    splits = 1;
+    p.tokens_per_split = ((std::max(1, max_context) + kDecTile - 1) / kDecTile) * kDecTile;
+  }
   p.splits = splits;
-  p.tokens_per_split = tiles_per_split * kDecTile;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
   p.ws_o = static_cast<float*>(workspace);

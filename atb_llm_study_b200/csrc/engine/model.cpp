@@ -1125,10 +1125,22 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
   for (int i = 0; i < n_ds; ++i) key += "/" + std::to_string(reinterpret_cast<uintptr_t>(deepstack[i]));
   static const bool no_graph = EnvInt("B200_DISABLE_GRAPHS", 0) != 0;
   auto it = enc_graphs_.find(key);
+  ++enc_tick_;
+  // keys seen once and not yet captured: bounded like the graphs (a serving
+  // loop whose buffers move would otherwise grow it without end)
+  if (it == enc_graphs_.end() && !enc_calls_.count(key) && enc_calls_.size() >= kMaxEncodeGraphs) enc_calls_.clear();
   if (it != enc_graphs_.end()) {
+    it->second.last_use = enc_tick_;
     B200_RETURN_IF(FromCuda(cudaGraphLaunch(it->second.exec, st)));
     launches_ = it->second.launches;
-  } else if (!no_graph && enc_graphs_.size() < kMaxEncodeGraphs && ++enc_calls_[key] >= 2) {
+  } else if (!no_graph && ++enc_calls_[key] >= 2) {
+    if (enc_graphs_.size() >= kMaxEncodeGraphs) {  // evict the least recently replayed graph
+      auto lru = enc_graphs_.begin();
+      for (auto g = enc_graphs_.begin(); g != enc_graphs_.end(); ++g)
+        if (g->second.last_use < lru->second.last_use) lru = g;
+      cudaGraphExecDestroy(lru->second.exec);  // an in-flight replay is freed when it completes
+      enc_graphs_.erase(lru);
+    }
     B200_RETURN_IF(FromCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed)));
     Status s = EncodeDevice(S, n_vis, vis_embeds, deepstack, n_ds, normalize, hidden_out);
     cudaGraph_t g = nullptr;
@@ -1137,7 +1149,7 @@ Status DecoderModel::Encode(const int64_t* ids, int64_t S, const int64_t* positi
     if (s == STATUS_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
     if (g) cudaGraphDestroy(g);
     if (s == STATUS_OK && e == cudaSuccess) {
-      enc_graphs_[key] = EncodeGraph{ex, launches_};
+      enc_graphs_[key] = EncodeGraph{ex, launches_, enc_tick_};
       enc_calls_.erase(key);
       B200_RETURN_IF(FromCuda(cudaGraphLaunch(ex, st)));
     } else {

@@ -199,14 +199,18 @@ class DecoderModel {
   std::map<int, cudaGraphExec_t> graphs_;
   std::map<int, int> decode_calls_;
   // text encode passes as CUDA graphs, keyed by the shape and the buffers the
-  // pass reads (a key is captured on its second call; at most kMaxEncodeGraphs)
+  // pass reads (a key is captured on its second call; at most kMaxEncodeGraphs,
+  // the least recently replayed one evicted to make room; the once-seen keys
+  // waiting for their second call are bounded by the same number)
   struct EncodeGraph {
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
+    uint64_t last_use = 0;
   };
   static constexpr size_t kMaxEncodeGraphs = 16;
   std::map<std::string, EncodeGraph> enc_graphs_;
   std::map<std::string, int> enc_calls_;
+  uint64_t enc_tick_ = 0;
   Status EncodeDevice(int64_t S, int64_t n_vis, const void* vis_embeds, const void* const* deepstack, int n_ds,
                       bool normalize, void* hidden_out);
   unsigned* err_ = nullptr;

@@ -1,7 +1,7 @@
 """Generate the committed golden fixtures by running the REFERENCE generator.
 
 Runs ``atb_cpp_llm/tests/python_reference/gen_cpu_reference.py`` from a
-reference checkout (default ``/root/reference``; it is imported, never copied)
+reference checkout (``--reference`` or ``ATB_LLM_REFERENCE``; it is imported, never copied)
 into a scratch directory, then packs the files that pin the decoder-layer hot
 path into compact ``.npz`` fixtures next to this script:
 
@@ -14,7 +14,7 @@ The inputs of the ``GetRopeIndex`` cases are not written by the generator,
 so ``get_rope_index`` is wrapped while the stages run to record its arguments.
 
 Usage (where a reference checkout exists; the tests read only the fixtures):
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout>   (or ATB_LLM_REFERENCE=<checkout>)
 """
 
 import argparse
@@ -44,7 +44,8 @@ def main():
     if os.environ.get("PYTHONHASHSEED") != "0":
         os.execve(sys.executable, [sys.executable] + sys.argv, dict(os.environ, PYTHONHASHSEED="0"))
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ATB_LLM_REFERENCE"),
+                    required="ATB_LLM_REFERENCE" not in os.environ)
     ap.add_argument("--max-bytes", type=int, default=600_000)
     args = ap.parse_args()
 

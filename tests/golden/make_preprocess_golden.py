@@ -12,7 +12,7 @@ tests regenerate); the PreprocessImage cases' uint8 input, PIL-chain fp16
 pixel values and grid.
 
 Usage (in a container that has the reference checkout and PIL):
-    python tests/golden/make_preprocess_golden.py [--reference /root/reference]
+    python tests/golden/make_preprocess_golden.py --reference <checkout>   (or ATB_LLM_REFERENCE=<checkout>)
 """
 
 import argparse
@@ -41,7 +41,8 @@ def prod_inputs():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ATB_LLM_REFERENCE"),
+                    required="ATB_LLM_REFERENCE" not in os.environ)
     args = ap.parse_args()
     tests_dir = os.path.join(args.reference, "atb_cpp_llm", "tests")
     sys.path.insert(0, os.path.join(tests_dir, "python_reference"))
