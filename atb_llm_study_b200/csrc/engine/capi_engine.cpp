@@ -330,3 +330,9 @@ extern "C" int b200_engine_context_len(b200_engine_t e, int slot, int64_t* out) 
   *out = e->model.ContextLen(slot);
   return *out < 0 ? ERROR_INVALID_PARAM : STATUS_OK;
 }
+
+extern "C" int b200_engine_kv_cache(b200_engine_t e, int layer, void** k_cache, void** v_cache, int64_t* num_blocks,
+                                    int* block_size, int* max_blocks_per_seq) {
+  if (!e) return ERROR_INVALID_PARAM;
+  return e->model.KvCache(layer, k_cache, v_cache, num_blocks, block_size, max_blocks_per_seq);
+}

@@ -542,6 +542,25 @@ Status DecoderModel::LoadSafetensors(const SafetensorsReader& r, const std::stri
   return STATUS_OK;
 }
 
+Status DecoderModel::KvCache(int l, void** k, void** v, int64_t* num_blocks, int* block_size,
+                             int* max_blocks) const {
+  if (l < 0 || l >= cfg_.layers || !ctx_) return ERROR_INVALID_PARAM;
+  if (cfg_.mla()) {
+    const int64_t rows = num_blocks_ * opt_.block_size;
+    if (k) *k = static_cast<uint16_t*>(lat_.data) + (int64_t)l * rows * (cfg_.kv_lora + cfg_.qk_rope);
+    if (v) *v = nullptr;
+  } else {
+    const int64_t kv_layer = 2 * num_blocks_ * cfg_.kv_heads * opt_.block_size * cfg_.head_dim;
+    uint16_t* kc = static_cast<uint16_t*>(kv_.data) + (int64_t)l * kv_layer;
+    if (k) *k = kc;
+    if (v) *v = kc + kv_layer / 2;
+  }
+  if (num_blocks) *num_blocks = num_blocks_;
+  if (block_size) *block_size = opt_.block_size;
+  if (max_blocks) *max_blocks = max_blocks_;
+  return STATUS_OK;
+}
+
 Status DecoderModel::ResetSlots() {
   std::fill(host_ctx_.begin(), host_ctx_.end(), 0);
   B200_RETURN_IF(FromCuda(cudaMemsetAsync(ctx_lens_.data, 0, ctx_lens_.bytes(), ctx_->GetStream())));

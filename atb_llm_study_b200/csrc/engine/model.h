@@ -110,6 +110,10 @@ class DecoderModel {
   size_t WeightBytes() const { return weight_bytes_; }
   size_t KvBytes() const { return kv_bytes_; }
   int64_t ContextLen(int slot) const { return slot >= 0 && slot < (int)host_ctx_.size() ? host_ctx_[slot] : -1; }
+  // Layer l's cache: GQA k / v [num_blocks, kv_heads, block_size, head_dim]
+  // (v null for a latent cache [num_blocks * block_size, kv_lora + qk_rope]);
+  // slot s owns blocks [s * max_blocks, (s + 1) * max_blocks) in order.
+  Status KvCache(int l, void** k, void** v, int64_t* num_blocks, int* block_size, int* max_blocks) const;
   // GPU kernel launches per Decode / Prefill call (for reporting).
   int DecodeLaunches() const;
   int PrefillLaunches() const;

@@ -623,6 +623,20 @@ B200_API int b200_engine_reset(b200_engine_t engine);
 B200_API int b200_engine_query(b200_engine_t engine, int what, int64_t* out);
 B200_API int b200_engine_context_len(b200_engine_t engine, int slot, int64_t* out);
 
+/* Device addresses of layer `layer`'s KV cache (ordered on the engine's
+ * stream; valid until b200_engine_destroy).  GQA models: k_cache / v_cache
+ * [num_blocks, kv_heads, block_size, head_dim] bf16.  Latent-attention models:
+ * k_cache is the latent cache [num_blocks * block_size, kv_lora + qk_rope]
+ * (per token the normalised compressed KV, then the roped key dims) and
+ * *v_cache is NULL.  Slot s owns blocks [s * max_blocks_per_seq, (s + 1) *
+ * max_blocks_per_seq) in order: its position p sits in block
+ * s * max_blocks_per_seq + p / block_size at offset p % block_size.  Output
+ * pointers may be NULL.  Replaces KVCacheManager::GetCachePtr
+ * (atb_cpp_llm/src/core/kv_cache_manager.h:58-66), which the reference only
+ * declares. */
+B200_API int b200_engine_kv_cache(b200_engine_t engine, int layer, void** k_cache, void** v_cache,
+                                  int64_t* num_blocks, int* block_size, int* max_blocks_per_seq);
+
 #ifdef __cplusplus
 }
 #endif
