@@ -26,6 +26,26 @@ __global__ void fill_normal_kernel(__nv_bfloat16* x, int64_t n, float mean, floa
   if (i + 1 < n) x[i + 1] = f2bf(mean + std * r * s);
 }
 
+// Element (r, c) of a rows x cols window takes the value the plain fill gives
+// global element gbase + r * gstride + c (pairs share one Box-Muller draw:
+// even index = cosine branch, odd = sine branch), so a shard of a matrix
+// filled through its window equals the same rows / columns of the whole
+// matrix filled at once.
+__global__ void fill_normal_window_kernel(__nv_bfloat16* x, int64_t rows, int64_t cols, float mean, float std,
+                                          uint64_t seed, int64_t gbase, int64_t gstride) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const int64_t r = i / cols, c = i % cols;
+  const uint64_t g = (uint64_t)(gbase + r * gstride + c);
+  const uint64_t h = mix64(seed * 0x9E3779B97F4A7C15ull + (g & ~1ull));
+  const float u1 = ((float)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+  const float u2 = (float)((h >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+  const float rad = sqrtf(-2.0f * logf(u1));
+  float s, co;
+  sincospif(2.0f * u2, &s, &co);
+  x[i] = f2bf(mean + std * rad * ((g & 1) ? s : co));
+}
+
 __global__ void fill_const_kernel(__nv_bfloat16* x, int64_t n, float v) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i < n) x[i] = f2bf(v);
@@ -110,6 +130,15 @@ int FillNormalBf16(void* x, int64_t n, float mean, float std, uint64_t seed, cud
   const int64_t threads = (n + 1) / 2;
   fill_normal_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(x), n, mean, std,
                                                                         seed);
+  return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
+}
+
+int FillNormalWindowBf16(void* x, int64_t rows, int64_t cols, float mean, float std, uint64_t seed, int64_t gbase,
+                         int64_t gstride, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const int64_t n = rows * cols;
+  fill_normal_window_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(x), rows, cols,
+                                                                          mean, std, seed, gbase, gstride);
   return cudaGetLastError() == cudaSuccess ? 0 : B200_ERROR_INFERENCE;
 }
 

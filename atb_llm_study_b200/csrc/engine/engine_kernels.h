@@ -8,6 +8,11 @@ namespace b200llm {
 
 // x[i] = mean + std * N(0,1) from a counter-based hash of (seed, i); bf16.
 int FillNormalBf16(void* x, int64_t n, float mean, float std, uint64_t seed, cudaStream_t st);
+// x[r * cols + c] = the value FillNormalBf16(seed) gives global element
+// gbase + r * gstride + c: fills a shard (row block / column block) of a
+// matrix with exactly the whole matrix's values at those positions.
+int FillNormalWindowBf16(void* x, int64_t rows, int64_t cols, float mean, float std, uint64_t seed, int64_t gbase,
+                         int64_t gstride, cudaStream_t st);
 // x[i] = value; bf16.
 int FillConstBf16(void* x, int64_t n, float value, cudaStream_t st);
 // out[i, :] = src[idx[i], :]; bf16 rows of width dim (dim % 8 == 0).

@@ -376,17 +376,62 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
 
 Status DecoderModel::InitRandomWeights(uint64_t seed, float std) {
   cudaStream_t st = ctx_->GetStream();
-  uint64_t k = seed * 1000003ull;
-  auto N = [&](DeviceTensor& t) { return FillNormalBf16(t.data, t.numel(), 0.f, std, ++k, st); };
+  const uint64_t k0 = seed * 1000003ull;
+  // Every matrix is filled as a window of the whole model's matrix (one hash
+  // key per matrix kind, values addressed by their index in the whole
+  // matrix): with tensor parallelism (rank tp_rank_ of tp_) or expert
+  // parallelism (rank ep_rank_ of ep_) each rank's shard holds exactly the
+  // values a one-GPU engine built from the same seed holds at those positions.
+  auto W = [&](const DeviceTensor& t, int64_t off, int64_t rows, int64_t cols, uint64_t key, int64_t gbase,
+               int64_t gstride) -> Status {
+    if (FillNormalWindowBf16(static_cast<uint16_t*>(t.data) + off, rows, cols, 0.f, std, k0 + key, gbase, gstride,
+                             st))
+      return ERROR_INFERENCE;
+    return STATUS_OK;
+  };
+  auto whole = [&](const DeviceTensor& t, uint64_t key) { return t.data ? W(t, 0, 1, t.numel(), key, 0, 0) : STATUS_OK; };
   auto O = [&](DeviceTensor& t) { return FillConstBf16(t.data, t.numel(), 1.f, st); };
-  B200_RETURN_IF(N(embed_));
-  if (!cfg_.tie_embeddings) B200_RETURN_IF(N(lm_head_));
-  B200_RETURN_IF(N(wqkv_));
-  B200_RETURN_IF(N(wo_));
-  B200_RETURN_IF(N(wgu_));
-  B200_RETURN_IF(N(wdown_));
-  for (DeviceTensor* t : {&router_, &egu_, &edown_, &sgu_, &sdown_, &wq_, &wkvb_}) B200_RETURN_IF(N(*t));
-  B200_RETURN_IF(O(kvnorm_));
+  const ModelConfig& g = gcfg_;
+  const int64_t H = cfg_.hidden, hd = cfg_.head_dim, L = cfg_.layers, rk = tp_rank_;
+  const int64_t n_dense = (int64_t)std::count_if(dense_idx_.begin(), dense_idx_.end(), [](int i) { return i >= 0; });
+  const int64_t n_moe = (int64_t)std::count_if(moe_idx_.begin(), moe_idx_.end(), [](int i) { return i >= 0; });
+  B200_RETURN_IF(whole(embed_, 1));
+  if (!cfg_.tie_embeddings)  // a tied embedding split over tensor-parallel ranks keeps the embedding's values
+    B200_RETURN_IF(W(lm_head_, 0, 1, cfg_.vocab * H, g.tie_embeddings ? 1 : 2, rk * cfg_.vocab * H, 0));
+  if (!cfg_.mla()) {
+    const int64_t ql = (int64_t)cfg_.heads * hd, kl = (int64_t)cfg_.kv_heads * hd;
+    const int64_t qg = (int64_t)g.heads * hd, kg = (int64_t)g.kv_heads * hd;
+    for (int64_t l = 0; l < L; ++l) {  // fused [q | k | v] rows, each a row block of the whole layer's
+      const int64_t lb = l * (ql + 2 * kl) * H, gb = l * (qg + 2 * kg) * H;
+      B200_RETURN_IF(W(wqkv_, lb, ql, H, 3, gb + rk * ql * H, H));
+      B200_RETURN_IF(W(wqkv_, lb + ql * H, kl, H, 3, gb + qg * H + rk * kl * H, H));
+      B200_RETURN_IF(W(wqkv_, lb + (ql + kl) * H, kl, H, 3, gb + (qg + kg) * H + rk * kl * H, H));
+    }
+  }
+  const int64_t AOl = cfg_.mla() ? (int64_t)cfg_.heads * cfg_.v_head : (int64_t)cfg_.heads * hd;
+  const int64_t AOg = g.mla() ? (int64_t)g.heads * g.v_head : (int64_t)g.heads * hd;
+  B200_RETURN_IF(W(wo_, 0, L * H, AOl, 4, rk * AOl, AOg));  // column block
+  const int64_t Il = cfg_.intermediate, Ig = g.intermediate;
+  for (int64_t d = 0; d < n_dense; ++d)  // interleaved gate/up rows: a row block per layer
+    B200_RETURN_IF(W(wgu_, d * 2 * Il * H, 2 * Il, H, 5, d * 2 * Ig * H + 2 * rk * Il * H, H));
+  if (n_dense) B200_RETURN_IF(W(wdown_, 0, n_dense * H, Il, 6, rk * Il, Ig));
+  if (n_moe) {
+    const int64_t E = g.experts, El = E / ep_, e0 = (int64_t)ep_rank_ * El;
+    const int64_t Iml = cfg_.moe_intermediate, Img = g.moe_intermediate;
+    const int64_t Isl = cfg_.shared_intermediate, Isg = g.shared_intermediate;
+    B200_RETURN_IF(whole(router_, 7));
+    for (int64_t m = 0; m < n_moe; ++m) {
+      for (int64_t e = 0; e < El; ++e)
+        B200_RETURN_IF(W(egu_, (m * El + e) * 2 * Iml * H, 2 * Iml, H, 8, (m * E + e0 + e) * 2 * Img * H +
+                         2 * rk * Iml * H, H));
+      B200_RETURN_IF(W(edown_, m * El * H * Iml, El * H, Iml, 9, (m * E + e0) * H * Img + rk * Iml, Img));
+      if (Isl > 0) B200_RETURN_IF(W(sgu_, m * 2 * Isl * H, 2 * Isl, H, 10, m * 2 * Isg * H + 2 * rk * Isl * H, H));
+    }
+    if (Isl > 0) B200_RETURN_IF(W(sdown_, 0, n_moe * H, Isl, 11, rk * Isl, Isg));
+  }
+  B200_RETURN_IF(whole(wq_, 12));
+  B200_RETURN_IF(whole(wkvb_, 13));
+  if (cfg_.mla()) B200_RETURN_IF(O(kvnorm_));
   absorb_dirty_ = true;
   B200_RETURN_IF(O(final_norm_));
   B200_RETURN_IF(O(qnorm_));

@@ -850,6 +850,79 @@ def moe_decode_bytes(C, P, batch, ctx):
     return 2 * (weights + cache)
 
 
+def sharded_parity(L, torch, dev, dist, world, rank, C, mode, seed=4242):
+    """The sharded code path against one GPU: a 2-layer copy of model C at
+    full width is built tensor-parallel (mode "tp") or expert-parallel ("ep")
+    over all ranks and, on rank 0, whole on one GPU from the same seed (the
+    engine's random init gives every shard the whole model's values at its
+    positions).  Both get rank 0's two 96-token prompts, then three decode
+    steps of fresh random tokens (eager, captured, replayed).  Rank 0 compares
+    its logits with the one-GPU engine's (tensor parallel: its vocabulary
+    shard) and the greedy tokens.  Collective: every rank calls it."""
+    import numpy as np
+
+    Cp = dict(C, num_hidden_layers=2)
+    H, V = Cp["hidden_size"], Cp["vocab_size"]
+    nseq, plen, steps = 2, 96, 3
+    T = nseq * plen
+    k = Cp.get("num_experts_per_tok", 1)
+    sym = 2 * T * H * 2 + (16 << 20) if mode == "tp" else 2 * ((64 << 10) + world * T * k * H * 2) + (1 << 20)
+    cfg = EngineConfig(None, json.dumps(Cp).encode(), dev.index, nseq, plen + steps + 16, T, BLOCK, seed, 0.02)
+    rng = np.random.default_rng(900 + (rank if mode == "ep" else 0))  # expert parallel: every rank its own prompts
+    prompts = rng.integers(0, V, T).astype(np.int64)
+    feed = rng.integers(0, V, (steps, nseq)).astype(np.int64)
+    vcols = V // world if mode == "tp" else V
+
+    def run(e, cols):
+        lens, slots = np.full(nseq, plen, np.int32), np.arange(nseq, dtype=np.int32)
+        nxt = np.zeros(nseq, np.int64)
+        lg = torch.empty(nseq, cols, dtype=torch.bfloat16, device=dev)
+        check(L.b200_engine_prefill(e, prompts.ctypes.data, 0, lens.ctypes.data, slots.ctypes.data, nseq, None,
+                                    nxt.ctypes.data, 0, lg.data_ptr()), "parity prefill")
+        torch.cuda.synchronize(dev)
+        logits, toks = [lg.float().cpu().numpy()], [nxt.copy()]
+        for i in range(steps):
+            out = np.zeros(nseq, np.int64)
+            check(L.b200_engine_decode(e, feed[i].ctypes.data, 0, slots.ctypes.data, nseq, out.ctypes.data, 0,
+                                       lg.data_ptr()), "parity decode")
+            torch.cuda.synchronize(dev)
+            logits.append(lg.float().cpu().numpy())
+            toks.append(out.copy())
+        return np.concatenate(logits), np.concatenate(toks)
+
+    comm = make_comm(L, dist, world, rank, dev, sym)
+    eng = ctypes.c_void_p()
+    create = L.b200_engine_create_tp if mode == "tp" else L.b200_engine_create_ep
+    check(create(ctypes.byref(cfg), comm, ctypes.byref(eng)), f"parity engine_create_{mode}")
+    try:
+        got, got_tok = run(eng, vcols)
+        errs = ctypes.c_uint(0)
+        check(L.b200_device_error_read(ctypes.addressof(errs), 1, None), "device_error_read")
+    finally:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        L.b200_engine_destroy(eng)
+        L.b200_comm_destroy(comm)
+    res = None
+    if rank == 0:
+        ref_eng = ctypes.c_void_p()
+        check(L.b200_engine_create(ctypes.byref(cfg), ctypes.byref(ref_eng)), "parity engine_create")
+        try:
+            ref, ref_tok = run(ref_eng, V)
+        finally:
+            L.b200_engine_destroy(ref_eng)
+        ref_shard = ref[:, :vcols]
+        cos = [float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30)) for a, b in zip(got, ref_shard)]
+        top2 = np.sort(ref, 1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 0.05 * np.abs(ref).max(1)  # greedy token outside the bf16 noise
+        same = got_tok == ref_tok
+        res = {"layers": 2, "rows": len(cos), "min_cos": round(min(cos), 6),
+               "tokens_equal": f"{int(same.sum())}/{len(same)}", "device_errors": errs.value,
+               "parity": bool(min(cos) >= 0.999 and same[clear].all() and errs.value == 0)}
+    dist.barrier()
+    return res
+
+
 def bench_ep(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, batch, ctx, name):
     """Expert parallel over all ranks: every rank serves its OWN `batch`
     sequences at context `ctx` (data-parallel attention, whole replicas of the
@@ -859,6 +932,7 @@ def bench_ep(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, batch,
     tokens each step (own seed per rank)."""
     import numpy as np
 
+    parity = sharded_parity(L, torch, dev, dist, world, rank, C, "ep")
     H, k = C["hidden_size"], C["num_experts_per_tok"]
     T = 2 * ctx  # prefill tokens per call (two whole prompts)
     half = (64 << 10) + world * T * k * H * 2
@@ -932,7 +1006,7 @@ def bench_ep(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, batch,
                                              "peak_source": f"{src} copy"},
                 "prefill_tok_s": world * T / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
                 "prefill": f"{world} ranks x 2x{ctx}",
-                "decode_launches_per_step": v.value, "device_errors": errs.value}
+                "decode_launches_per_step": v.value, "device_errors": errs.value, "parity": parity}
     finally:
         torch.cuda.synchronize(dev)
         dist.barrier()
@@ -948,6 +1022,7 @@ def bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, seqs, 
     ranks."""
     import numpy as np
 
+    parity = sharded_parity(L, torch, dev, dist, world, rank, C, "tp")
     T = max(seqs * plen, ctx)
     comm = make_comm(L, dist, world, rank, dev, 2 * T * C["hidden_size"] * 2 + (16 << 20))
     max_ctx = ctx + warm + steps + 16
@@ -1015,7 +1090,7 @@ def bench_tp(L, torch, dev, dist, world, rank, steps, warm, stream_of, C, seqs, 
         return {"tp": world, "decode_batch": batch, "decode_ctx": ctx, "decode_tok_s": batch / (dec_ms / 1e3),
                 "decode_ms_per_step": dec_ms, "prefill": f"{seqs}x{plen}",
                 "prefill_tok_s": seqs * plen / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
-                "decode_launches_per_step": v.value, "device_errors": errs.value, "note": note}
+                "decode_launches_per_step": v.value, "device_errors": errs.value, "note": note, "parity": parity}
     finally:
         torch.cuda.synchronize(dev)
         dist.barrier()
@@ -1258,9 +1333,36 @@ def run_b200(args, rank, world, local_rank):
     if ds:
         result["deepseek_v2_lite"] = ds
     if dist:
+        # The sharded runs, compact, as the line's last key: speed-up / efficiency
+        # against the one-GPU sections of this same run (tensor parallel: one
+        # model's decode step, strong scaling; expert parallel: every rank its
+        # own batch, weak scaling) and the sharded-vs-one-GPU parity verdict.
+        mg = {"n": world}
+
+        def entry(sec, one_ms=None, one_tok_s=None):
+            e = {"decode_tok_s": round(sec["decode_tok_s"], 1), "ms": round(sec["decode_ms_per_step"], 3)}
+            if one_ms:
+                e["speedup_vs_1gpu"] = round(one_ms / sec["decode_ms_per_step"], 3)
+                e["eff"] = round(one_ms / sec["decode_ms_per_step"] / world, 3)
+            if one_tok_s:
+                e["eff"] = round(sec["decode_tok_s"] / (world * one_tok_s), 3)
+            par = sec.get("parity") or {}
+            e["parity"] = par.get("parity")
+            e["min_cos"] = par.get("min_cos")
+            return e
+
+        if tp:
+            mg["tp_qwen3_8b"] = entry(tp, one_ms=dec_ms / steps)
+        if tp_mx:
+            mg["tp_mixtral"] = entry(tp_mx, one_ms=mx["decode_ms_per_step"] if mx else None)
+        if ep_mx:
+            mg["ep_mixtral"] = entry(ep_mx, one_tok_s=mx["decode_tok_s"] if mx else None)
+        if ep_ds:
+            mg["ep_deepseek"] = entry(ep_ds, one_tok_s=ds["decode_tok_s"] if ds else None)
+        result["multi_gpu"] = mg
         dist.barrier()
     if rank == 0:
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             try:
                 result["cpu_baseline"] = cpu_baseline()
             except Exception as e:  # the CPU leg must not sink the GPU number
