@@ -24,6 +24,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -624,6 +625,11 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
       }
     }
   }
+  static const int forced = [] {  // tuning override for swapped (decode-sized) GEMMs: B200_GEMM_SPLITS=<n>
+    const char* v = std::getenv("B200_GEMM_SPLITS");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (forced > 0 && g.swap) best = std::max(1, std::min(forced, g.kb_total));
   g.kb_per_split = (g.kb_total + best - 1) / best;
   g.splits = (g.kb_total + g.kb_per_split - 1) / g.kb_per_split;
   g.ws_bytes = g.splits > 1 ? (int64_t)g.splits * M * N * (int64_t)sizeof(float) : 0;

@@ -489,6 +489,51 @@ B200_API int b200_ep_combine(b200_comm_t comm, const void* results, int64_t recv
                              const void* residual, const void* shared, void* out, const void* norm_weight,
                              void* normed, float eps, b200_stream_t stream);
 
+/* -------------------------------------------------------- layer-graph seam */
+
+/* One pre-norm decoder layer, inputs in the reference's variant-pack order:
+ *   inputs[] = hidden [T, H], q_w [nq*hd, H], k_w [nkv*hd, H], v_w [nkv*hd, H],
+ *              o_w [H, nq*hd], (q_norm_w [hd], k_norm_w [hd] when use_qk_norm),
+ *              gate_w [I, H], up_w [I, H], down_w [H, I], input_ln_w [H],
+ *              post_ln_w [H]                    (bf16, device),
+ *              cos, sin [T, hd]                 (fp32, device; rotation over the whole head),
+ *              (mask when use_mask; never read),
+ *              seqlen [num_seqs]                (int32, HOST; lengths of the packed sequences, sum T)
+ * num_inputs = 13 + 2 * use_qk_norm + use_mask (15 / 16 with QK norm, as
+ * the reference's graph).  use_mask != 0 gives causal attention (key j masked
+ * for query i when j > i, the only mask the reference builds,
+ * MakeCausalMaskFp16, atb_cpp_llm/src/runners/text_runner.cpp:74-85; its
+ * tensor is not read); use_mask == 0 attends over the whole sequence.
+ * output [T, H] bf16 (may alias hidden).  out = h1 + down(silu(gate n2) * up n2),
+ * h1 = hidden + o(attn(rope(qknorm(qkv(n1))))), n1 / n2 the RMSNorms.
+ * workspace >= b200_text_decoder_layer_workspace_bytes (256-byte aligned);
+ * calls sharing a workspace must not overlap on the GPU.
+ * Replaces TextDecoderLayerGraph::Build + ExecuteOperation
+ * (atb_cpp_llm/src/components/text/decoder_layer_graph.cpp:13-154,
+ * atb_cpp_llm/src/families/base_model.h:91-148). */
+B200_API int64_t b200_text_decoder_layer_workspace_bytes(int64_t T, int hidden, int num_heads, int num_kv_heads,
+                                                         int head_dim, int intermediate);
+B200_API int b200_text_decoder_layer(const void* const* inputs, int num_inputs, void* output, int64_t T,
+                                     int num_seqs, int hidden, int num_heads, int num_kv_heads, int head_dim,
+                                     int intermediate, float epsilon, int use_qk_norm, int use_mask,
+                                     void* workspace, int64_t workspace_bytes, b200_stream_t stream);
+
+/* One vision (ViT) block, inputs in the reference's variant-pack order:
+ *   inputs[] = hidden [N, H], qkv_w [3H, H], qkv_b [3H], proj_w [H, H], proj_b [H],
+ *              fc1_w [I, H], fc1_b [I], fc2_w [H, I], fc2_b [H],
+ *              n1_w, n1_b, n2_w, n2_b [H]      (bf16, device),
+ *              c, s [N, head_dim]               (fp32, device; the 2-D vision rope tables),
+ *              seq [num_seqs]                   (int32, HOST; attention stays within each sequence)
+ * num_inputs = 16, H = num_heads * head_dim.  out = r1 + fc2(gelu_tanh(fc1(LN2(r1)))),
+ * r1 = hidden + proj(attn(rope(qkv(LN1(hidden))))) (bidirectional).
+ * output [N, H] bf16 (may alias hidden); workspace >= b200_vision_block_workspace_bytes.
+ * Replaces VisionBlockGraph::Build (atb_cpp_llm/src/components/vision/vision_block_graph.cpp:12-79)
+ * + ExecuteOperation. */
+B200_API int64_t b200_vision_block_workspace_bytes(int64_t N, int hidden, int intermediate);
+B200_API int b200_vision_block(const void* const* inputs, int num_inputs, void* output, int64_t N, int num_seqs,
+                               int hidden, int num_heads, int head_dim, int intermediate, float epsilon,
+                               void* workspace, int64_t workspace_bytes, b200_stream_t stream);
+
 /* ----------------------------------------------------------------- engine */
 
 /* A decoder model on one GPU: weights, a paged KV cache of max_batch slots x
