@@ -5,6 +5,7 @@
 #include <set>
 
 #include "engine/engine_kernels.h"
+#include "engine/weight_plan.h"
 #include "fused.h"
 #include "gemm.h"
 #include "mla.h"
@@ -148,34 +149,17 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
   if (opt.max_batch <= 0 || opt.max_context <= 0 || opt.max_prefill_tokens <= 0 ||
       (opt.block_size != 64 && opt.block_size != 128))
     return ERROR_INVALID_PARAM;
-  // Tensor parallel: this rank keeps nq/P query heads (and the matching kv
-  // heads), I/P of the MLP width and V/P of the vocabulary; everything below
-  // sizes from that local view.
-  ModelConfig cfg = whole;
   if (opt.comm && opt.expert_parallel) {
     // Expert parallel: whole replica of everything but the routed experts, which split into equal blocks
     B200_RETURN_IF(b200_comm_info(opt.comm, &ep_, &ep_rank_, &ep_bufs_[0], &ep_bufs_[1], nullptr));
-    if (whole.experts <= 0 || whole.experts % ep_ || whole.experts > 256) return ERROR_UNSUPPORTED;
   } else if (opt.comm) {
     B200_RETURN_IF(b200_comm_info(opt.comm, &tp_, &tp_rank_, &tp_buf_[0], &tp_buf_[1], nullptr));
-    if (tp_ > 1) {
-      // GQA attention (dense or mixture-of-experts MLPs; an expert's width is split like a dense MLP's)
-      if (whole.mla() || whole.mrope) return ERROR_UNSUPPORTED;
-      if (whole.heads % tp_ || whole.kv_heads % tp_ || whole.intermediate % tp_ || whole.vocab % tp_ ||
-          (whole.intermediate / tp_) % 8 || (whole.vocab / tp_) % 8 || whole.hidden > 8192)
-        return ERROR_UNSUPPORTED;
-      if (whole.experts > 0 && (whole.moe_intermediate % tp_ || (whole.moe_intermediate / tp_) % 8 ||
-                                whole.shared_intermediate % tp_ || (whole.shared_intermediate / tp_) % 8))
-        return ERROR_UNSUPPORTED;
-      cfg.heads /= tp_;
-      cfg.kv_heads /= tp_;
-      cfg.intermediate /= tp_;
-      cfg.vocab /= tp_;
-      cfg.moe_intermediate /= tp_;
-      cfg.shared_intermediate /= tp_;
-      cfg.tie_embeddings = false;  // lm_head is this rank's vocabulary rows, the embedding stays whole
-    }
   }
+  // Tensor parallel: this rank keeps nq/P query heads (and the matching kv
+  // heads), I/P of the MLP width and V/P of the vocabulary; everything below
+  // sizes from that local view.
+  B200_RETURN_IF(MakeShardView(whole, tp_, tp_rank_, ep_, ep_rank_, view_));
+  const ModelConfig cfg = view_.local;
   cfg_ = cfg;
   B200_RETURN_IF(ContextManager::Create(opt.device, ctx_));
   alloc_.reset(new TensorAllocator(ctx_->GetStream()));
@@ -441,131 +425,58 @@ Status DecoderModel::InitRandomWeights(uint64_t seed, float std) {
   return ctx_->Synchronize();
 }
 
-Status DecoderModel::SetWeight(const std::string& name_in, const void* host, DType dtype, int64_t numel) {
+Status DecoderModel::SetWeight(const std::string& name, const void* host, DType dtype, int64_t numel) {
   if (!host || numel <= 0) return ERROR_INVALID_PARAM;
-  std::string name = name_in;
-  if (starts_with(name, "model.language_model.")) name = "model." + name.substr(21);
+  // Tensor parallel: the whole tensor arrives and this rank keeps a block of rows
+  // (column-parallel q/k/v, gate/up, lm_head) or of columns (row-parallel o,
+  // down); expert parallel: only this rank's experts.  The placement is the
+  // host plan the shard query b200_weight_shard also runs.
+  std::vector<WeightCopy> ops;
+  B200_RETURN_IF(PlanWeight(view_, name, numel, ops));
+  if (ops.empty()) return STATUS_OK;
   std::vector<uint16_t> b16;
   const char* dt = dtype == DType::BF16 ? "BF16" : dtype == DType::FP16 ? "F16" : dtype == DType::FP32 ? "F32" : "";
   B200_RETURN_IF(ToBf16(static_cast<const uint8_t*>(host), dt, (size_t)numel, b16));
-  const int64_t H = cfg_.hidden, hd = cfg_.head_dim, I = cfg_.intermediate, QKV = cfg_.qkv_dim();
-  const int64_t AO = (int64_t)cfg_.heads * hd;
   cudaStream_t st = ctx_->GetStream();
-  auto put = [&](const DeviceTensor& t, int64_t elem_off, int64_t expect) -> Status {
-    if (numel != expect) return ERROR_INVALID_PARAM;
-    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(static_cast<uint16_t*>(t.data) + elem_off, b16.data(),
-                                            (size_t)numel * 2, cudaMemcpyHostToDevice, st)));
-    return ctx_->Synchronize();
-  };
-  // Tensor parallel: the whole tensor arrives; this rank keeps a block of rows
-  // (column-parallel q/k/v, gate/up, lm_head) or of columns (row-parallel o, down).
-  const int64_t P = tp_, rk = tp_rank_;
-  auto put_rows = [&](const DeviceTensor& t, int64_t elem_off, int64_t expect, int64_t rows_local,
-                      int64_t row_len) -> Status {
-    if (numel != expect) return ERROR_INVALID_PARAM;
-    B200_RETURN_IF(FromCuda(cudaMemcpyAsync(static_cast<uint16_t*>(t.data) + elem_off,
-                                            b16.data() + rk * rows_local * row_len,
-                                            (size_t)(rows_local * row_len) * 2, cudaMemcpyHostToDevice, st)));
-    return ctx_->Synchronize();
-  };
-  auto put_cols = [&](const DeviceTensor& t, int64_t elem_off, int64_t rows, int64_t cols_local) -> Status {
-    if (numel != rows * cols_local * P) return ERROR_INVALID_PARAM;
-    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(static_cast<uint16_t*>(t.data) + elem_off, (size_t)cols_local * 2,
-                                              b16.data() + rk * cols_local, (size_t)cols_local * P * 2,
-                                              (size_t)cols_local * 2, (size_t)rows, cudaMemcpyHostToDevice, st)));
-    return ctx_->Synchronize();
-  };
-  if (name == "model.embed_tokens.weight") {
-    B200_RETURN_IF(put(embed_, 0, gcfg_.vocab * H));
-    if (gcfg_.tie_embeddings && !cfg_.tie_embeddings)  // tensor parallel: lm_head = this rank's rows
-      return put_rows(lm_head_, 0, gcfg_.vocab * H, cfg_.vocab, H);
-    return STATUS_OK;
+  for (const WeightCopy& op : ops) {
+    DeviceTensor* t = WeightTensor(op.dst);
+    if (!t || !t->data) return ERROR_WEIGHT_LOAD;
+    if (op.rows <= 0 || op.dst_off + (op.rows - 1) * op.dst_pitch + op.width > t->numel() ||
+        op.src_off + (op.rows - 1) * op.src_pitch + op.width > numel)
+      return ERROR_INVALID_PARAM;
+    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(static_cast<uint16_t*>(t->data) + op.dst_off, (size_t)op.dst_pitch * 2,
+                                              b16.data() + op.src_off, (size_t)op.src_pitch * 2,
+                                              (size_t)op.width * 2, (size_t)op.rows, cudaMemcpyHostToDevice, st)));
+    if (cfg_.mla() && (op.dst == WTensor::WQ || op.dst == WTensor::KVNORM || op.dst == WTensor::WKVB ||
+                       op.dst == WTensor::WO))
+      absorb_dirty_ = true;
   }
-  if (name == "lm_head.weight") {
-    if (cfg_.tie_embeddings) return STATUS_OK;
-    return put_rows(lm_head_, 0, gcfg_.vocab * H, cfg_.vocab, H);
+  return ctx_->Synchronize();
+}
+
+DeviceTensor* DecoderModel::WeightTensor(WTensor t) {
+  switch (t) {
+    case WTensor::EMBED: return &embed_;
+    case WTensor::LM_HEAD: return &lm_head_;
+    case WTensor::FINAL_NORM: return &final_norm_;
+    case WTensor::WQ: return &wq_;
+    case WTensor::KVNORM: return &kvnorm_;
+    case WTensor::WKVB: return &wkvb_;
+    case WTensor::WO: return &wo_;
+    case WTensor::WQKV: return &wqkv_;
+    case WTensor::QNORM: return &qnorm_;
+    case WTensor::KNORM: return &knorm_;
+    case WTensor::ILN: return &iln_;
+    case WTensor::PLN: return &pln_;
+    case WTensor::WGU: return &wgu_;
+    case WTensor::WDOWN: return &wdown_;
+    case WTensor::ROUTER: return &router_;
+    case WTensor::EGU: return &egu_;
+    case WTensor::EDOWN: return &edown_;
+    case WTensor::SGU: return &sgu_;
+    case WTensor::SDOWN: return &sdown_;
   }
-  if (name == "model.norm.weight") return put(final_norm_, 0, H);
-  const std::string pre = "model.layers.";
-  if (!starts_with(name, pre)) return ERROR_WEIGHT_LOAD;
-  size_t dot = name.find('.', pre.size());
-  if (dot == std::string::npos) return ERROR_WEIGHT_LOAD;
-  const int l = std::atoi(name.substr(pre.size(), dot - pre.size()).c_str());
-  if (l < 0 || l >= cfg_.layers) return ERROR_WEIGHT_LOAD;
-  const std::string leaf = name.substr(dot + 1);
-  if (cfg_.mla() && starts_with(leaf, "self_attn.")) {
-    const int64_t nh = cfg_.heads, R = cfg_.kv_lora, dr = cfg_.qk_rope;
-    const int64_t NQP = nh * (cfg_.qk_nope + dr) + R + dr, KVB = nh * (cfg_.qk_nope + cfg_.v_head);
-    const int64_t AOm = nh * cfg_.v_head;
-    absorb_dirty_ = true;
-    if (leaf == "self_attn.q_proj.weight") return put(wq_, (int64_t)l * NQP * H, nh * (cfg_.qk_nope + dr) * H);
-    if (leaf == "self_attn.kv_a_proj_with_mqa.weight")
-      return put(wq_, (int64_t)l * NQP * H + nh * (cfg_.qk_nope + dr) * H, (R + dr) * H);
-    if (leaf == "self_attn.kv_a_layernorm.weight") return put(kvnorm_, (int64_t)l * R, R);
-    if (leaf == "self_attn.kv_b_proj.weight") return put(wkvb_, (int64_t)l * KVB * R, KVB * R);
-    if (leaf == "self_attn.o_proj.weight") return put(wo_, (int64_t)l * H * AOm, H * AOm);
-    return ERROR_WEIGHT_LOAD;
-  }
-  const int64_t nq = (int64_t)cfg_.heads * hd, nk = (int64_t)cfg_.kv_heads * hd;
-  if (leaf == "self_attn.q_proj.weight") return put_rows(wqkv_, (int64_t)l * QKV * H, nq * P * H, nq, H);
-  if (leaf == "self_attn.k_proj.weight") return put_rows(wqkv_, (int64_t)l * QKV * H + nq * H, nk * P * H, nk, H);
-  if (leaf == "self_attn.v_proj.weight")
-    return put_rows(wqkv_, (int64_t)l * QKV * H + (nq + nk) * H, nk * P * H, nk, H);
-  if (leaf == "self_attn.o_proj.weight") return put_cols(wo_, (int64_t)l * H * AO, H, AO);
-  if (leaf == "self_attn.q_norm.weight") return put(qnorm_, (int64_t)l * hd, hd);
-  if (leaf == "self_attn.k_norm.weight") return put(knorm_, (int64_t)l * hd, hd);
-  if (leaf == "input_layernorm.weight") return put(iln_, (int64_t)l * H, H);
-  if (leaf == "post_attention_layernorm.weight") return put(pln_, (int64_t)l * H, H);
-  // rows 2j / 2j+1 of a fused gate/up matrix hold gate[j] / up[j] (SwiGLU epilogue layout);
-  // `inter` rows of the source starting at row src_row
-  auto put_interleaved = [&](const DeviceTensor& t, int64_t elem_off, int64_t inter, bool up,
-                             int64_t src_row = 0, int64_t parts = 1) -> Status {
-    if (numel != inter * parts * H) return ERROR_INVALID_PARAM;
-    uint16_t* dst = static_cast<uint16_t*>(t.data) + elem_off + (up ? H : 0);
-    B200_RETURN_IF(FromCuda(cudaMemcpy2DAsync(dst, (size_t)2 * H * 2, b16.data() + src_row * H, (size_t)H * 2,
-                                              (size_t)H * 2, (size_t)inter, cudaMemcpyHostToDevice, st)));
-    return ctx_->Synchronize();
-  };
-  const int di = dense_idx_[l], mi = moe_idx_[l];
-  if (di >= 0) {
-    if (leaf == "mlp.down_proj.weight") return put_cols(wdown_, (int64_t)di * H * I, H, I);
-    if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight")
-      return put_interleaved(wgu_, (int64_t)di * 2 * I * H, I, leaf[4] == 'u', rk * I, P);
-    return ERROR_WEIGHT_LOAD;
-  }
-  // MoE layer: Mixtral "block_sparse_moe.{gate, experts.E.w1/w3/w2}", Qwen3-MoE /
-  // DeepSeek "mlp.{gate, experts.E.gate_proj/up_proj/down_proj, shared_experts.*}"
-  const int64_t E = cfg_.experts, Im = cfg_.moe_intermediate, Is = cfg_.shared_intermediate;
-  std::string m;
-  if (starts_with(leaf, "block_sparse_moe.")) m = leaf.substr(17);
-  else if (starts_with(leaf, "mlp.")) m = leaf.substr(4);
-  else return ERROR_WEIGHT_LOAD;
-  if (m == "gate.weight") return put(router_, (int64_t)mi * E * H, E * H);
-  if (starts_with(m, "shared_experts.") && Is > 0) {
-    const std::string s = m.substr(15);
-    if (s == "down_proj.weight") return put_cols(sdown_, (int64_t)mi * H * Is, H, Is);
-    if (s == "gate_proj.weight" || s == "up_proj.weight")
-      return put_interleaved(sgu_, (int64_t)mi * 2 * Is * H, Is, s[0] == 'u', rk * Is, P);
-    return ERROR_WEIGHT_LOAD;
-  }
-  if (!starts_with(m, "experts.")) return ERROR_WEIGHT_LOAD;
-  const size_t d2 = m.find('.', 8);
-  if (d2 == std::string::npos) return ERROR_WEIGHT_LOAD;
-  const int e = std::atoi(m.substr(8, d2 - 8).c_str());
-  if (e < 0 || e >= E) return ERROR_WEIGHT_LOAD;
-  const std::string w = m.substr(d2 + 1);
-  const int64_t El = E / ep_, e0 = (int64_t)ep_rank_ * El;
-  if (e < e0 || e >= e0 + El) {  // another rank's expert (expert parallel)
-    const bool known = w == "w1.weight" || w == "w2.weight" || w == "w3.weight" || w == "gate_proj.weight" ||
-                       w == "up_proj.weight" || w == "down_proj.weight";
-    return known ? STATUS_OK : ERROR_WEIGHT_LOAD;
-  }
-  const int64_t ge = (int64_t)mi * El + (e - e0);  // expert slot in the MoE stacks
-  if (w == "w2.weight" || w == "down_proj.weight") return put_cols(edown_, ge * H * Im, H, Im);
-  if (w == "w1.weight" || w == "gate_proj.weight")
-    return put_interleaved(egu_, ge * 2 * Im * H, Im, false, rk * Im, P);
-  if (w == "w3.weight" || w == "up_proj.weight") return put_interleaved(egu_, ge * 2 * Im * H, Im, true, rk * Im, P);
-  return ERROR_WEIGHT_LOAD;
+  return nullptr;
 }
 
 Status DecoderModel::LoadSafetensors(const SafetensorsReader& r, const std::string& prefix) {

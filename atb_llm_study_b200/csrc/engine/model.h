@@ -56,6 +56,29 @@ struct ModelConfig {
   int dense_layers() const { return experts > 0 ? std::min(first_dense, layers) : layers; }
 };
 
+// Weight placement (engine/weight_plan.h): where each Hugging Face weight goes
+// in one rank's device tensors.
+// The device tensors of a decoder model (DecoderModel's members of the same names).
+enum class WTensor : int {
+  EMBED, LM_HEAD, FINAL_NORM, WQ, KVNORM, WKVB, WO, WQKV, QNORM, KNORM, ILN, PLN, WGU, WDOWN, ROUTER, EGU, EDOWN,
+  SGU, SDOWN
+};
+
+// rows x width elements: source row r at src_off + r * src_pitch goes to
+// dst_off + r * dst_pitch of tensor `dst` (all in bf16 elements).
+struct WeightCopy {
+  WTensor dst;
+  int64_t dst_off, dst_pitch, src_off, src_pitch, width, rows;
+};
+
+// One rank's view of a model: the whole config, the local (sharded) config,
+// the group sizes and ranks, and which layers are dense / mixture-of-experts.
+struct ShardView {
+  ModelConfig whole, local;
+  int tp = 1, tp_rank = 0, ep = 1, ep_rank = 0;
+  std::vector<int> dense_idx, moe_idx;  // per layer: index into the dense / MoE stacks (-1 = other kind)
+};
+
 struct EngineOptions {
   int device = 0;
   int max_batch = 64;          // KV-cache sequence slots
@@ -129,6 +152,8 @@ class DecoderModel {
 
   ModelConfig cfg_;   // this rank's view (heads, kv heads, intermediate, vocab divided by tp_)
   ModelConfig gcfg_;  // the whole model
+  ShardView view_;    // both, with the group sizes / ranks the weight placement plan reads
+  DeviceTensor* WeightTensor(WTensor t);
   int tp_ = 1, tp_rank_ = 0;
   void* tp_buf_[2] = {nullptr, nullptr};  // this rank's partial-sum buffers in the group's symmetric memory
   Status TpProject(const void* A, int64_t K, const void* W, int64_t T, bool decode, int parity, const void* norm_w);

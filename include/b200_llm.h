@@ -613,6 +613,25 @@ B200_API int b200_engine_destroy(b200_engine_t engine);
 B200_API int b200_engine_set_weight(b200_engine_t engine, const char* name, const void* host, int dtype,
                                     int64_t numel);
 
+/* Host functions (no GPU): the part of one whole weight that a rank of a
+ * tensor-parallel group (tp_rank of tp_world; ep_world = 1) or of an
+ * expert-parallel group (ep_rank of ep_world; tp_world = 1) keeps, exactly as
+ * its b200_engine_create_tp / _create_ep engine places it: the dense bf16 rows
+ * (q / k / v heads, gate / up / lm_head rows) or columns (o / down) of its
+ * block, the whole tensor when replicated (norms, router, MLA, the vision
+ * tower), nothing (*out_numel = 0) for another rank's expert.  The weight
+ * comes from host memory (dtype 0 bf16, 1 fp16, 2 fp32) or from one tensor of
+ * a safetensors file; out holds out_capacity bf16 values.  Returns the status
+ * b200_engine_set_weight would (ERROR_WEIGHT_LOAD: a name the model does not
+ * use).  Replaces the per-rank placement the reference lacks
+ * (LoadQwen3VLWeights loads one device, qwen3vl_weights.cpp:79-264). */
+B200_API int b200_weight_shard(const char* config_json, int tp_world, int tp_rank, int ep_world, int ep_rank,
+                               const char* name, const void* host, int dtype, int64_t numel, void* out,
+                               int64_t out_capacity, int64_t* out_numel);
+B200_API int b200_weight_shard_file(const char* config_json, const char* safetensors_path, const char* name,
+                                    int tp_world, int tp_rank, int ep_world, int ep_rank, void* out,
+                                    int64_t out_capacity, int64_t* out_numel);
+
 /* Prefill fresh sequences packed back to back: ids [sum(seq_lens)] (host or
  * device), seq_lens / slots [num_seqs] (host), optional position_ids [3, T]
  * (host, mrope; NULL = 0..len-1 per sequence).  Fills the KV cache of each
