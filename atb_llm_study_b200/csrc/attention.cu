@@ -258,6 +258,11 @@ struct DecodeParams {
   float* ws_o;    // [batch][nq][splits][HD]
   float* ws_lse;  // [batch][nq][splits]
   unsigned* err;
+  // the next projection's weights, pulled into L2 by the CTAs of the last
+  // wave (linear CTA index >= pf_first) after their last tile load
+  const uint8_t* pf;
+  int64_t pf_bytes;
+  int pf_first;
 };
 
 // byte offset of 16-byte chunk c (0..15) of token row r inside a [64 x 128]
@@ -346,6 +351,11 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const __grid_
         tma_load_2d(dst + kDecTileBytes + kDecHalfBytes, &tmV, &full[s], 64, row);
       }
       __syncwarp();
+    }
+    if (lane == 0 && p.pf) {
+      const int64_t lin = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+      const int64_t total = (int64_t)gridDim.x * gridDim.y * gridDim.z;
+      prefetch_l2_share(p.pf, p.pf_bytes, lin - p.pf_first, total - p.pf_first);
     }
   } else {
   // ---- compute warps 0-3 ----
@@ -753,11 +763,12 @@ extern "C" int64_t b200_paged_decode_workspace_bytes(int batch, int nq, int head
   return (int64_t)batch * nq * s * (kDecHD + 1) * (int64_t)sizeof(float) + 256;
 }
 
-extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
-                                 const int32_t* block_tables, int max_blocks_per_seq, const int32_t* context_lens,
-                                 int batch, int nq, int nkv, int head_dim, int block_size, int64_t num_blocks,
-                                 float scale, void* out, int64_t out_stride, void* workspace, int64_t workspace_bytes,
-                                 int max_context, b200_stream_t stream) {
+namespace b200 {
+int paged_decode_launch(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                        const int32_t* block_tables, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                        int nq, int nkv, int head_dim, int block_size, int64_t num_blocks, float scale, void* out,
+                        int64_t out_stride, void* workspace, int64_t workspace_bytes, int max_context,
+                        cudaStream_t stream, const void* prefetch, int64_t prefetch_bytes) {
   if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out || batch < 0 || nq <= 0 || nkv <= 0 ||
       nq % nkv || max_blocks_per_seq <= 0 || num_blocks <= 0 || max_context < 0)
     return B200_ERROR_INVALID_PARAM;
@@ -799,6 +810,15 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_
   int dev = 0;
   cudaGetDevice(&dev);
   p.err = b200::error_word(dev);
+  p.pf = nullptr;
+  p.pf_bytes = 0;
+  p.pf_first = 0;
+  if (prefetch && prefetch_bytes >= 16 && (reinterpret_cast<uintptr_t>(prefetch) & 15u) == 0) {
+    const int64_t total = (int64_t)batch * nkv * splits;
+    p.pf = static_cast<const uint8_t*>(prefetch);
+    p.pf_bytes = prefetch_bytes & ~int64_t(15);
+    p.pf_first = (int)std::max<int64_t>(0, total - 2 * (int64_t)num_sms());  // the last wave (2 CTAs per SM)
+  }
 
   CUtensorMap tk, tv;
   if (!make_cache_tmap(&tk, k_cache, rows) || !make_cache_tmap(&tv, v_cache, rows)) return B200_ERROR_UNSUPPORTED;
@@ -812,4 +832,15 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_
     B200_CHECK_LAUNCH();
   }
   return B200_OK;
+}
+}  // namespace b200
+
+extern "C" int b200_paged_decode(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                 const int32_t* block_tables, int max_blocks_per_seq, const int32_t* context_lens,
+                                 int batch, int nq, int nkv, int head_dim, int block_size, int64_t num_blocks,
+                                 float scale, void* out, int64_t out_stride, void* workspace, int64_t workspace_bytes,
+                                 int max_context, b200_stream_t stream) {
+  return b200::paged_decode_launch(q, q_stride, k_cache, v_cache, block_tables, max_blocks_per_seq, context_lens,
+                                   batch, nq, nkv, head_dim, block_size, num_blocks, scale, out, out_stride, workspace,
+                                   workspace_bytes, max_context, stream, nullptr, 0);
 }

@@ -145,11 +145,38 @@ B200_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16);
+// issued by one thread, nothing waits for it.
+B200_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
+
+// This CTA's share of an L2 prefetch of [base, base + bytes) split evenly over
+// `parts` CTAs (part index `part`), in 32 KB requests.
+B200_DEV void prefetch_l2_share(const uint8_t* base, int64_t bytes, int64_t part, int64_t parts) {
+  if (!base || bytes <= 0 || part < 0 || part >= parts) return;
+  const int64_t chunk = (((bytes + parts - 1) / parts) + 15) & ~int64_t(15);
+  const int64_t end = (part + 1) * chunk < bytes ? (part + 1) * chunk : bytes;
+  for (int64_t off = part * chunk; off < end; off += 32768) {
+    const int64_t n = end - off;
+    prefetch_l2_bulk(base + off, (uint32_t)(n < 32768 ? n : 32768));
+  }
+}
+
 B200_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+B200_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 

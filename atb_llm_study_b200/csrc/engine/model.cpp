@@ -1,6 +1,7 @@
 #include "engine/model.h"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <set>
 
@@ -36,6 +37,13 @@ namespace b200llm {
 
 namespace {
 constexpr int B200_EPI_NONE_ = B200_EPI_NONE;
+// Bytes of the next projection's weights a decode kernel pulls into L2 from its
+// tail: about what HBM delivers in the ~8 us a launch boundary leaves idle
+// (tuning override: B200_DECODE_PREFETCH_MB=<n>, 0 = off).
+const int64_t kPrefetchBytes = [] {
+  const char* v = std::getenv("B200_DECODE_PREFETCH_MB");
+  return (v ? std::atoll(v) : 48ll) << 20;
+}();
 bool starts_with(const std::string& s, const std::string& p) { return s.compare(0, p.size(), p) == 0; }
 }  // namespace
 
@@ -534,10 +542,14 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
   float* ws = gemm_ws_.as<float>();
   // Projections may split K (decode-sized M): they then leave fp32 partials in
   // ws and the next kernel, which reads the result anyway, finishes the sum.
+  // Decode steps stream every weight once: each projection (and the decode
+  // attention) pulls the first bytes of the NEXT projection's weights into L2
+  // from its tail, so HBM keeps streaming across the launch boundary.
   auto gemm = [&](const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t N, int64_t K,
-                  int epi, const void* R, int64_t ldr, int* splits) {
+                  int epi, const void* R, int64_t ldr, int* splits, const void* pf = nullptr, int64_t pf_bytes = 0) {
     ++launches_;
-    return b200::gemm_launch(A, lda, B, ldb, C, ldc, T, N, K, epi, nullptr, R, ldr, ws, gemm_ws_bytes_, st, splits);
+    return b200::gemm_launch(A, lda, B, ldb, C, ldc, T, N, K, epi, nullptr, R, ldr, ws, gemm_ws_bytes_, st, splits,
+                             decode && kPrefetchBytes ? pf : nullptr, std::min<int64_t>(pf_bytes, kPrefetchBytes));
   };
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
   const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;
@@ -569,15 +581,19 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
                                                nq, nkv, (int)hd, (int)hd, scale, 1, st));
     } else {
       launches_ += attn_ws_bytes_ > 0 ? 2 : 1;
-      B200_RETURN_IF(b200_paged_decode(q, QKV, kc, vc, bt_batch_.as<int32_t>(), max_blocks_, ctx_batch_.as<int32_t>(),
-                                       batch, nq, nkv, (int)hd, opt_.block_size, num_blocks_, scale, attn_.data, AO,
-                                       attn_ws_.data, attn_ws_bytes_, opt_.max_context, st));
+      B200_RETURN_IF(b200::paged_decode_launch(q, QKV, kc, vc, bt_batch_.as<int32_t>(), max_blocks_,
+                                               ctx_batch_.as<int32_t>(), batch, nq, nkv, (int)hd, opt_.block_size,
+                                               num_blocks_, scale, attn_.data, AO, attn_ws_.data, attn_ws_bytes_,
+                                               opt_.max_context, st,
+                                               tp_ > 1 || !kPrefetchBytes ? nullptr : bf(wo_, (int64_t)l * H * AO),
+                                               std::min<int64_t>(H * AO * 2, kPrefetchBytes)));
     }
     if (tp_ > 1) {  // row-parallel o: partial sums, all-reduced with the residual and the post-attention norm
       B200_RETURN_IF(TpProject(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), T, decode, 0, bf(pln_, (int64_t)l * H)));
     } else {
     B200_RETURN_IF(gemm(attn_.data, AO, bf(wo_, (int64_t)l * H * AO), AO, hidden_.data, H, H, AO, B200_EPI_RESIDUAL,
-                        hidden_.data, H, &s_o));
+                        hidden_.data, H, &s_o, dense_idx_[l] >= 0 ? bf(wgu_, dense_idx_[l] * 2 * I * H) : nullptr,
+                        2 * I * H * 2));
     }
     }  // GQA attention
     if (tp_ > 1) {
@@ -612,13 +628,16 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
     // MLP block
     const int64_t dl = dense_idx_[l];
     B200_RETURN_IF(gemm(normed_.data, H, bf(wgu_, dl * 2 * I * H), H, act_.data, I, 2 * I, H, B200_EPI_SWIGLU,
-                        nullptr, 0, &s_gu));
+                        nullptr, 0, &s_gu, bf(wdown_, dl * H * I), H * I * 2));
     if (s_gu > 1) {
       ++launches_;
       B200_RETURN_IF(b200::splitk_reduce(ws, s_gu, T, 2 * I, B200_EPI_SWIGLU, nullptr, nullptr, 0, act_.data, I, st));
     }
+    const bool next_gqa = l + 1 < L && !cfg_.mla();
     B200_RETURN_IF(gemm(act_.data, I, bf(wdown_, dl * H * I), I, hidden_.data, H, H, I, B200_EPI_RESIDUAL,
-                        hidden_.data, H, &s_d));
+                        hidden_.data, H, &s_d,
+                        next_gqa ? bf(wqkv_, (int64_t)(l + 1) * QKV * H) : l + 1 == L ? lm_head_.data : nullptr,
+                        next_gqa ? QKV * H * 2 : cfg_.vocab * H * 2));
     if (l < (int)inject_feats_.size() && inject_n_ > 0) {
       // deepstack: hidden[rows] += feature[l] between this layer and the next norm
       if (s_d > 1) {
@@ -729,10 +748,10 @@ Status DecoderModel::MlaBlock(int l, int64_t T, bool decode, int batch, int* s_o
     B200_RETURN_IF(b200::gemm_launch(ckv_.data, R, bf(wkvb_, (int64_t)l * KVB * R), R, kvb_.data, KVB, T, KVB, R,
                                      B200_EPI_NONE, nullptr, nullptr, 0, nullptr, 0, st, nullptr));
     B200_RETURN_IF(b200::mla_build_k(kvb_.data, KVB, kpe_.data, kbuf_.data, T, (int)nh, st));
-    B200_RETURN_IF(b200_flash_prefill_ex(q, NQP, dn + dr, kbuf_.data, nh * (dn + dr), dn + dr,
-                                         static_cast<uint16_t*>(kvb_.data) + dn, KVB, dn + dv, attn_.data, nh * dv,
-                                         dv, cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, (int)nh, (int)nh,
-                                         (int)(dn + dr), (int)dv, cfg_.attn_scale, 1, st));
+    B200_RETURN_IF(b200_flash_prefill_packed(q, NQP, dn + dr, kbuf_.data, nh * (dn + dr), dn + dr,
+                                             static_cast<uint16_t*>(kvb_.data) + dn, KVB, dn + dv, attn_.data,
+                                             nh * dv, dv, cu_.as<int32_t>(), cur_num_seqs_, cur_max_len_, T, (int)nh,
+                                             (int)nh, (int)(dn + dr), (int)dv, cfg_.attn_scale, 1, st));
     return (Status)b200::gemm_launch(attn_.data, nh * dv, bf(wo_, (int64_t)l * H * nh * dv), nh * dv, hidden_.data,
                                      H, T, H, nh * dv, B200_EPI_RESIDUAL, nullptr, hidden_.data, H, ws,
                                      gemm_ws_bytes_, st, s_o);

@@ -1,9 +1,15 @@
-// Prefill attention on the 5th-generation tensor cores (64- or 128-wide heads).
+// Prefill attention on the 5th-generation tensor cores: 64- or 128-wide heads,
+// multi-head latent attention's decompressed heads (192-wide query / key:
+// 128 no-rope + 64 rope dims, 128-wide value), and 16- / 32-wide heads run as
+// 64-wide ones: a 3-D tensor map views every head as its own row of hd
+// elements, and the 64-column box fills the columns past hd with zeros, so the
+// scores are exact and only the first hd output columns are stored.
 //
 // One CTA = 128 query rows of one head of one sequence, 192 threads:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               (two 64-column boxes each, 128-byte swizzle) through a
-//               2-stage ring guarded by full/empty mbarriers.
+//               (64-column boxes, 128-byte swizzle) through rings guarded by
+//               full/empty mbarriers: 2 K stages; 2 V stages, 1 for 192-wide
+//               query/key heads (their tiles fill shared memory otherwise).
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma:
 //               S_j = Q K_j^T into one of two TMEM score buffers (M=128,
 //               N=128, K=128), and O += P_j V_j into the TMEM output
@@ -35,13 +41,16 @@ constexpr int kThreads = 192;
 constexpr int kTile = 128;                    // query rows per CTA = keys per tile
 constexpr int kBoxBytes = kTile * 128;        // 128 rows x 64 bf16 (one 128-byte swizzle span)
 constexpr int kPBytes = 2 * kBoxBytes;        // P: 128 rows x 128 keys
-// head width HD (64 or 128): Q, K and V tiles are HD / 64 boxes of 128 rows
-template <int HD>
+// query/key head width HDK (64, 128 or 192) and value width HDV (64 or 128):
+// Q and K tiles are HDK / 64 boxes of 128 rows, V tiles HDV / 64 boxes
+template <int HDK, int HDV>
 struct TcCfg {
-  static constexpr int BOXES = HD / 64;
-  static constexpr int TILE = BOXES * kBoxBytes;
-  static constexpr int SMEM = 5 * TILE + kPBytes + 1024 + 256;  // Q, K x2, V x2, P + alignment + barriers
-  static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD) | (1u << 16);  // B operand (V) MN-major
+  static constexpr int BOXES_QK = HDK / 64, BOXES_V = HDV / 64;
+  static constexpr int TILE_QK = BOXES_QK * kBoxBytes, TILE_V = BOXES_V * kBoxBytes;
+  static constexpr int V_STAGES = HDK > 128 ? 1 : 2;
+  // Q, K x2, V x V_STAGES, P + alignment + barriers
+  static constexpr int SMEM = 3 * TILE_QK + V_STAGES * TILE_V + kPBytes + 1024 + 256;
+  static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HDV) | (1u << 16);  // B operand (V) MN-major
 };
 constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256,384)
 constexpr float kRescaleLog2 = 8.f;           // move the running max only when it grows by > 2^8
@@ -80,22 +89,24 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <int HD, bool CAUSAL>
+// HEADS3D: the maps are [rows][heads][hd] views (coordinates: column 0, head
+// index, row) of heads narrower than the 64-column box; out_cols = hd.
+template <int HDK, int HDV, bool CAUSAL, bool HEADS3D = false>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, int64_t os,
                             int64_t ohs, const int32_t* __restrict__ cu, int nq, int nkv, int64_t qhs, int64_t khs,
-                            int64_t vhs, float scale_log2, int mblocks, unsigned* err) {
+                            int64_t vhs, float scale_log2, int mblocks, int out_cols, unsigned* err) {
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  using Cf = TcCfg<HD>;
-  constexpr int kTileBytes = Cf::TILE;
+  using Cf = TcCfg<HDK, HDV>;
+  constexpr int kTileBytes = Cf::TILE_QK, kVBytes = Cf::TILE_V, VS = Cf::V_STAGES;
   uint8_t* sK = smem + kTileBytes;
   uint8_t* sV = smem + 3 * kTileBytes;
-  uint8_t* sP = smem + 5 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes + kPBytes);
+  uint8_t* sP = sV + VS * kVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 3;
@@ -152,7 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const int qc = (int)(h * qhs), kc = (int)(kvh * khs), vc = (int)(kvh * vhs);
       mbar_arrive_expect_tx(q_full, kTileBytes);
-      for (int bx = 0; bx < Cf::BOXES; ++bx) tma_load_2d(sQ + bx * kBoxBytes, &tmQ, q_full, qc + 64 * bx, start + m0);
+      if (HEADS3D) tma_load_3d(sQ, &tmQ, q_full, 0, h, start + m0);
+      else
+        for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
+          tma_load_2d(sQ + bx * kBoxBytes, &tmQ, q_full, qc + 64 * bx, start + m0);
       for (int j = 0; j < ntiles && !*abort_flag; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -162,15 +176,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        for (int bx = 0; bx < Cf::BOXES; ++bx)
-          tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
-        if (j >= 2 && !mbar_wait(&v_empty[st], ph ^ 1, err)) {
+        if (HEADS3D) tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, kvh, row);
+        else
+          for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
+            tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
+        const int vst = j % VS;
+        const uint32_t vph = (j / VS) & 1;
+        if (j >= VS && !mbar_wait(&v_empty[vst], vph ^ 1, err)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        for (int bx = 0; bx < Cf::BOXES; ++bx)
-          tma_load_2d(sV + st * kTileBytes + bx * kBoxBytes, &tmV, &v_full[st], vc + 64 * bx, row);
+        mbar_arrive_expect_tx(&v_full[vst], kVBytes);
+        if (HEADS3D) tma_load_3d(sV + vst * kVBytes, &tmV, &v_full[vst], 0, kvh, row);
+        else
+          for (int bx = 0; bx < Cf::BOXES_V; ++bx)
+            tma_load_2d(sV + vst * kVBytes + bx * kBoxBytes, &tmV, &v_full[vst], vc + 64 * bx, row);
       }
     }
     __syncwarp();
@@ -186,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
+        for (int ks = 0; ks < HDK / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
           umma_bf16(tmem + st * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
         }
@@ -200,18 +220,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + 1 < ntiles && !(ok = issue_s(j + 1))) break;
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(p_full, j & 1, err) || !mbar_wait(&v_full[st], ph, err)) {
+        const int vst = j % VS;
+        if (!mbar_wait(p_full, j & 1, err) || !mbar_wait(&v_full[vst], (j / VS) & 1, err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + st * kTileBytes);
+        const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + vst * kVBytes);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
                     smem_desc_mn128(v0 + ks * 2048, kBoxBytes), Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
-        umma_commit(&v_empty[st]);
+        umma_commit(&v_empty[vst]);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -282,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < HDV / 32; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
             tmem_ld_wait();
@@ -309,13 +330,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = qpos < len;
       __nv_bfloat16* orow = out + (int64_t)(start + (valid ? qpos : 0)) * os + (int64_t)h * ohs;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HDV / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
         tmem_ld_wait();
         if (valid) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
+            if (HEADS3D && c * 32 + g * 8 >= out_cols) break;
             float f[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * g + i]) * inv;
@@ -366,22 +388,40 @@ bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int HD, bool CAUSAL>
+// [rows][heads][hd] view of a row-major bf16 matrix (row stride ld, head
+// stride hs, elements) for heads narrower than 64: box = 64 x 1 head x 128
+// rows, the 64 - hd columns past each head and rows past `rows` read as zeros.
+bool make_map_heads(CUtensorMap* m, const void* ptr, int64_t rows, int64_t heads, int64_t hd, int64_t hs,
+                    int64_t ld) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)(hs * 2), (cuuint64_t)(ld * 2)};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)kTile};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HDK, int HDV, bool CAUSAL, bool HEADS3D = false>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* out, int64_t os,
               int64_t ohs, const int32_t* cu, int num_seqs, int mblocks, int nq, int nkv, int64_t qhs, int64_t khs,
-              int64_t vhs, float scale_log2, cudaStream_t st) {
-  auto k = flash_prefill_tc_kernel<HD, CAUSAL>;
+              int64_t vhs, float scale_log2, int out_cols, cudaStream_t st) {
+  auto k = flash_prefill_tc_kernel<HDK, HDV, CAUSAL, HEADS3D>;
+  using Cf = TcCfg<HDK, HDV>;
+  static_assert(Cf::SMEM <= 227 * 1024, "shared memory");
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return B200_ERROR_UNSUPPORTED;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<HD>::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM) != cudaSuccess)
       return B200_ERROR_UNSUPPORTED;
     attr_set[dev] = true;
   }
-  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, TcCfg<HD>::SMEM, st, mq, mk, mv,
-                static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks,
+  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, Cf::SMEM, st, mq, mk, mv,
+                static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks, out_cols,
                 b200::error_word(dev));
   B200_CHECK_LAUNCH();
   return B200_OK;
@@ -395,7 +435,10 @@ extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_
                                          int64_t out_head_stride, const int32_t* cu_seqlens, int num_seqs,
                                          int max_seqlen, int64_t total_tokens, int nq, int nkv, int head_dim_qk,
                                          int head_dim_v, float scale, int causal, b200_stream_t stream) {
-  if (head_dim_qk != head_dim_v || (head_dim_qk != 128 && head_dim_qk != 64) || total_tokens <= 0)
+  const bool tc_shape = (head_dim_qk == head_dim_v && (head_dim_qk == 128 || head_dim_qk == 64 ||
+                                                      head_dim_qk == 32 || head_dim_qk == 16)) ||
+                        (head_dim_qk == 192 && head_dim_v == 128);
+  if (!tc_shape || total_tokens <= 0)
     return b200_flash_prefill_ex(q, q_stride, q_head_stride, k, k_stride, k_head_stride, v, v_stride, v_head_stride,
                                  out, out_stride, out_head_stride, cu_seqlens, num_seqs, max_seqlen, nq, nkv,
                                  head_dim_qk, head_dim_v, scale, causal, stream);
@@ -406,28 +449,41 @@ extern "C" int b200_flash_prefill_packed(const void* q, int64_t q_stride, int64_
     if (s < 0 || s % 8) return B200_ERROR_INVALID_PARAM;
   for (const void* p : {q, k, v, (const void*)out})
     if (reinterpret_cast<uintptr_t>(p) & 15u) return B200_ERROR_INVALID_PARAM;
-  const int hd = head_dim_qk;
+  const int hd = head_dim_qk, hdv = head_dim_v;
   const int64_t qcols = (int64_t)(nq - 1) * q_head_stride + hd, kcols = (int64_t)(nkv - 1) * k_head_stride + hd,
-                vcols = (int64_t)(nkv - 1) * v_head_stride + hd;
+                vcols = (int64_t)(nkv - 1) * v_head_stride + hdv;
   if (q_stride < qcols || k_stride < kcols || v_stride < vcols ||
-      out_stride < (int64_t)(nq - 1) * out_head_stride + hd)
+      out_stride < (int64_t)(nq - 1) * out_head_stride + hdv)
     return B200_ERROR_INVALID_PARAM;
   if (num_seqs == 0 || max_seqlen == 0) return B200_OK;
   if (num_seqs > 65535 || nq > 65535 || total_tokens > INT32_MAX || qcols > INT32_MAX || kcols > INT32_MAX ||
       vcols > INT32_MAX)
     return B200_ERROR_UNSUPPORTED;
+  const int mblocks = (max_seqlen + kTile - 1) / kTile;
+  const float sl2 = scale * 1.4426950408889634f;
   // the maps end at the last packed row and at each operand's last head, so
   // no tile reads past the buffers: rows beyond total_tokens read as zeros
   CUtensorMap mq, mk, mv;
+  if (hd < 64) {  // narrow heads as 64-wide ones, zero-filled past hd
+    if (!make_map_heads(&mq, q, total_tokens, nq, hd, q_head_stride, q_stride) ||
+        !make_map_heads(&mk, k, total_tokens, nkv, hd, k_head_stride, k_stride) ||
+        !make_map_heads(&mv, v, total_tokens, nkv, hd, v_head_stride, v_stride))
+      return B200_ERROR_UNSUPPORTED;
+    return causal ? launch_tc<64, 64, true, true>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs,
+                                                  mblocks, nq, nkv, q_head_stride, k_head_stride, v_head_stride, sl2,
+                                                  hd, stream)
+                  : launch_tc<64, 64, false, true>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens,
+                                                   num_seqs, mblocks, nq, nkv, q_head_stride, k_head_stride,
+                                                   v_head_stride, sl2, hd, stream);
+  }
   if (!make_map(&mq, q, total_tokens, qcols, q_stride) || !make_map(&mk, k, total_tokens, kcols, k_stride) ||
       !make_map(&mv, v, total_tokens, vcols, v_stride))
     return B200_ERROR_UNSUPPORTED;
-  const int mblocks = (max_seqlen + kTile - 1) / kTile;
-  const float sl2 = scale * 1.4426950408889634f;
-#define B200_TC(HD, C)                                                                                          \
-  launch_tc<HD, C>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq, nkv,         \
-                   q_head_stride, k_head_stride, v_head_stride, sl2, stream)
-  if (hd == 128) return causal ? B200_TC(128, true) : B200_TC(128, false);
-  return causal ? B200_TC(64, true) : B200_TC(64, false);
+#define B200_TC(HK, HV, C)                                                                                     \
+  launch_tc<HK, HV, C>(mq, mk, mv, out, out_stride, out_head_stride, cu_seqlens, num_seqs, mblocks, nq, nkv,     \
+                       q_head_stride, k_head_stride, v_head_stride, sl2, HV, stream)
+  if (hd == 192) return causal ? B200_TC(192, 128, true) : B200_TC(192, 128, false);
+  if (hd == 128) return causal ? B200_TC(128, 128, true) : B200_TC(128, 128, false);
+  return causal ? B200_TC(64, 64, true) : B200_TC(64, 64, false);
 #undef B200_TC
 }

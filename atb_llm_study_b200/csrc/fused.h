@@ -27,4 +27,12 @@ int splitk_bias_residual_layernorm(const float* partials, int splits, int64_t ro
                                    void* hidden, const void* gamma, const void* beta, void* normed, float eps,
                                    cudaStream_t stream);
 
+// b200_paged_decode, whose last wave of CTAs also pulls `prefetch_bytes` of
+// the next projection's weights into L2 (nullptr: none).
+int paged_decode_launch(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                        const int32_t* block_tables, int max_blocks_per_seq, const int32_t* context_lens, int batch,
+                        int nq, int nkv, int head_dim, int block_size, int64_t num_blocks, float scale, void* out,
+                        int64_t out_stride, void* workspace, int64_t workspace_bytes, int max_context,
+                        cudaStream_t stream, const void* prefetch, int64_t prefetch_bytes);
+
 }  // namespace b200

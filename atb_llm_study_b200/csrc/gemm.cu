@@ -73,6 +73,11 @@ struct Params {
   int64_t gN;
   int gF;          // feature tiles per group
   int64_t gRows;   // rows of the token operand (goff is clamped to it)
+  // Decode chains: bytes of the NEXT projection's weights this launch pulls
+  // into L2 from its tail (each CTA a share, after its last tile load), so HBM
+  // keeps streaming across the launch boundary.  pf_bytes % 16 == 0.
+  const uint8_t* pf;
+  int64_t pf_bytes;
 };
 
 // One output tile: its MMA tile coordinates, K range, the TMA row coordinates
@@ -349,6 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         first = false;
       }
+      if (!*abort_flag) prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -582,6 +588,8 @@ Params make_params(const b200::GemmPlan& g, int64_t M, int64_t N, int64_t K, voi
   p.gN = 0;
   p.gF = 0;
   p.gRows = 0;
+  p.pf = nullptr;
+  p.pf_bytes = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   p.err = b200::error_word(dev);
@@ -639,7 +647,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
 
 int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
                 int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
-                cudaStream_t st, int* splits_out) {
+                cudaStream_t st, int* splits_out, const void* prefetch, int64_t prefetch_bytes) {
   if (splits_out) *splits_out = 1;
   if (!A || !B || !Cp || M < 0 || N < 0 || K <= 0) return B200_ERROR_INVALID_PARAM;
   if (epi < B200_EPI_NONE || epi > B200_EPI_BIAS_RESIDUAL) return B200_ERROR_INVALID_PARAM;
@@ -662,7 +670,11 @@ int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp
     g.splits = 1;
     g.kb_per_split = g.kb_total;
   }
-  const Params p = make_params(g, M, N, K, Cp, ldc, bias, R, ldr, ws);
+  Params p = make_params(g, M, N, K, Cp, ldc, bias, R, ldr, ws);
+  if (prefetch && prefetch_bytes >= 16 && (reinterpret_cast<uintptr_t>(prefetch) & 15u) == 0) {
+    p.pf = static_cast<const uint8_t*>(prefetch);
+    p.pf_bytes = prefetch_bytes & ~int64_t(15);
+  }
   CUtensorMap ta, tb;
   const void* mA = g.swap ? B : A;  // operand on the 128-row MMA side
   const void* mB = g.swap ? A : B;

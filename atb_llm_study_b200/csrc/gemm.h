@@ -20,10 +20,13 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms);
 // splits_out is not null, the kernel only stores fp32 partial tiles
 // ws[split][M][N] and *splits_out returns the split count: the caller reduces
 // them (splitk_reduce, or a consumer kernel that fuses the reduction).
-// Otherwise the epilogue is applied and *splits_out = 1.
+// Otherwise the epilogue is applied and *splits_out = 1.  prefetch /
+// prefetch_bytes (optional, 16-byte aligned): the next projection's weights,
+// pulled into L2 from this launch's tail so HBM keeps streaming across the
+// launch boundary of a decode chain.
 int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
                 int64_t K, int epilogue, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
-                cudaStream_t stream, int* splits_out);
+                cudaStream_t stream, int* splits_out, const void* prefetch = nullptr, int64_t prefetch_bytes = 0);
 
 // C[M, N'] = epilogue(sum_s ws[s][M][N]).
 int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epilogue, const void* bias, const void* R,

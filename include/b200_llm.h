@@ -257,8 +257,9 @@ B200_API int b200_flash_prefill_ex(const void* q, int64_t q_stride, int64_t q_he
                                    int head_dim_qk, int head_dim_v, float scale, int causal, b200_stream_t stream);
 
 /* b200_flash_prefill_ex for callers that know the packed row count on the
- * host (total_tokens = cu_seqlens[num_seqs]).  128-wide heads run on the
- * tcgen05 tensor cores: 128 query rows per CTA, K/V tiles of 128 keys by TMA
+ * host (total_tokens = cu_seqlens[num_seqs]).  64- and 128-wide heads and
+ * latent attention's decompressed heads (192-wide query / key, 128-wide value)
+ * run on the tcgen05 tensor cores: 128 query rows per CTA, K/V tiles of 128 keys by TMA
  * (tile reads stop at total_tokens and at each operand's last head), scores
  * and the output accumulator in TMEM, the running max moved only when it grows
  * by more than 2^8 (exact rescaling, rarely needed).  Other head widths, or

@@ -1,8 +1,10 @@
-"""tcgen05 prefill attention (b200_flash_prefill_packed, 64- and 128-wide heads)
-against the numpy oracle and a torch fp32 reference.
+"""tcgen05 prefill attention (b200_flash_prefill_packed: 64- and 128-wide heads,
+and latent attention's decompressed 192-wide query/key with 128-wide value
+heads) against the numpy oracle and a torch fp32 reference.
 
 Cases: packed variable-length sequences around the 128-row tile edges, causal
-and bidirectional, 64- and 128-wide heads, GQA, the packed q|k|v layout of the
+and bidirectional, 16-, 32-, 64- and 128-wide heads (the narrow ones through
+zero-filled 64-wide tiles), GQA, the packed q|k|v layout of the
 engine; the Qwen3-8B
 prefill shape (8 x 2048, 32 query / 8 kv heads) against torch fp32 SDPA; and
 scores that keep growing along the keys so the running max moves (the rescale
@@ -33,7 +35,7 @@ def _run(d, W, nq, nkv, hd, cu, lens, causal, T, out=None):
     return out
 
 
-@pytest.mark.parametrize("causal,hd", [(1, 128), (0, 128), (1, 64), (0, 64)])
+@pytest.mark.parametrize("causal,hd", [(1, 128), (0, 128), (1, 64), (0, 64), (1, 32), (0, 32), (1, 16), (0, 16)])
 def test_varlen_tile_edges(causal, hd):
     rng = np.random.default_rng(7 + causal + hd)
     lens = [1, 63, 127, 128, 129, 300, 17, 1000]
@@ -114,4 +116,50 @@ def test_growing_scores_rescale_output_rows():
         rel = ((got - ref).abs().max() / ref.abs().max()).item()
         assert cos > 0.9999, (causal, cos)
         assert rel < 0.02, (causal, rel)
+    assert G.device_errors() == 0
+
+
+@pytest.mark.parametrize("causal", [1, 0])
+def test_mla_heads_192_qk_128_v(causal):
+    """DeepSeek-V2's decompressed heads in the engine's layout: q from the fused
+    projection (row stride 16 x 192 + 576, head stride 192), k packed [T, 16 x
+    192], v the value half of kv_b's output (row stride 16 x 256, head stride
+    256, offset 128); the YaRN softmax scale; tile edges around 128 rows."""
+    rng = np.random.default_rng(192 + causal)
+    lens = [1, 127, 128, 129, 640, 33]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T, nh = int(cu[-1]), 16
+    NQP, KVB = nh * 192 + 576, nh * 256
+    qf = rng.standard_normal((T, NQP)).astype(np.float32)
+    kf = rng.standard_normal((T, nh * 192)).astype(np.float32)
+    vf = rng.standard_normal((T, KVB)).astype(np.float32)
+    qd, kd, vd = G.bf16(qf), G.bf16(kf), G.bf16(vf)
+    scale = 0.1355
+    out = torch.empty(T, nh * 128, dtype=torch.bfloat16, device=G.DEV)
+    G.check(G.L().b200_flash_prefill_packed(qd.data_ptr(), NQP, 192, kd.data_ptr(), nh * 192, 192,
+                                            vd.data_ptr() + 128 * 2, KVB, 256, out.data_ptr(), nh * 128, 128,
+                                            G.i32(cu).data_ptr(), len(lens), max(lens), T, nh, nh, 192, 128, scale,
+                                            causal, G.stream()), "flash_prefill_packed 192/128")
+    got = G.host(out).reshape(T, nh, 128)
+    q = G.rounded(qf)[:, :nh * 192].reshape(T, nh, 192)
+    k = G.rounded(kf).reshape(T, nh, 192)
+    v = G.rounded(vf).reshape(T, nh, 256)[:, :, 128:]
+    ref = np.zeros((T, nh, 128), np.float32)
+    for a, b in zip(cu[:-1], cu[1:]):
+        s = np.einsum("qhd,khd->hqk", q[a:b], k[a:b]) * np.float32(scale)
+        if causal:
+            s = np.where(np.triu(np.ones((b - a, b - a), bool), 1)[None], -np.inf, s)
+        s = s - s.max(-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(-1, keepdims=True)
+        ref[a:b] = np.einsum("hqk,khd->qhd", p, v[a:b])
+    assert G.cosine(got, ref) > 0.9999
+    assert G.max_rel_err(got, ref) < 0.02
+    # the legacy-MMA kernel behind b200_flash_prefill_ex on the same inputs
+    old = torch.empty_like(out)
+    G.check(G.L().b200_flash_prefill_ex(qd.data_ptr(), NQP, 192, kd.data_ptr(), nh * 192, 192,
+                                        vd.data_ptr() + 128 * 2, KVB, 256, old.data_ptr(), nh * 128, 128,
+                                        G.i32(cu).data_ptr(), len(lens), max(lens), nh, nh, 192, 128, scale, causal,
+                                        G.stream()), "flash_prefill_ex 192/128")
+    assert G.cosine(got, G.host(old).reshape(T, nh, 128)) > 0.9999
     assert G.device_errors() == 0
