@@ -161,9 +161,14 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(const __grid_const
     bar_compute();
     if (*abort_flag) break;
     const uint8_t* sC = smem + s * kTileBytes;
-    float sc[2][4];
+    // Four independent accumulator chains over the 36 k-steps (k-step kk feeds
+    // chain kk % 4), summed at the end: one warp per scheduler issues these
+    // MMAs back to back, and a single chain would wait out every MMA's latency.
+    float sc4[4][2][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) sc4[a][j][0] = sc4[a][j][1] = sc4[a][j][2] = sc4[a][j][3] = 0.f;
 #pragma unroll 4
     for (int kk = 0; kk < kD / 16; ++kk) {
       const int mat = lane >> 3;
@@ -178,9 +183,14 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(const __grid_const
         const int c = kk * 2 + (mat & 1);
         ldmatrix_x4(kb4, smem_u32(sC + lat_off(r, c, kBoxBytes)));
       }
-      mma_bf16_16816(sc[0], qa, kb4);
-      mma_bf16_16816(sc[1], qa, kb4 + 2);
+      mma_bf16_16816(sc4[kk & 3][0], qa, kb4);
+      mma_bf16_16816(sc4[kk & 3][1], qa, kb4 + 2);
     }
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[j][e] = (sc4[0][j][e] + sc4[1][j][e]) + (sc4[2][j][e] + sc4[3][j][e]);
     // scale, mask, tile row max across the four warps
     const int kbase = t_begin + i * kTile + warp * 16;
     float mx[2] = {-INFINITY, -INFINITY};
