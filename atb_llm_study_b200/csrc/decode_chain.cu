@@ -97,38 +97,56 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+constexpr int kMaxSplits = 8;  // split-K slices an element-wise phase reads (the plans use at most 4 here)
 // generic-proxy writes of this thread -> visible to later TMA (async proxy) reads
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Poll the arrival counter until it reaches `target`; false on the time limit
-// or when another CTA aborted (the abort word is then set here too).
+// Poll the arrival counter (relaxed) until it reaches `target`, then one
+// acquire fence; false on the time limit or when another CTA aborted (the
+// abort word is then set here too).
 __device__ bool wait_count(unsigned* sync, unsigned target, unsigned* err) {
   const uint64_t t0 = global_timer_ns();
 #pragma unroll 1
   for (int i = 0;; ++i) {
-    if (ld_acquire_gpu(sync) >= target) return true;
-    if (ld_acquire_gpu(sync + 2)) return false;
-    if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
-      raise_error(err, DEV_ERR_WAIT_TIMEOUT);
-      atomicExch(sync + 2, 1u);
-      return false;
+    if (ld_relaxed_gpu(sync) >= target) {
+      fence_acquire_gpu();
+      return true;
+    }
+    if ((i & 63) == 63) {
+      if (ld_relaxed_gpu(sync + 2)) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        raise_error(err, DEV_ERR_WAIT_TIMEOUT);
+        atomicExch(sync + 2, 1u);
+        return false;
+      }
     }
   }
 }
 
-// Grid barrier `idx` for the 128 epilogue threads of every CTA.
+// Grid barrier `idx` for the 128 epilogue threads of every CTA: every thread
+// makes its stores visible at GPU scope (and to the async proxy of later TMA
+// reads), the CTA's threads meet, then one of them adds the CTA's arrival and
+// polls for everyone's.
 __device__ bool grid_barrier(const Params& p, int idx, int et) {
   fence_proxy_async_global();  // this thread's stores -> later TMA reads of other CTAs
   __threadfence();
   epi_sync();
   __shared__ int ok_s;
   if (et == 0) {
-    atomicAdd(p.sync, 1u);
+    red_release_add(p.sync, 1u);
     ok_s = wait_count(p.sync, (unsigned)(idx + 1) * gridDim.x, p.err) ? 1 : 0;
-    __threadfence();
   }
   epi_sync();
   return ok_s != 0;
@@ -150,11 +168,14 @@ __device__ void res_norm_phase(const Params& p, const Phase& g, const __nv_bfloa
       if (idx < nchunk) {
         __nv_bfloat16* hp = p.hidden + (int64_t)r * H + idx * 8;
         unpack8(__ldcg(reinterpret_cast<const uint4*>(hp)), v[c]);
-        for (int s = 0; s < g.splits; ++s) {
-          const float4* src = reinterpret_cast<const float4*>(g.ws + ((int64_t)s * p.T + r) * H + idx * 8);
-          const float4 a = __ldcg(src), b = __ldcg(src + 1);
-          v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
-          v[c][4] += b.x; v[c][5] += b.y; v[c][6] += b.z; v[c][7] += b.w;
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; ++s) {  // unrolled: every slice's loads in flight together
+          if (s < g.splits) {
+            const float4* src = reinterpret_cast<const float4*>(g.ws + ((int64_t)s * p.T + r) * H + idx * 8);
+            const float4 a = __ldcg(src), b = __ldcg(src + 1);
+            v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
+            v[c][4] += b.x; v[c][5] += b.y; v[c][6] += b.z; v[c][7] += b.w;
+          }
         }
         const uint4 hb = pack8(v[c]);
         __stcg(reinterpret_cast<uint4*>(hp), hb);
@@ -186,20 +207,40 @@ __device__ void res_norm_phase(const Params& p, const Phase& g, const __nv_bfloa
 // act[t, f/2 ..] = silu(gate) * up over the gate/up partials (rows interleaved).
 __device__ void swiglu_phase(const Params& p, const Phase& g, int et) {
   const int64_t N = g.N, n8 = N / 8, total = (int64_t)p.T * n8;
+  const int64_t stride = (int64_t)gridDim.x * kEpi;
+  constexpr int kItems = 4;  // items per thread per round, all their loads issued together
 #pragma unroll 1
-  for (int64_t it = (int64_t)blockIdx.x * kEpi + et; it < total; it += (int64_t)gridDim.x * kEpi) {
-    const int64_t t = it / n8, f0 = (it % n8) * 8;
-    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int s = 0; s < g.splits; ++s) {
-      const float4* src = reinterpret_cast<const float4*>(g.ws + ((int64_t)s * p.T + t) * N + f0);
-      const float4 a = __ldcg(src), b = __ldcg(src + 1);
-      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  for (int64_t it0 = (int64_t)blockIdx.x * kEpi + et; it0 < total; it0 += kItems * stride) {
+    float v[kItems][8];
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+      const int64_t it = it0 + j * stride;
+      if (it < total) {
+        const int64_t t = it / n8, f0 = (it % n8) * 8;
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; ++s) {
+          if (s < g.splits) {
+            const float4* src = reinterpret_cast<const float4*>(g.ws + ((int64_t)s * p.T + t) * N + f0);
+            const float4 a = __ldcg(src), b = __ldcg(src + 1);
+            v[j][0] += a.x; v[j][1] += a.y; v[j][2] += a.z; v[j][3] += a.w;
+            v[j][4] += b.x; v[j][5] += b.y; v[j][6] += b.z; v[j][7] += b.w;
+          }
+        }
+      }
     }
-    uint2 o;
-    o.x = pack2(silu_f(v[0]) * v[1], silu_f(v[2]) * v[3]);
-    o.y = pack2(silu_f(v[4]) * v[5], silu_f(v[6]) * v[7]);
-    __stcg(reinterpret_cast<uint2*>(p.act + t * p.I + f0 / 2), o);
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      const int64_t it = it0 + j * stride;
+      if (it < total) {
+        const int64_t t = it / n8, f0 = (it % n8) * 8;
+        uint2 o;
+        o.x = pack2(silu_f(v[j][0]) * v[j][1], silu_f(v[j][2]) * v[j][3]);
+        o.y = pack2(silu_f(v[j][4]) * v[j][5], silu_f(v[j][6]) * v[j][7]);
+        __stcg(reinterpret_cast<uint2*>(p.act + t * p.I + f0 / 2), o);
+      }
+    }
   }
 }
 
@@ -220,9 +261,12 @@ __device__ void qk_rope_phase(const Params& p, const Phase& g, int et) {
     const int h = (int)(it % nheads);
     float x[E] = {0, 0, 0, 0};
     const float* src = g.ws + t * QKV + (int64_t)h * HD + lane * E;
-    for (int s = 0; s < g.splits; ++s) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(src + (int64_t)s * p.T * QKV));
-      x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) {
+      if (s < g.splits) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(src + (int64_t)s * p.T * QKV));
+        x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
+      }
     }
     __nv_bfloat16* hp = p.qkv + t * QKV + (int64_t)h * HD + lane * E;
     const bool is_q = h < p.nq, is_k = !is_q && h < p.nq + p.nkv;
@@ -377,9 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_chain_kernel(const __grid_
           pdl_done = true;
         } else {
           const unsigned target = (unsigned)(gate[g] + 1) * gridDim.x;
-          if (ld_acquire_gpu(p.sync) < target) {
+          if (ld_relaxed_gpu(p.sync) < target) {
             if (!block) return false;
             if (!wait_count(p.sync, target, p.err)) return false;
+          } else {
+            fence_acquire_gpu();
           }
         }
         fence_proxy_async_global();
@@ -397,11 +443,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_chain_kernel(const __grid_
         }
         return true;
       };
+      // Entering a phase whose inputs are not ready yet: pull this CTA's next
+      // kPrefetchTiles weight tiles into L2 first, so HBM keeps streaming
+      // through the barrier beyond what the shared-memory ring holds.
+      constexpr int kPrefetchTiles = 24;
+      auto prefetch_ahead = [&](Cursor from, int kb) {
+        int n = 0;
+        while (n < kPrefetchTiles) {
+          for (; kb < from.kb1 && n < kPrefetchTiles; ++kb, ++n)
+            tma_prefetch_l2_2d(&maps.w[from.g], kb * BK, from.tm * BM);
+          if (!next_unit(p, from, false)) break;
+          kb = from.kb;
+        }
+      };
       Cursor c;
-      int stage = 0;
+      int stage = 0, last_g = -1;
       uint32_t phase = 0;
       bool ok = true;
       for (bool more = next_unit(p, c, true); more && ok; more = next_unit(p, c, false)) {
+        if (c.g != last_g) {
+          last_g = c.g;
+          if (!passed[c.g] && gate[c.g] >= 0) prefetch_ahead(c, c.kb);
+        }
         for (int kb = c.kb; kb < c.kb1 && ok; ++kb) {
           if (np == kStages - 1) ok = issue_tokens(true) && !*abort_flag;  // ring full of waiting k-blocks
           if (!ok) break;

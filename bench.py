@@ -39,7 +39,7 @@ METRIC = "Qwen3-8B bf16 decode & prefill tok/s at 1/2/4/8 B200; kernel % of roof
 PREFILL_SEQS, PREFILL_LEN, DECODE_BATCH, DECODE_CTX, BLOCK = 8, 2048, 64, 2048, 128
 # DRAM bytes (read + write) of one paged-decode launch at the bench shape, from
 # an ncu capture of `bench.py --profile-kernel decode_attention`.
-DECODE_ATTN_DRAM_BYTES = 537.974784e6 + 5.952256e6
+DECODE_ATTN_DRAM_BYTES = 537.43744e6 + 4.910592e6
 
 
 def peaks():
@@ -424,6 +424,98 @@ def kernel_roofline_prefill_gemm(L, torch, dev, reps=10):
     ms = e0.elapsed_time(e1) / reps
     del A, B, C
     return ms, 2.0 * M * N * K
+
+
+def kernel_roofline_decode_gemm(L, torch, dev, reps=20):
+    """The Qwen3-8B decode gate/up projection on its own: M 64 tokens, N 2 x
+    12288, K 4096, swapped split-K tcgen05 GEMM + the SwiGLU reduce, one of 36
+    weight copies per launch (every launch streams from HBM, 7.2 GB > L2):
+    algorithmic bytes = the 201 MB of weights."""
+    M, N, K, copies = DECODE_BATCH, 2 * 12288, 4096, 36
+    g = torch.Generator(device=dev).manual_seed(4)
+    W = torch.empty(copies, N, K, dtype=torch.bfloat16, device=dev).normal_(0, 0.02, generator=g)
+    A = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    C = torch.empty(M, N // 2, dtype=torch.bfloat16, device=dev)
+    wsb = L.b200_gemm_workspace_bytes(M, N, K, 3)
+    ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
+    i = [0]
+
+    def run(st):
+        check(L.b200_gemm_bf16(A.data_ptr(), K, W[i[0] % copies].data_ptr(), K, C.data_ptr(), N // 2, M, N, K, 3,
+                               None, None, 0, ws.data_ptr(), wsb, st.cuda_stream), "decode gemm")
+        i[0] += 1
+
+    ms = _time_launches(torch, dev, run, reps)
+    del W
+    return ms, N * K * 2
+
+
+def bandwidth_kernels(L, torch, dev, reps=20):
+    """Achieved HBM GB/s of the bandwidth-bound ops on their own, at the shapes
+    the benchmarked models run them, inputs larger than L2 where the shape has
+    that much data: bytes = every byte the op must read and write once."""
+    import numpy as np
+
+    hbm, _, _, src = peaks()
+    g = torch.Generator(device=dev).manual_seed(5)
+    out = {}
+
+    def line(name, shape, nbytes, run):
+        ms = _time_launches(torch, dev, run, reps)
+        out[name] = {"shape": shape, "ms": ms, "bytes": nbytes, "GBps": nbytes / (ms / 1e3) / 1e9,
+                     "frac": nbytes / (ms / 1e3) / 1e9 / hbm, "peak_source": f"{src} copy bandwidth"}
+
+    # RMSNorm at the Qwen3-8B prefill shape: read x, write out
+    T, H = PREFILL_SEQS * PREFILL_LEN, 4096
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    y = torch.empty_like(x)
+    line("rmsnorm", f"{T}x{H}", 2 * T * H * 2,
+         lambda s: check(L.b200_rmsnorm(x.data_ptr(), None, w.data_ptr(), y.data_ptr(), None, T, H, H, 1e-6,
+                                        s.cuda_stream), "rmsnorm"))
+    # QK RMSNorm + rope in place on q|k|v rows + the paged K/V write, Qwen3-8B prefill shape
+    nq, nkv, hd = 32, 8, 128
+    W = (nq + 2 * nkv) * hd
+    qkv = torch.randn(T, W, device=dev, generator=g).to(torch.bfloat16)
+    cos = torch.rand(T, hd, device=dev, generator=g)
+    sin = torch.rand(T, hd, device=dev, generator=g)
+    nblk = T // BLOCK
+    kc = torch.empty(nblk, nkv, BLOCK, hd, dtype=torch.bfloat16, device=dev)
+    vc = torch.empty_like(kc)
+    slots = torch.arange(T, dtype=torch.int64, device=dev)
+    nw = torch.ones(hd, dtype=torch.bfloat16, device=dev)
+    line("qk_norm_rope_kv_write", f"{T}x(32+8+8)x128",
+         T * W * 2 + T * (nq + nkv) * hd * 2 + T * 2 * nkv * hd * 2 + 2 * T * hd * 4,
+         lambda s: check(L.b200_qk_norm_rope(qkv.data_ptr(), T, nq, nkv, hd, W, nw.data_ptr(), nw.data_ptr(), 1e-6,
+                                             cos.data_ptr(), sin.data_ptr(), slots.data_ptr(), kc.data_ptr(),
+                                             vc.data_ptr(), nblk, BLOCK, s.cuda_stream), "qk_norm_rope"))
+    del qkv, kc, vc, cos, sin
+    # MoE combine at the Mixtral prefill shape (8 x 1024 tokens, top-2), with residual and the next RMSNorm
+    Tm, k = MX_PREFILL_SEQS * MX_PREFILL_LEN, 2
+    yp = torch.randn(Tm * k, H, device=dev, generator=g).to(torch.bfloat16)
+    pos = torch.randperm(Tm * k, device=dev, generator=g).to(torch.int32)
+    tw = torch.rand(Tm, k, device=dev, generator=g)
+    res = torch.randn(Tm, H, device=dev, generator=g).to(torch.bfloat16)
+    o = torch.empty_like(res)
+    nrm = torch.empty_like(res)
+    line("moe_combine_residual_rmsnorm", f"{Tm}x{k}x{H}", (Tm * k * H + 3 * Tm * H) * 2 + Tm * k * 8,
+         lambda s: check(L.b200_moe_combine(yp.data_ptr(), pos.data_ptr(), tw.data_ptr(), Tm, k, H, res.data_ptr(),
+                                            None, o.data_ptr(), w.data_ptr(), nrm.data_ptr(), 1e-6, s.cuda_stream),
+                         "moe_combine"))
+    del yp, res, o, nrm
+    # bilinear position-embedding interpolation of the Qwen3-VL vision tower (48x48 table -> 28x28 grid)
+    table = torch.randn(2304, 1024, device=dev, generator=g).to(torch.bfloat16)
+    pe = torch.empty(784, 1024, dtype=torch.bfloat16, device=dev)
+    grid = np.array([[1, 28, 28]], np.int64)
+    line("pos_embed_interp", "2304x1024 -> 784x1024", 784 * 1024 * 2 * (4 + 1),
+         lambda s: check(L.b200_pos_embed_interp(table.data_ptr(), 48, 1024, grid.ctypes.data, 1, 2, pe.data_ptr(),
+                                                 0, s.cuda_stream), "pos_embed_interp"))
+    # the Qwen3-8B decode gate/up projection (swapped split-K tcgen05 GEMM + SwiGLU reduce)
+    ms, nbytes = kernel_roofline_decode_gemm(L, torch, dev, reps)
+    out["decode_gate_up_gemm"] = {"shape": "M64 N24576 K4096 (+ SwiGLU reduce)", "ms": ms, "bytes": nbytes,
+                                  "GBps": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / hbm,
+                                  "peak_source": f"{src} copy bandwidth"}
+    return out
 
 
 QWEN3VL_2B = dict(
@@ -1265,6 +1357,7 @@ def run_b200(args, rank, world, local_rank):
         ds["kernel_roofline"] = kernel_line(kernel_roofline_mla_decode,
                                             "mla_decode_kernel (+combine), batch 32 x 16 heads, context 4096")
 
+    bw = bandwidth_kernels(L, torch, dev) if not args.no_bw_kernels else None
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
     pf_tok_s = world * T * steps / (pf_ms / 1e3)
     result = {
@@ -1332,6 +1425,8 @@ def run_b200(args, rank, world, local_rank):
         result["mixtral_8x7b"] = mx
     if ds:
         result["deepseek_v2_lite"] = ds
+    if bw:
+        result["bandwidth_kernels"] = bw
     if dist:
         # The sharded runs, compact, as the line's last key: speed-up / efficiency
         # against the one-GPU sections of this same run (tensor parallel: one
@@ -1432,8 +1527,9 @@ def main():
     ap.add_argument("--mixtral-only", action="store_true", help="only the Mixtral-8x7B section")
     ap.add_argument("--no-deepseek", action="store_true", help="skip the DeepSeek-V2-Lite section")
     ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
+    ap.add_argument("--no-bw-kernels", action="store_true", help="skip the bandwidth-bound kernel lines")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "prefill_attention", "mla_decode",
-                                                 "moe_gemm", "image_preprocess"],
+                                                 "moe_gemm", "image_preprocess", "decode_gemm", "bw_kernels"],
                     help="run only this kernel at its bench shape (3 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1447,9 +1543,13 @@ def main():
         from atb_llm_study_b200 import capi
 
         dev = torch.device("cuda", local_rank)
+        if args.profile_kernel == "bw_kernels":
+            print(json.dumps(bandwidth_kernels(capi.lib(), torch, dev, reps=3)))
+            return
         fn = {"decode_attention": kernel_roofline_decode_attention, "prefill_gemm": kernel_roofline_prefill_gemm,
               "prefill_attention": kernel_roofline_prefill_attention, "mla_decode": kernel_roofline_mla_decode,
-              "moe_gemm": kernel_roofline_moe_gemm, "image_preprocess": kernel_roofline_image_preprocess}[args.profile_kernel]
+              "moe_gemm": kernel_roofline_moe_gemm, "image_preprocess": kernel_roofline_image_preprocess,
+              "decode_gemm": kernel_roofline_decode_gemm}[args.profile_kernel]
         ms, work = fn(capi.lib(), torch, dev, reps=3)
         print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
         return
