@@ -7,7 +7,6 @@
 
 #include "engine/engine_kernels.h"
 #include "engine/weight_plan.h"
-#include "decode_chain.h"
 #include "fused.h"
 #include "gemm.h"
 #include "mla.h"
@@ -361,18 +360,6 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
   }
   attn_ws_bytes_ = mla ? 0 : b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
   if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
-  // Decode chain (dense GQA layers on one GPU, up to 64 decode rows): one
-  // persistent launch for the projections between two decode attentions.
-  chain_ws_bytes_ = 0;
-  if (!mla && cfg.experts == 0 && tp_ == 1 && ep_ == 1 && hd == 128 && EnvInt("B200_DECODE_CHAIN", 0) != 0) {
-    const int64_t tmax = std::min<int64_t>(opt.max_batch, 64);
-    chain_ws_bytes_ = b200::chain_workspace_bytes(tmax, H, I, cfg.heads, cfg.kv_heads, (int)hd);
-    if (chain_ws_bytes_ > 0) {
-      B200_RETURN_IF(A(chain_ws_, DType::FP32, {(chain_ws_bytes_ + 3) / 4}));
-      B200_RETURN_IF(A(chain_sync_, DType::INT32, {4}));
-      B200_RETURN_IF(FromCuda(cudaMemsetAsync(chain_sync_.data, 0, chain_sync_.bytes(), ctx_->GetStream())));
-    }
-  }
 
   pinned_bytes_ = (size_t)max_t_ * 8 * 5 + (size_t)(opt.max_batch + 1) * 16 + (size_t)H * 4 + 4096;
   B200_RETURN_IF(FromCuda(cudaMallocHost(&pinned_, pinned_bytes_)));
@@ -566,7 +553,6 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
   };
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
   const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;
-  if (decode && chain_ws_bytes_ > 0 && batch <= 64) return RunDecodeChain(batch);
   int s_qkv = 1, s_o = 1, s_gu = 1, s_d = 1;
   for (int l = 0; l < L; ++l) {
     if (l == 0) {
@@ -678,75 +664,6 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
       ++launches_;
       B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, next_norm, normed_.data, nullptr, T, H, H, cfg_.eps, st));
     }
-  }
-  return STATUS_OK;
-}
-
-// Decode step of a dense GQA model as alternating launches: one decode chain
-// (b200::chain_launch) for the projections between two attentions, one paged
-// decode attention per layer.  Chain 0 projects layer 0's q/k/v (the input
-// norm already ran); chain l+1 runs layer l's o projection + post norm, its
-// MLP + the next input norm, and layer l+1's q/k/v + rope + KV write; the last
-// chain ends with the residual stream in hidden_ for the head.
-Status DecoderModel::RunDecodeChain(int batch) {
-  cudaStream_t st = ctx_->GetStream();
-  const int64_t H = cfg_.hidden, hd = cfg_.head_dim, I = cfg_.intermediate, QKV = cfg_.qkv_dim();
-  const int64_t AO = (int64_t)cfg_.heads * hd;
-  const int nq = cfg_.heads, nkv = cfg_.kv_heads, L = cfg_.layers;
-  const float scale = 1.0f / std::sqrt((float)hd);
-  const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;
-  auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
-  b200::ChainArgs a{};
-  a.T = batch;
-  a.H = H;
-  a.I = I;
-  a.nq = nq;
-  a.nkv = nkv;
-  a.hd = (int)hd;
-  a.eps = cfg_.eps;
-  a.attn = attn_.data;
-  a.hidden = hidden_.data;
-  a.normed = normed_.data;
-  a.act = act_.data;
-  a.qkv = qkv_.data;
-  a.cos_tab = cos_.as<float>();
-  a.sin_tab = sin_.as<float>();
-  a.slots = slots_.as<int64_t>();
-  a.num_blocks = num_blocks_;
-  a.block_size = opt_.block_size;
-  a.workspace = chain_ws_.data;
-  a.workspace_bytes = chain_ws_bytes_;
-  a.sync = chain_sync_.as<unsigned>();
-  auto set_qkv = [&](int l) {  // layer l's q/k/v projection, QK norms and cache
-    a.w_qkv = bf(wqkv_, (int64_t)l * QKV * H);
-    a.q_norm = cfg_.qk_norm ? bf(qnorm_, (int64_t)l * hd) : nullptr;
-    a.k_norm = cfg_.qk_norm ? bf(knorm_, (int64_t)l * hd) : nullptr;
-    a.k_cache = bf(kv_, (int64_t)l * kv_layer);
-    a.v_cache = bf(kv_, (int64_t)l * kv_layer + kv_layer / 2);
-  };
-  ++launches_;
-  B200_RETURN_IF(b200_rmsnorm(hidden_.data, nullptr, bf(iln_, 0), normed_.data, nullptr, batch, H, H, cfg_.eps, st));
-  a.flags = b200::CHAIN_QKV;
-  set_qkv(0);
-  ++launches_;
-  B200_RETURN_IF(b200::chain_launch(a, st));
-  for (int l = 0; l < L; ++l) {
-    uint16_t* kc = bf(kv_, (int64_t)l * kv_layer);
-    launches_ += attn_ws_bytes_ > 0 ? 2 : 1;
-    B200_RETURN_IF(b200::paged_decode_launch(qkv_.data, QKV, kc, kc + kv_layer / 2, bt_batch_.as<int32_t>(),
-                                             max_blocks_, ctx_batch_.as<int32_t>(), batch, nq, nkv, (int)hd,
-                                             opt_.block_size, num_blocks_, scale, attn_.data, AO, attn_ws_.data,
-                                             attn_ws_bytes_, opt_.max_context, st, nullptr, 0));
-    const int64_t dl = dense_idx_[l];
-    a.flags = b200::CHAIN_O | b200::CHAIN_MLP | (l + 1 < L ? b200::CHAIN_QKV : 0);
-    a.w_o = bf(wo_, (int64_t)l * H * AO);
-    a.post_norm = bf(pln_, (int64_t)l * H);
-    a.w_gu = bf(wgu_, dl * 2 * I * H);
-    a.w_down = bf(wdown_, dl * H * I);
-    a.next_norm = l + 1 < L ? bf(iln_, (int64_t)(l + 1) * H) : nullptr;
-    if (l + 1 < L) set_qkv(l + 1);
-    ++launches_;
-    B200_RETURN_IF(b200::chain_launch(a, st));
   }
   return STATUS_OK;
 }

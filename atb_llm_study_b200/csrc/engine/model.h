@@ -144,9 +144,6 @@ class DecoderModel {
 
  private:
   Status RunLayers(int64_t T, bool decode, int batch);
-  Status RunDecodeChain(int batch);
-  DeviceTensor chain_ws_, chain_sync_;  // decode chain: fp32 partials, grid-barrier counters
-  int64_t chain_ws_bytes_ = 0;
   Status Head(int64_t rows, bool gather, int64_t* next_tokens, bool next_on_device, void* logits);
   Status DecodeDevice(int batch);
   void* LayerPtr(const DeviceTensor& t, int l, int64_t per_layer_elems) const {

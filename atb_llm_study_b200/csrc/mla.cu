@@ -53,10 +53,7 @@ __device__ __forceinline__ uint32_t lat_off(int r, int c, int box_bytes) {
 
 __device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-constexpr int kAhead = 3;  // tiles ahead of the one being loaded that are prefetched into L2
-
 struct MlaParams {
-  const __nv_bfloat16* cache;  // latent cache [num_blocks * block_size, 576] (L2 prefetch address)
   const __nv_bfloat16* q;  // [batch, q_stride]: head h at h*576 (512 latent + 64 rope)
   int64_t q_stride;
   const int32_t* block_tables;
@@ -144,22 +141,6 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(const __grid_const
         mbar_arrive_expect_tx(&full[s], kTileBytes);
 #pragma unroll 1
         for (int j = 0; j < kD / 64; ++j) tma_load_2d(dst + j * kBoxBytes, &tmC, &full[s], j * 64, row);
-        // The ring holds two tiles; pull the tile kAhead tiles further on into
-        // L2 now (its 64 rows are one contiguous run of the latent cache), so
-        // its TMA load later finds it there and more of the latent stream is
-        // in flight than shared memory can hold.
-        const int ia = i + kAhead;
-        if (ia < ntiles) {
-          const int tok_a = t_begin + ia * kTile;
-          int blk_a = p.block_tables[(int64_t)b * p.max_blocks + tok_a / p.block_size];
-          if (blk_a >= 0 && blk_a < p.num_blocks) {
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.cache) +
-                                 ((int64_t)blk_a * p.block_size + tok_a % p.block_size) * kD * 2;
-            prefetch_l2_bulk(src, 32768);
-            prefetch_l2_bulk(src + 32768, 32768);
-            prefetch_l2_bulk(src + 65536, kTile * kD * 2 - 65536);
-          }
-        }
       }
       __syncwarp();
     }
@@ -660,7 +641,6 @@ extern "C" int b200_mla_decode(const void* q, int64_t q_stride, const void* late
   CUtensorMap tm;
   if (!make_latent_tmap(&tm, latent_cache, num_blocks * block_size)) return B200_ERROR_UNSUPPORTED;
   MlaParams p;
-  p.cache = static_cast<const __nv_bfloat16*>(latent_cache);
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_stride = q_stride;
   p.block_tables = block_tables;

@@ -7,6 +7,8 @@
 // shuffles plus one shared-memory hop.
 #include <math.h>
 
+#include <algorithm>
+
 #include <cstdlib>
 
 #include "common.cuh"
@@ -645,7 +647,12 @@ int qk_norm_rope_launch(void* qkv, int64_t T, int nq, int nkv, int head_dim, int
   auto vc = static_cast<__nv_bfloat16*>(v_cache);
   unsigned* err = current_error_word();
   const int64_t p_ld = row_stride, p_slice = T * row_stride;  // partials [splits][T][row_stride]
-  dim3 g((unsigned)T, (unsigned)((nq + 2 * nkv + 3) / 4));  // one warp per (token, head)
+  // one CTA (4 warps) per token and head group: with few tokens (decode) every
+  // warp gets one head; with many (prefill) one CTA walks all heads of its
+  // token, so the grid stays a few CTAs per SM instead of ~12 per token
+  const int64_t nh4 = (nq + 2 * nkv + 3) / 4;
+  const int64_t gy = std::min<int64_t>(nh4, std::max<int64_t>(1, (8 * 148 + T - 1) / T));
+  dim3 g((unsigned)T, (unsigned)gy);
   switch (head_dim) {
     case 32: launch_kernel(qk_norm_rope_kernel<32>, g, 128, 0, stream, q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
     case 64: launch_kernel(qk_norm_rope_kernel<64>, g, 128, 0, stream, q, nq, nkv, row_stride, qn, kn, eps, cos_tab, sin_tab, slot_mapping, kc, vc, num_blocks, block_size, err, partials, splits, p_ld, p_slice); break;
