@@ -536,6 +536,66 @@ VL_VISION_FLOP = (24 * (2 * 784 * (3 * 1024 * 1024 + 1024 * 1024 + 2 * 4096 * 10
 VL_TEXT_FLOP = 28 * (2 * 256 * (2048 * (2048 + 2 * 1024) + 2048 * 2048 + 3 * 2048 * 6144) + 2 * 256 * 256 * 2048)
 
 
+def bench_qwen3vl_text_layer(L, torch, dev, reps=20, cpu=True):
+    """One Qwen3-VL-2B text decoder layer, S = 256 prefill (hidden 2048, 16 q / 8
+    kv heads x 128, SwiGLU 6144, QK-norm, interleaved mrope [24, 20, 20] theta
+    5e6 at t = h = w = arange(256), causal; weights N(0, 0.02), activations
+    N(0, 1)), through the layer-graph seam b200_text_decoder_layer, CUDA events;
+    the same layer on the host cores with the numpy fp32 oracle (median of 5
+    after a warm-up).  Algorithmic work: 26.04 GFLOP, 100.7 MB of weights."""
+    import numpy as np
+
+    import oracle
+
+    S, H, nq, nkv, hd, I = 256, 2048, 16, 8, 128, 6144
+    rng = np.random.default_rng(0)
+    f = np.float32
+    w = {"q_w": rng.standard_normal((nq * hd, H), f) * 0.02, "k_w": rng.standard_normal((nkv * hd, H), f) * 0.02,
+         "v_w": rng.standard_normal((nkv * hd, H), f) * 0.02, "o_w": rng.standard_normal((H, nq * hd), f) * 0.02,
+         "qn_w": np.ones(hd, f), "kn_w": np.ones(hd, f), "gate_w": rng.standard_normal((I, H), f) * 0.02,
+         "up_w": rng.standard_normal((I, H), f) * 0.02, "down_w": rng.standard_normal((H, I), f) * 0.02,
+         "iln_w": np.ones(H, f), "pln_w": np.ones(H, f)}
+    x = np.random.default_rng(1).standard_normal((S, H), f)
+    pos = np.arange(S)
+    cos, sin = oracle.mrope_cos_sin(np.stack([pos, pos, pos])[:, None, :], hd, 5e6, (24, 20, 20))
+    cos, sin = cos[0], sin[0]
+    order = ["q_w", "k_w", "v_w", "o_w", "qn_w", "kn_w", "gate_w", "up_w", "down_w", "iln_w", "pln_w"]
+    dw = {k: torch.from_numpy(w[k]).to(dev).to(torch.bfloat16) for k in order}
+    xd = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    cd, sd = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    out = torch.empty_like(xd)
+    seqlen = np.array([S], np.int32)
+    ptrs = [xd.data_ptr()] + [dw[k].data_ptr() for k in order] + [cd.data_ptr(), sd.data_ptr(), seqlen.ctypes.data]
+    pack = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    wsb = L.b200_text_decoder_layer_workspace_bytes(S, H, nq, nkv, hd, I)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+    def run(st):
+        check(L.b200_text_decoder_layer(ctypes.addressof(pack), len(ptrs), out.data_ptr(), S, 1, H, nq, nkv, hd, I,
+                                        1e-6, 1, 0, ws.data_ptr(), wsb, st.cuda_stream), "text_decoder_layer")
+
+    ms = _time_launches(torch, dev, run, reps)
+    flop, wbytes = 26.04e9, 100.7e6
+    hbm, tf_burst, _, src = peaks()
+    res = {"workload": "Qwen3-VL-2B text decoder layer, S=256 prefill (the reference's CPU golden layer config), "
+                       "through b200_text_decoder_layer",
+           "gpu_ms": ms, "tensor_frac": flop / (ms / 1e3) / 1e12 / tf_burst,
+           "hbm_frac": wbytes / (ms / 1e3) / 1e9 / hbm, "peak_source": f"{src} bf16 burst / copy"}
+    if cpu:
+        layer = lambda: oracle.decoder_layer(x, w, cos, sin, nq, nkv, hd, 1e-6, causal=True)
+        layer()
+        ts = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            layer()
+            ts.append(time.perf_counter() - t0)
+        cms = statistics.median(ts) * 1e3
+        res["cpu_baseline"] = {"value": cms, "unit": "ms/layer", "cores": blas_threads(), "kind": "port",
+                               "sample": "numpy fp32 oracle decoder layer, S=256, median of 5 after a warm-up"}
+        res["speedup_vs_cpu"] = cms / ms
+    return res
+
+
 def bench_qwen3vl(L, torch, dev, steps, warm, stream_of):
     """Qwen3-VL-2B embedding request: 448x448 image (grid 1x28x28 = 784 patches,
     196 merged tokens) inside a 256-token prompt; vision tower alone, then the
@@ -701,6 +761,117 @@ MX_PREFILL_FLOP = (2 * 32 * MX_ACTIVE_LAYER_PARAMS * MX_PREFILL_SEQS * MX_PREFIL
                    + 32 * MX_PREFILL_SEQS * 2 * MX_PREFILL_LEN ** 2 * 4096 + 2 * 32000 * 4096 * MX_PREFILL_SEQS)
 
 
+def _cpu_time(fn, budget_s=6.0, max_reps=3):
+    fn()  # warm
+    t0, reps = time.perf_counter(), 0
+    while True:
+        fn()
+        reps += 1
+        if time.perf_counter() - t0 > budget_s or reps >= max_reps:
+            break
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_moe_decode_baseline(model):
+    """The numpy fp32 oracle's decode step for the MoE sections, timed on the
+    host cores at the section's shape and scaled to the model's layers (an
+    extrapolation, like the headline's): one MoE decode layer (attention over
+    the batch's contexts + the routed experts it reaches) x layers + 1/8 of
+    lm_head x 8.  Bounded sample: the experts share a few distinct weight
+    arrays (each one is read from host DRAM all the same, being far larger than
+    the CPU caches), the caches and weights are random."""
+    import numpy as np
+
+    import oracle
+    from oracle import mla as omla
+    from oracle import moe as omoe
+
+    rng = np.random.default_rng(3)
+    f = np.float32
+
+    def nrm(*shape, s=0.02):
+        return rng.standard_normal(shape, f) * s
+
+    if model == "mixtral":
+        c = MIXTRAL_8X7B
+        H, nq, nkv, hd, I, E, K = 4096, 32, 8, 128, 14336, 8, 2
+        B, ctx, layers, V = MX_BATCH, MX_CTX, 32, 32000
+        w = {"q_w": nrm(nq * hd, H), "k_w": nrm(nkv * hd, H), "v_w": nrm(nkv * hd, H), "o_w": nrm(H, nq * hd)}
+        pool = [{"gate_w": nrm(I, H), "up_w": nrm(I, H), "down_w": nrm(H, I)} for _ in range(2)]
+        experts = [pool[e % 2] for e in range(E)]
+        router = nrm(E, H, s=1.0)
+        nblk = ctx // BLOCK + 1
+        kc = rng.standard_normal((B * nblk, nkv, BLOCK, hd), f)
+        vc = rng.standard_normal((B * nblk, nkv, BLOCK, hd), f)
+        tables = np.arange(B * nblk).reshape(B, nblk)
+        x = rng.standard_normal((B, H), f)
+        cos, sin = oracle.rope1d_cos_sin(np.full(B, ctx), hd, c["rope_theta"])
+        ones = np.ones(H, f)
+
+        def layer():
+            n = oracle.rms_norm(x, ones, 1e-5)
+            q = oracle.rope_half(oracle.linear(n, w["q_w"]).reshape(B, nq, hd), cos, sin)
+            k = oracle.rope_half(oracle.linear(n, w["k_w"]).reshape(B, nkv, hd), cos, sin)
+            v = oracle.linear(n, w["v_w"]).reshape(B, nkv, hd)
+            slots = oracle.slot_mapping(tables[0], np.array([ctx]), BLOCK)
+            oracle.kv_cache_write(kc, k[:1], slots)
+            oracle.kv_cache_write(vc, v[:1], slots)
+            a = oracle.paged_decode_attention(q, kc, vc, tables, np.full(B, ctx + 1))
+            h = x + oracle.linear(a.reshape(B, -1), w["o_w"])
+            y, _, _ = omoe.moe_ffn(oracle.rms_norm(h, ones, 1e-5), router, experts, K, renormalize=True)
+            return h + y
+
+        what = (f"numpy fp32 oracle: one Mixtral-8x7B decode layer (batch {B}, context {ctx}: GQA paged attention, "
+                f"8 experts top-2, 2 distinct expert weight arrays)")
+    else:
+        H, nh, R, dr, dn, dv, Im, E, K = 2048, 16, 512, 64, 128, 128, 1408, 64, 6
+        B, ctx, layers, V = DS_BATCH, DS_CTX, 27, 102400
+        rs = DEEPSEEK_V2_LITE["rope_scaling"]
+        cfg = {"heads": nh, "qk_nope": dn, "qk_rope": dr, "v_head": dv, "kv_lora": R, "eps": 1e-6, "theta": 10000.0,
+               "yarn": {"factor": rs["factor"], "orig_max_pos": rs["original_max_position_embeddings"],
+                        "beta_fast": rs["beta_fast"], "beta_slow": rs["beta_slow"], "mscale": rs["mscale"],
+                        "mscale_all_dim": rs["mscale_all_dim"]}}
+        w = {"q_w": nrm(nh * (dn + dr), H), "kva_w": nrm(R + dr, H), "kv_norm": np.ones(R, f),
+             "kvb_w": nrm(nh * (dn + dv), R), "o_w": nrm(H, nh * dv)}
+        qabs, oabs = omla.absorbed_weights(w, cfg)  # folded once, as the engine does at load
+        pool = [{"gate_w": nrm(Im, H), "up_w": nrm(Im, H), "down_w": nrm(H, Im)} for _ in range(8)]
+        experts = [pool[e % 8] for e in range(E)]
+        shared = {"gate_w": nrm(2 * Im, H), "up_w": nrm(2 * Im, H), "down_w": nrm(H, 2 * Im)}
+        router = nrm(E, H, s=1.0)
+        caches = [rng.standard_normal((ctx + 1, R + dr), f) for _ in range(B)]
+        x = rng.standard_normal((B, H), f)
+        cos, sin = omla.rope_cfg_tables(np.full(B, ctx), cfg)
+        ones = np.ones(H, f)
+        scale = omla.softmax_scale(cfg)
+
+        def layer():
+            n = oracle.rms_norm(x, ones, 1e-6)
+            q = oracle.linear(n, qabs).reshape(B, nh, R + dr)
+            q[:, :, R:] = omla.rope_deinterleave(q[:, :, R:], cos[:, None, :], sin[:, None, :])
+            kv_a = oracle.linear(n, w["kva_w"])
+            cnew = oracle.rms_norm(kv_a[:, :R], w["kv_norm"], 1e-6)
+            kpe = omla.rope_deinterleave(kv_a[:, R:], cos, sin)
+            for b in range(B):  # the cache write of this token
+                caches[b][ctx, :R], caches[b][ctx, R:] = cnew[b], kpe[b]
+            lat = omla.latent_decode(q.reshape(B, -1), caches, [ctx + 1] * B, nh, scale)
+            h = x + oracle.linear(lat, oabs)
+            y, _, _ = omoe.moe_ffn(oracle.rms_norm(h, ones, 1e-6), router, experts, K, renormalize=False,
+                                     shared=shared)
+            return h + y
+
+        what = (f"numpy fp32 oracle: one DeepSeek-V2-Lite MoE decode layer (batch {B}, context {ctx}: absorbed "
+                f"latent attention, 64 experts top-6 + 2 shared, 8 distinct expert weight arrays)")
+    lm = nrm(V // 8, H)
+    t_layer, reps = _cpu_time(layer)
+    t0 = time.perf_counter()
+    oracle.linear(x, lm)
+    t_head = (time.perf_counter() - t0) * 8
+    step = layers * t_layer + t_head
+    return {"value": B / step, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+            "sample": f"{what} timed x{reps} = {t_layer * 1e3:.1f} ms/layer, scaled to {layers} layers + lm_head "
+                      f"(extrapolated)"}
+
+
 def bench_mixtral(L, torch, dev, steps, warm, stream_of):
     """Mixtral-8x7B on one GPU (93 GB of bf16 weights): prefill 8 x 1024 per
     step; decode batch 32 at context 4096 (paged KV, block 128)."""
@@ -846,6 +1017,32 @@ def bench_deepseek(L, torch, dev, steps, warm, stream_of):
                                         nxt[2 * g:].data_ptr(), 1, None), "prefill ctx")
         torch.cuda.synchronize(dev)
         fill_s = time.perf_counter() - t0
+        # prefill throughput: 2 x 4096-token prompts per call (the fill's shape), CUDA events, after a warm-up call
+        pf_ids = torch.from_numpy(rng.integers(0, V, 2 * DS_CTX).astype(np.int64)).to(dev)
+        pf_next = torch.empty(2, dtype=torch.int64, device=dev)
+
+        def prefill_call(g):
+            sl = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, pf_ids.data_ptr(), 1, lens.ctypes.data, sl.ctypes.data, 2, None,
+                                        pf_next.data_ptr(), 1, None), "prefill")
+
+        check(L.b200_engine_reset(eng), "reset")
+        prefill_call(0)
+        torch.cuda.synchronize(dev)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(est)
+        for g in range(1, 4):
+            prefill_call(g)
+        p1.record(est)
+        torch.cuda.synchronize(dev)
+        pf_ms = p0.elapsed_time(p1) / 3
+        # refill the slots the timed calls reused, so every slot again holds a distinct 4096-token context
+        check(L.b200_engine_reset(eng), "reset")
+        for g in range(DS_BATCH // 2):
+            ids = torch.from_numpy(rng.integers(0, V, 2 * DS_CTX).astype(np.int64)).to(dev)
+            slots = np.array([2 * g, 2 * g + 1], np.int32)
+            check(L.b200_engine_prefill(eng, ids.data_ptr(), 1, lens.ctypes.data, slots.ctypes.data, 2, None,
+                                        nxt[2 * g:].data_ptr(), 1, None), "prefill ctx")
         slots_all = np.arange(DS_BATCH, dtype=np.int32)
         feed_host = rng.integers(0, V, (warm + steps + 1, DS_BATCH)).astype(np.int64)
         feed = torch.from_numpy(feed_host).to(dev)
@@ -889,10 +1086,36 @@ def bench_deepseek(L, torch, dev, steps, warm, stream_of):
             "decode_roofline": {"bound": "hbm", "bytes_per_step": nbytes, "achieved": nbytes / (dec_ms / 1e3) / 1e9,
                                 "peak": hbm, "unit": "GB/s", "frac": nbytes / (dec_ms / 1e3) / 1e9 / hbm,
                                 "peak_source": f"{src} copy"},
+            "prefill_tok_s": 2 * DS_CTX / (pf_ms / 1e3), "prefill_ms_per_step": pf_ms,
+            "prefill": "2 x 4096-token prompts per call",
             "prefill_fill_s": fill_s, "decode_launches_per_step": v.value,
         }
     finally:
         L.b200_engine_destroy(eng)
+
+
+def kernel_roofline_mla_prefill_attention(L, torch, dev, reps=10):
+    """Latent attention's prefill (decompressed heads: 192-wide query / key,
+    128-wide value, 16 heads) on the tcgen05 kernel at the DeepSeek-V2-Lite
+    prefill shape (2 causal sequences of 4096 tokens, the engine's operand
+    layouts): flops = 2 * 16 * sum(S^2 / 2) * (192 + 128)."""
+    S, nseq, nh = DS_CTX, 2, 16
+    T = S * nseq
+    NQP, KVB = nh * 192 + 576, nh * 256
+    g = torch.Generator(device=dev).manual_seed(6)
+    q = torch.randn(T, NQP, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, nh * 192, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, KVB, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(T, nh * 128, dtype=torch.bfloat16, device=dev)
+    cu = torch.tensor([0, S, 2 * S], dtype=torch.int32, device=dev)
+
+    def run(st):
+        check(L.b200_flash_prefill_packed(q.data_ptr(), NQP, 192, k.data_ptr(), nh * 192, 192, v.data_ptr() + 256,
+                                          KVB, 256, out.data_ptr(), nh * 128, 128, cu.data_ptr(), nseq, S, T, nh, nh,
+                                          192, 128, 0.1, 1, st.cuda_stream), "mla prefill attention")
+
+    ms = _time_launches(torch, dev, run, reps)
+    return ms, 2.0 * nh * nseq * (S * S / 2) * (192 + 128)
 
 
 def make_comm(L, dist, world, rank, dev, sym_bytes):
@@ -1339,10 +1562,20 @@ def run_b200(args, rank, world, local_rank):
                              MX_PREFILL_SEQS, MX_PREFILL_LEN, MX_BATCH, MX_CTX,
                              "one Mixtral-8x7B sharded over all ranks: every expert's width split, router replicated")
     vl = None if args.no_vl else bench_qwen3vl(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+    if vl:
+        vl["text_layer"] = bench_qwen3vl_text_layer(L, torch, dev,
+                                                    cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
     pp = None if args.no_vl else bench_preprocess(L, torch, dev, steps, warm,
                                                   cpu_baseline=rank == 0 and not args.no_cpu_baseline)
     mx = None if args.no_mixtral else bench_mixtral(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
     ds = None if args.no_deepseek else bench_deepseek(L, torch, dev, max(3, min(steps, 10)), warm, stream_of)
+    for sec, name in ((mx, "mixtral"), (ds, "deepseek")):
+        if sec and rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                sec["cpu_baseline"] = cpu_moe_decode_baseline(name)
+                sec["speedup_vs_cpu"] = sec["decode_tok_s"] / sec["cpu_baseline"]["value"]
+            except Exception as e:  # the baseline is a report, never a reason to lose the GPU line
+                sec["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
 
     def kernel_line(fn, name):
         ms, nbytes = fn(L, torch, dev)
@@ -1356,6 +1589,11 @@ def run_b200(args, rank, world, local_rank):
     if ds:
         ds["kernel_roofline"] = kernel_line(kernel_roofline_mla_decode,
                                             "mla_decode_kernel (+combine), batch 32 x 16 heads, context 4096")
+        fa_ms2, fa_fl2 = kernel_roofline_mla_prefill_attention(L, torch, dev)
+        ds["prefill_attention_roofline"] = {
+            "kernel": "flash_prefill_tc_kernel<192, 128> (tcgen05), causal 2x4096, 16 heads", "bound": "tensor",
+            "ms": fa_ms2, "achieved": fa_fl2 / (fa_ms2 / 1e3) / 1e12, "peak": tf_burst, "unit": "TFLOP/s",
+            "frac": fa_fl2 / (fa_ms2 / 1e3) / 1e12 / tf_burst, "peak_source": f"{src} bf16 burst"}
 
     bw = bandwidth_kernels(L, torch, dev) if not args.no_bw_kernels else None
     dec_tok_s = world * DECODE_BATCH * steps / (dec_ms / 1e3)
@@ -1529,7 +1767,8 @@ def main():
     ap.add_argument("--deepseek-only", action="store_true", help="only the DeepSeek-V2-Lite section")
     ap.add_argument("--no-bw-kernels", action="store_true", help="skip the bandwidth-bound kernel lines")
     ap.add_argument("--profile-kernel", choices=["decode_attention", "prefill_gemm", "prefill_attention", "mla_decode",
-                                                 "moe_gemm", "image_preprocess", "decode_gemm", "bw_kernels"],
+                                                 "moe_gemm", "image_preprocess", "decode_gemm", "bw_kernels",
+                                                 "mla_prefill_attention"],
                     help="run only this kernel at its bench shape (3 warm-up + 3 launches), for ncu")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1549,7 +1788,8 @@ def main():
         fn = {"decode_attention": kernel_roofline_decode_attention, "prefill_gemm": kernel_roofline_prefill_gemm,
               "prefill_attention": kernel_roofline_prefill_attention, "mla_decode": kernel_roofline_mla_decode,
               "moe_gemm": kernel_roofline_moe_gemm, "image_preprocess": kernel_roofline_image_preprocess,
-              "decode_gemm": kernel_roofline_decode_gemm}[args.profile_kernel]
+              "decode_gemm": kernel_roofline_decode_gemm,
+              "mla_prefill_attention": kernel_roofline_mla_prefill_attention}[args.profile_kernel]
         ms, work = fn(capi.lib(), torch, dev, reps=3)
         print(json.dumps({"kernel": args.profile_kernel, "ms": ms, "work_per_launch": work}))
         return
@@ -1573,7 +1813,11 @@ def main():
         fn = bench_qwen3vl if args.vl_only else bench_mixtral if args.mixtral_only else bench_deepseek
         res = fn(L, torch, dev, args.steps, args.warmup, stream_of)
         if args.vl_only:
+            res["text_layer"] = bench_qwen3vl_text_layer(L, torch, dev, cpu=not args.no_cpu_baseline)
             res["image_preprocess"] = bench_preprocess(L, torch, dev, args.steps, args.warmup)
+        elif not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_moe_decode_baseline("mixtral" if args.mixtral_only else "deepseek")
+            res["speedup_vs_cpu"] = res["decode_tok_s"] / res["cpu_baseline"]["value"]
         print(json.dumps(res), flush=True)
         return
     run_b200(args, rank, world, local_rank)
