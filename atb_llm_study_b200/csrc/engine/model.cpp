@@ -44,6 +44,9 @@ const int64_t kPrefetchBytes = [] {
   const char* v = std::getenv("B200_DECODE_PREFETCH_MB");
   return (v ? std::atoll(v) : 48ll) << 20;
 }();
+// Stream-K flags: one per 128-row weight tile of a decode gate/up projection
+// (2 x intermediate / 128 tiles; 1024 covers intermediate sizes up to 65536).
+constexpr int64_t kSkFlags = 1024;
 bool starts_with(const std::string& s, const std::string& p) { return s.compare(0, p.size(), p) == 0; }
 }  // namespace
 
@@ -358,6 +361,9 @@ Status DecoderModel::Init(const ModelConfig& whole, const EngineOptions& opt) {
     // split-K accumulator + tile counters start at zero; every GEMM leaves them zero
     B200_RETURN_IF(FromCuda(cudaMemsetAsync(gemm_ws_.data, 0, gemm_ws_.bytes(), ctx_->GetStream())));
   }
+  // stream-K tile flags of the decode gate/up projection: zero, and every launch leaves them zero
+  B200_RETURN_IF(A(sk_flags_, DType::INT32, {kSkFlags}));
+  B200_RETURN_IF(FromCuda(cudaMemsetAsync(sk_flags_.data, 0, sk_flags_.bytes(), ctx_->GetStream())));
   attn_ws_bytes_ = mla ? 0 : b200_paged_decode_workspace_bytes(opt.max_batch, cfg.heads, (int)hd, opt.max_context);
   if (attn_ws_bytes_ > 0) B200_RETURN_IF(A(attn_ws_, DType::FP32, {(attn_ws_bytes_ + 3) / 4}));
 
@@ -549,7 +555,8 @@ Status DecoderModel::RunLayers(int64_t T, bool decode, int batch) {
                   int epi, const void* R, int64_t ldr, int* splits, const void* pf = nullptr, int64_t pf_bytes = 0) {
     ++launches_;
     return b200::gemm_launch(A, lda, B, ldb, C, ldc, T, N, K, epi, nullptr, R, ldr, ws, gemm_ws_bytes_, st, splits,
-                             decode && kPrefetchBytes ? pf : nullptr, std::min<int64_t>(pf_bytes, kPrefetchBytes));
+                             decode && kPrefetchBytes ? pf : nullptr, std::min<int64_t>(pf_bytes, kPrefetchBytes),
+                             sk_flags_.as<int>(), (int)kSkFlags);
   };
   auto bf = [](const DeviceTensor& t, int64_t off) { return static_cast<uint16_t*>(t.data) + off; };
   const int64_t kv_layer = 2 * num_blocks_ * nkv * opt_.block_size * hd;

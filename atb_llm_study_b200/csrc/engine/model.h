@@ -217,7 +217,7 @@ class DecoderModel {
   DeviceTensor block_tables_, ctx_lens_;
   // activations / scratch
   DeviceTensor ids_, hidden_, normed_, qkv_, attn_, act_, cos_, sin_, pos_, slots_, cu_, last_idx_, last_hidden_,
-      logits_, next_, seq_slots_, ctx_batch_, bt_batch_, gemm_ws_, attn_ws_, inject_idx_, pooled_;
+      logits_, next_, seq_slots_, ctx_batch_, bt_batch_, gemm_ws_, attn_ws_, inject_idx_, pooled_, sk_flags_;
   int64_t gemm_ws_bytes_ = 0, attn_ws_bytes_ = 0;
   std::vector<int32_t> host_ctx_;
   // pinned staging for host <-> device copies

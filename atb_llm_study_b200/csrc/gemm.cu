@@ -19,6 +19,13 @@
 // in a workspace slice with plain coalesced stores, and the reduction (with
 // the epilogue) runs in the consumer — splitk_reduce for the C ABI call, or a
 // kernel that reads the result anyway (residual + RMSNorm, QK-norm + rope).
+// A swapped SwiGLU projection with enough k-blocks per SM (the decode
+// gate/up) runs "stream-K" instead: every CTA takes an equal, contiguous run
+// of the (tile, k-block) sequence, so a tile is cut at most once; the CTA
+// holding a tile's head stores its fp32 partial first thing and raises the
+// tile's flag, the CTA holding the tail finishes that tile last, adding the
+// head's partial (loaded while its own MMAs run) before the SwiGLU epilogue.
+// No partial stores for whole tiles and no separate reduce launch.
 //
 // No TMA multicast is used (the library also runs in multi-GPU jobs).
 #include <math.h>
@@ -78,6 +85,9 @@ struct Params {
   // keeps streaming across the launch boundary.  pf_bytes % 16 == 0.
   const uint8_t* pf;
   int64_t pf_bytes;
+  // Stream-K (swapped SwiGLU only): one flag per tile, zero between launches;
+  // ws then holds one 128 x BN fp32 partial per tile, [tile][token][row].
+  int* sk_flags;
 };
 
 // One output tile: its MMA tile coordinates, K range, the TMA row coordinates
@@ -86,12 +96,16 @@ struct Unit {
   int tm, tn, kb0, kb1;
   int a_row, b_row;
   int64_t row0, col0, row_lim, col_lim;
+  int piece;  // stream-K: kPieceWhole, kPieceHead or kPieceTail of tile tm
 };
+constexpr int kPieceWhole = 0, kPieceHead = 1, kPieceTail = 2;
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+// x * sigmoid(x) with the fast division intrinsic (the epilogue warps are few:
+// an IEEE division per element would dominate a decode gate/up epilogue).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // Epilogue on 8 consecutive features f0..f0+7 of token `tok` (non-SwiGLU kinds).
 template <int EPI>
@@ -153,10 +167,17 @@ __device__ __forceinline__ void emit_chunk(float v[32], int64_t row, int64_t col
       }
     }
   } else if (EPI == B200_EPI_SWIGLU) {
+    // Lanes 2j / 2j+1 hold the gate / up rows of feature j: the even lane
+    // finishes tokens 0..15 of the chunk, the odd lane tokens 16..31, one
+    // exchange per token pair (each lane sends what its partner lacks).
+    const bool odd = lane & 1;
+    const int64_t f = row >> 1;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      if (!(lane & 1) && row < p.rows && col0 + i < p.cols) p.C[(col0 + i) * p.ldc + row / 2] = f2bf(silu_f(v[i]) * up);
+    for (int i = 0; i < 16; ++i) {
+      const float other = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
+      const int tok = odd ? 16 + i : i;
+      const float o = odd ? silu_f(other) * v[16 + i] : silu_f(v[i]) * other;
+      if (row < p.rows && col0 + tok < p.cols) p.C[(col0 + tok) * p.ldc + f] = f2bf(o);
     }
   } else if (row < p.rows) {
 #pragma unroll
@@ -240,7 +261,55 @@ __device__ __forceinline__ Unit get_unit(int w, const Params& p, const int* gtab
   return u;
 }
 
-template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false>
+// Stream-K schedule of CTA c out of G over tiles_m tiles of kb_total k-blocks
+// (tiles_n == 1): the run [c*W/G, (c+1)*W/G) of the tile-major k-block
+// sequence, W = tiles_m * kb_total, at least kb_total long, so it cuts at
+// most the tile it starts in (a tail piece) and the tile it ends in (a head
+// piece).  Order: the head piece first, the whole tiles, the tail piece last.
+struct SkRun {
+  int s, e, t0, t1, whole0, whole_n;
+  bool head, tail;
+};
+
+__device__ __forceinline__ SkRun sk_run(const Params& p, int c, int G) {
+  SkRun r;
+  const int64_t W = (int64_t)p.tiles_m * p.kb_total;
+  r.s = (int)(W * c / G);
+  r.e = (int)(W * (c + 1) / G);
+  r.t0 = r.s / p.kb_total;
+  r.t1 = (r.e - 1) / p.kb_total;
+  r.tail = r.s % p.kb_total != 0;
+  r.head = r.e % p.kb_total != 0;
+  r.whole0 = r.tail ? r.t0 + 1 : r.t0;
+  r.whole_n = (r.head ? r.t1 - 1 : r.t1) - r.whole0 + 1;
+  return r;
+}
+
+__device__ __forceinline__ int sk_units(const SkRun& r) { return (int)r.head + r.whole_n + (int)r.tail; }
+
+template <int BN>
+__device__ __forceinline__ Unit sk_unit(int i, const SkRun& r, const Params& p) {
+  int t;
+  if (r.head && i == 0) t = r.t1;
+  else if (i - (int)r.head < r.whole_n) t = r.whole0 + i - (int)r.head;
+  else t = r.t0;
+  Unit u;
+  u.tm = t;
+  u.tn = 0;
+  const int base = t * p.kb_total;
+  u.kb0 = max(r.s, base) - base;
+  u.kb1 = min(r.e, base + p.kb_total) - base;
+  u.piece = u.kb0 > 0 ? kPieceTail : (u.kb1 < p.kb_total ? kPieceHead : kPieceWhole);
+  u.a_row = t * BM;
+  u.b_row = 0;
+  u.row0 = (int64_t)t * BM;
+  u.col0 = 0;
+  u.row_lim = p.rows;
+  u.col_lim = p.cols;
+  return u;
+}
+
+template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false, bool SK = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const Params p) {
@@ -253,7 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* skbar = tempty + 2;  // stream-K, one-shot: [0] head partial stored (128), [1] tail flag seen (1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(skbar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   int* gtab = reinterpret_cast<int*>(smem + C::STAGES * C::STAGE_BYTES + 256);  // grouped launches only
@@ -261,6 +331,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int units = p.tiles_m * p.tiles_n * p.splits;
   pdl_trigger();
+  // unit sequence of this CTA: w = w0, w0 + wstep, ... < wend (stream-K: its own run)
+  SkRun skr{};
+  if (SK) {
+    skr = sk_run(p, blockIdx.x, gridDim.x);
+    units = sk_units(skr);
+  }
+  const int w0 = SK ? 0 : blockIdx.x, wstep = SK ? 1 : gridDim.x;
+  auto unit_at = [&](int w, const int* gt) { return SK ? sk_unit<BN>(w, skr, p) : get_unit<BN, SWAP, GROUPED>(w, p, gt); };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -271,6 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
     }
+    mbar_init(&skbar[0], 128);
+    mbar_init(&skbar[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -317,25 +397,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // previous kernel on the stream, so the weight stream starts while that
       // kernel drains.  Activation tiles are only loaded after the wait.
       // (Grouped launches already waited: their tiles depend on the offsets.)
+      // The first STAGES k-blocks of the CTA's unit sequence (across unit
+      // boundaries: a stream-K head piece may be short) are preloaded.
       int pre = 0;
-      if (!GROUPED && (int)blockIdx.x < units) {
-        const Unit u0 = get_unit<BN, SWAP, GROUPED>(blockIdx.x, p, gtab);
-        pre = min(C::STAGES, u0.kb1 - u0.kb0);
-        for (int i = 0; i < pre; ++i) {
-          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          if (SWAP) tma_load_2d(sA + i * C::A_BYTES, &tmA, &full[i], (u0.kb0 + i) * BK, u0.a_row);
-          else tma_load_2d(sB + i * C::B_BYTES, &tmB, &full[i], (u0.kb0 + i) * BK, u0.b_row);
+      if (!GROUPED) {
+        for (int w = w0; w < units && pre < C::STAGES; w += wstep) {
+          const Unit u0 = unit_at(w, gtab);
+          for (int kb = u0.kb0; kb < u0.kb1 && pre < C::STAGES; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+            if (SWAP) tma_load_2d(sA + pre * C::A_BYTES, &tmA, &full[pre], kb * BK, u0.a_row);
+            else tma_load_2d(sB + pre * C::B_BYTES, &tmB, &full[pre], kb * BK, u0.b_row);
+          }
         }
       }
       pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
-      bool first = true;
-      for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x) {
-        const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
-          if (first && kb - u.kb0 < pre) {
-            // stage == kb - kb0 already expects both halves; add the activation half
+      int issued = 0;  // k-blocks of the sequence so far
+      for (int w = w0; w < units && !*abort_flag; w += wstep) {
+        const Unit u = unit_at(w, gtab);
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++issued) {
+          if (issued < pre) {
+            // stage == issued already expects both halves; add the activation half
             if (SWAP) tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, u.b_row);
             else tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, u.a_row);
           } else {
@@ -352,7 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
-        first = false;
       }
       if (!*abort_flag) prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
     }
@@ -363,8 +445,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
-        const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
+      for (int w = w0; w < units && !*abort_flag; w += wstep, ++local) {
+        const Unit u = unit_at(w, gtab);
         const int kb0 = u.kb0, kb1 = u.kb1;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -407,11 +489,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int rit = q * 32 + lane;
     int local = 0;
-    for (int w = blockIdx.x; w < units && !*abort_flag; w += gridDim.x, ++local) {
-      const Unit u = get_unit<BN, SWAP, GROUPED>(w, p, gtab);
+    for (int w = w0; w < units && !*abort_flag; w += wstep, ++local) {
+      const Unit u = unit_at(w, gtab);
       const int split = w / (p.tiles_m * p.tiles_n);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      // stream-K tail piece: the head's partial of this tile, loaded before
+      // this tile's own accumulator is ready
+      float head[SK ? BN : 1];
+      if (SK && u.piece == kPieceTail) {
+        if (warp == 2 && lane == 0) {
+          volatile int* f = p.sk_flags + u.tm;
+          const uint64_t t0 = global_timer_ns();
+          bool ok = true;
+          while (*f == 0) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              raise_error(p.err, DEV_ERR_WAIT_TIMEOUT);
+              ok = false;
+              break;
+            }
+          }
+          __threadfence();
+          if (ok) *f = 0;  // flags are zero between launches
+          mbar_arrive(&skbar[1]);
+        }
+        if (!mbar_wait(&skbar[1], 0, p.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        const float* hp = p.ws + (int64_t)u.tm * BM * BN + rit;
+#pragma unroll
+        for (int c = 0; c < BN; ++c) head[c] = __ldcg(hp + c * BM);
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) {
         *abort_flag = 1;
         break;
@@ -430,6 +539,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         const int64_t col0 = u.col0 + ch * 32;
+        if (SK && u.piece == kPieceHead) {
+          // this tile's head: fp32 partial [token][row] (coalesced over rows)
+          float* hp = p.ws + (int64_t)u.tm * BM * BN + (int64_t)ch * 32 * BM + rit;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) __stcg(hp + i * BM, v[i]);
+          continue;
+        }
+        if (SK && u.piece == kPieceTail) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += ch == 0 ? head[i] : head[(BN > 32 ? 32 : 0) + i];  // static indices
+        }
         if (PARTIAL) {
           // this K slice's partial tile -> ws[split][token][feature] (plain coalesced stores)
           if (row < p.rows) {
@@ -451,6 +571,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (SK && u.piece == kPieceHead) {
+        __threadfence();  // every thread's partial stores before the flag
+        mbar_arrive(&skbar[0]);
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait(&skbar[0], 0, p.err)) atomicExch(p.sk_flags + u.tm, 1);
+          else *abort_flag = 1;
+        }
+      }
     }
   }
 
@@ -505,9 +633,9 @@ int num_sms() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
-template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false>
+template <int BN, int EPI, bool SWAP, bool PARTIAL, bool GROUPED = false, bool SK = false>
 int launch_t(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int grid, cudaStream_t st) {
-  auto k = gemm_tcgen05_kernel<BN, EPI, SWAP, PARTIAL, GROUPED>;
+  auto k = gemm_tcgen05_kernel<BN, EPI, SWAP, PARTIAL, GROUPED, SK>;
   constexpr int smem = GROUPED ? Cfg<BN>::SMEM_GROUPED : Cfg<BN>::SMEM;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -590,6 +718,7 @@ Params make_params(const b200::GemmPlan& g, int64_t M, int64_t N, int64_t K, voi
   p.gRows = 0;
   p.pf = nullptr;
   p.pf_bytes = 0;
+  p.sk_flags = nullptr;
   int dev = 0;
   cudaGetDevice(&dev);
   p.err = b200::error_word(dev);
@@ -647,7 +776,8 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms) {
 
 int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, int64_t M, int64_t N,
                 int64_t K, int epi, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
-                cudaStream_t st, int* splits_out, const void* prefetch, int64_t prefetch_bytes) {
+                cudaStream_t st, int* splits_out, const void* prefetch, int64_t prefetch_bytes, int* sk_flags,
+                int sk_flag_count) {
   if (splits_out) *splits_out = 1;
   if (!A || !B || !Cp || M < 0 || N < 0 || K <= 0) return B200_ERROR_INVALID_PARAM;
   if (epi < B200_EPI_NONE || epi > B200_EPI_BIAS_RESIDUAL) return B200_ERROR_INVALID_PARAM;
@@ -681,10 +811,31 @@ int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp
   const int64_t ldmA = g.swap ? ldb : lda, ldmB = g.swap ? lda : ldb;
   if (!make_tmap(&ta, mA, p.rows, K, ldmA, BM) || !make_tmap(&tb, mB, p.cols, K, ldmB, g.bn))
     return B200_ERROR_UNSUPPORTED;
+  // Stream-K for a swapped SwiGLU projection over at least one whole tile of
+  // k-blocks per SM (the decode gate/up): even runs, no reduce launch.
+  const bool sk = sk_flags && g.swap && g.bn == 64 && epi == B200_EPI_SWIGLU && g.tiles_n == 1 &&
+                  g.tiles_m >= sms && g.tiles_m <= sk_flag_count && (g.tiles_m % sms) != 0 && ws &&
+                  (reinterpret_cast<uintptr_t>(sk_flags) & 3u) == 0 &&
+                  ws_bytes >= (int64_t)g.tiles_m * BM * 64 * (int64_t)sizeof(float);
+  if (sk) {
+    g.splits = 1;
+    g.kb_per_split = g.kb_total;
+    p = make_params(g, M, N, K, Cp, ldc, bias, R, ldr, ws);
+    p.ws = static_cast<float*>(ws);
+    p.sk_flags = sk_flags;
+    p.pf = prefetch && prefetch_bytes >= 16 && (reinterpret_cast<uintptr_t>(prefetch) & 15u) == 0
+               ? static_cast<const uint8_t*>(prefetch) : nullptr;
+    p.pf_bytes = p.pf ? (prefetch_bytes & ~int64_t(15)) : 0;
+  }
   const int units = g.tiles_m * g.tiles_n * g.splits;
-  const int grid = std::min(units, sms);
+  const int grid = sk ? sms : std::min(units, sms);
   const bool partial = g.splits > 1;
   int rc;
+  if (sk) {
+    rc = launch_t<64, B200_EPI_SWIGLU, true, false, false, true>(ta, tb, p, grid, st);
+    if (rc == B200_OK && splits_out) *splits_out = 1;
+    return rc;
+  }
   if (g.bn == 256) {
     rc = partial ? launch_epi<256, false, true>(epi, ta, tb, p, grid, st) : launch_epi<256, false, false>(epi, ta, tb, p, grid, st);
   } else if (g.bn == 128) {

@@ -23,10 +23,15 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int epilogue, int sms);
 // Otherwise the epilogue is applied and *splits_out = 1.  prefetch /
 // prefetch_bytes (optional, 16-byte aligned): the next projection's weights,
 // pulled into L2 from this launch's tail so HBM keeps streaming across the
-// launch boundary of a decode chain.
+// launch boundary of a decode chain.  sk_flags (optional): sk_flag_count
+// ints, zero, which every launch leaves zero; with them a swapped SwiGLU
+// projection of at least as many 128-row weight tiles as SMs runs stream-K
+// (ws then holds the cut tiles' fp32 partials) and writes its final output
+// (*splits_out = 1).
 int gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
                 int64_t K, int epilogue, const void* bias, const void* R, int64_t ldr, void* ws, int64_t ws_bytes,
-                cudaStream_t stream, int* splits_out, const void* prefetch = nullptr, int64_t prefetch_bytes = 0);
+                cudaStream_t stream, int* splits_out, const void* prefetch = nullptr, int64_t prefetch_bytes = 0,
+                int* sk_flags = nullptr, int sk_flag_count = 0);
 
 // C[M, N'] = epilogue(sum_s ws[s][M][N]).
 int splitk_reduce(const float* ws, int splits, int64_t M, int64_t N, int epilogue, const void* bias, const void* R,

@@ -2,10 +2,11 @@
 several packed sequences into the paged KV cache, then greedy decode steps
 (eager first, CUDA-graph replays after), against the numpy whole-model oracle.
 
-Two configurations: "narrow" (every projection runs unsplit) and "wide"
+Three configurations: "narrow" (every projection runs unsplit), "wide"
 (decode-sized projections split K, so the fused consumers — QK-norm/rope over
 split-K partials, residual + RMSNorm over split-K partials, SwiGLU reduce —
-are on the path).
+are on the path) and "wide-mlp" (150 gate/up weight tiles: the decode gate/up
+runs stream-K, cut tiles finished from their head's partial).
 
 Bar: cosine >= 0.999 of every last-token logit row; the greedy token must
 match the oracle's wherever the oracle's top-2 margin exceeds the bf16 noise.
@@ -37,6 +38,9 @@ NARROW = dict(model_type="qwen3", hidden_size=512, num_hidden_layers=3, num_atte
               tie_word_embeddings=False)
 WIDE = dict(NARROW, hidden_size=2048, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
             intermediate_size=4096)
+# 2 x 9600 / 128 = 150 weight tiles >= 148 SMs: the decode gate/up runs stream-K, 8 k-blocks a tile, so
+# nearly every SM's run cuts a tile (head / tail pieces, flags reset by every launch: 4 decode steps)
+WIDE_MLP = dict(NARROW, num_hidden_layers=2, intermediate_size=9600)
 
 
 def make_weights(C, seed=0):
@@ -99,7 +103,8 @@ def check_rows(C, logits, seqs, w):
             assert int(np.argmax(got)) == int(np.argmax(ref)), i
 
 
-@pytest.mark.parametrize("C,block", [(NARROW, 128), (NARROW, 64), (WIDE, 128)], ids=["narrow-128", "narrow-64", "wide"])
+@pytest.mark.parametrize("C,block", [(NARROW, 128), (NARROW, 64), (WIDE, 128), (WIDE_MLP, 128)],
+                         ids=["narrow-128", "narrow-64", "wide", "wide-mlp-stream-k"])
 def test_engine_prefill_then_decode(C, block):
     w = make_weights(C)
     eng = create_engine(C, w, block=block)
