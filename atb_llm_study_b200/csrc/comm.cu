@@ -142,13 +142,20 @@ __global__ void __launch_bounds__(kArThreads) allreduce_rmsnorm_kernel(Peers pp,
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
       if (idx < nch) {
-        for (int r = 0; r < pp.world; ++r) {
-          const uint4* src = reinterpret_cast<const uint4*>(pp.base[r] + buf_off) + t * nch + idx;
-          float a[8];
-          unpack8(__ldcg(src), a);
+        // every rank's partial requested before the first add (rank order kept):
+        // one NVLink round trip, not one per rank
+        uint4 part[kMaxRanks];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[c][i] += a[i];
-        }
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < pp.world) part[r] = __ldcg(reinterpret_cast<const uint4*>(pp.base[r] + buf_off) + t * nch + idx);
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < pp.world) {
+            float a[8];
+            unpack8(part[r], a);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[c][i] += a[i];
+          }
         float res[8];
         unpack8(*reinterpret_cast<const uint4*>(hidden + t * H + idx * 8), res);
 #pragma unroll
@@ -252,8 +259,14 @@ __global__ void gather_argmax_kernel(Peers pp, int64_t rows, int64_t* out, uint6
   for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
     float bv = -INFINITY;
     int32_t bi = INT32_MAX;
-    for (int k = 0; k < pp.world; ++k) {
-      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(pp.base[k] + kFlagBytes + r * 8));
+    uint2 pr[kMaxRanks];  // every rank's pair requested before the comparisons
+#pragma unroll
+    for (int k = 0; k < kMaxRanks; ++k)
+      if (k < pp.world) pr[k] = __ldcg(reinterpret_cast<const uint2*>(pp.base[k] + kFlagBytes + r * 8));
+#pragma unroll
+    for (int k = 0; k < kMaxRanks; ++k) {
+      if (k >= pp.world) break;
+      const uint2 u = pr[k];
       const float v = __uint_as_float(u.x);
       const int32_t i = (int32_t)u.y;
       if (v > bv || (v == bv && i < bi)) {

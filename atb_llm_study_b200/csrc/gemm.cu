@@ -662,11 +662,22 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   if (gid >= tokens * nv) return;
   const int64_t tok = gid / nv, f0 = (gid % nv) * 8;
   float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int s = 0; s < splits; ++s) {
-    const float4* src = reinterpret_cast<const float4*>(ws + ((int64_t)s * tokens + tok) * feats + f0);
-    const float4 a = src[0], b = src[1];
-    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  constexpr int kBatch = 8;  // the loads of up to 8 splits in flight before they are summed (split order kept)
+  for (int s0 = 0; s0 < splits; s0 += kBatch) {
+    float4 a[kBatch][2];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (s0 + i < splits) {
+        const float4* src = reinterpret_cast<const float4*>(ws + ((int64_t)(s0 + i) * tokens + tok) * feats + f0);
+        a[i][0] = src[0];
+        a[i][1] = src[1];
+      }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (s0 + i < splits) {
+        v[0] += a[i][0].x; v[1] += a[i][0].y; v[2] += a[i][0].z; v[3] += a[i][0].w;
+        v[4] += a[i][1].x; v[5] += a[i][1].y; v[6] += a[i][1].z; v[7] += a[i][1].w;
+      }
   }
   if (EPI == B200_EPI_SWIGLU) {
     uint2 o;

@@ -84,6 +84,29 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
 // h = hidden + sum_s partials[s][row] (a split-K projection finished here),
 // hidden = bf16(h), out = rmsnorm(bf16(h)) * w.
 constexpr int kRowThreads = 512;
+constexpr int kBatchSplits = 8;  // split-K partial loads issued together before they are summed
+
+// v[0..7] += sum over s < splits of the 8 fp32 at p + s * slice (in split
+// order): the loads of up to kBatchSplits slices are all in flight before the
+// first add, so the L2 latency is paid once, not once per split.
+__device__ __forceinline__ void add_split_partials8(float v[8], const float* p, int64_t slice, int splits) {
+  for (int s0 = 0; s0 < splits; s0 += kBatchSplits) {
+    float4 a[kBatchSplits][2];
+#pragma unroll
+    for (int i = 0; i < kBatchSplits; ++i)
+      if (s0 + i < splits) {
+        const float4* src = reinterpret_cast<const float4*>(p + (int64_t)(s0 + i) * slice);
+        a[i][0] = src[0];
+        a[i][1] = src[1];
+      }
+#pragma unroll
+    for (int i = 0; i < kBatchSplits; ++i)
+      if (s0 + i < splits) {
+        v[0] += a[i][0].x; v[1] += a[i][0].y; v[2] += a[i][0].z; v[3] += a[i][0].w;
+        v[4] += a[i][1].x; v[5] += a[i][1].y; v[6] += a[i][1].z; v[7] += a[i][1].w;
+      }
+  }
+}
 
 template <int CH>
 __global__ void __launch_bounds__(kRowThreads) splitk_residual_rmsnorm_kernel(const float* __restrict__ partials,
@@ -105,12 +128,7 @@ __global__ void __launch_bounds__(kRowThreads) splitk_residual_rmsnorm_kernel(co
     const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
     if (idx < nchunk) {
       unpack8(*reinterpret_cast<const uint4*>(hidden + row * dim + idx * 8), v[c]);
-      for (int s = 0; s < splits; ++s) {
-        const float4* src = reinterpret_cast<const float4*>(partials + ((int64_t)s * rows + row) * dim + idx * 8);
-        const float4 a = src[0], b = src[1];
-        v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
-        v[c][4] += b.x; v[c][5] += b.y; v[c][6] += b.z; v[c][7] += b.w;
-      }
+      add_split_partials8(v[c], partials + row * dim + idx * 8, rows * dim, splits);
       const uint4 hb = pack8(v[c]);
       *reinterpret_cast<uint4*>(hidden + row * dim + idx * 8) = hb;
       unpack8(hb, v[c]);  // normalise the stored (bf16) residual stream
@@ -118,13 +136,19 @@ __global__ void __launch_bounds__(kRowThreads) splitk_residual_rmsnorm_kernel(co
       for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
     }
   }
+  uint4 wv[CH];  // the norm weight, loaded while the row sum is reduced
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
+    if (idx < nchunk) wv[c] = *reinterpret_cast<const uint4*>(w + idx * 8);
+  }
   const float inv = rsqrtf(block_sum<kNormThreads>(ss, red) / (float)dim + eps);
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int64_t idx = threadIdx.x + (int64_t)c * kNormThreads;
     if (idx < nchunk) {
       float g[8], o[8];
-      unpack8(*reinterpret_cast<const uint4*>(w + idx * 8), g);
+      unpack8(wv[c], g);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = v[c][i] * inv * g[i];
       *reinterpret_cast<uint4*>(out + row * dim + idx * 8) = pack8(o);
@@ -205,12 +229,7 @@ __global__ void __launch_bounds__(kNormThreads) splitk_bias_residual_layernorm_k
     if (idx < nchunk) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
-      for (int sp = 0; sp < splits; ++sp) {
-        const float4* src = reinterpret_cast<const float4*>(partials + ((int64_t)sp * rows + row) * dim + idx * 8);
-        const float4 a = src[0], q = src[1];
-        v[c][0] += a.x; v[c][1] += a.y; v[c][2] += a.z; v[c][3] += a.w;
-        v[c][4] += q.x; v[c][5] += q.y; v[c][6] += q.z; v[c][7] += q.w;
-      }
+      add_split_partials8(v[c], partials + row * dim + idx * 8, rows * dim, splits);
       float t[8];
       unpack8(*reinterpret_cast<const uint4*>(bias + idx * 8), t);
 #pragma unroll
@@ -333,9 +352,21 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
 #pragma unroll
       for (int e = 0; e < E; ++e) x[e] = 0.f;
       const float* src = partials + t * p_ld + (int64_t)h * HD + lane * E;
-      for (int s = 0; s < splits; ++s) {
+      // all splits' loads in flight before the first add (split order kept)
+      for (int s0 = 0; s0 < splits; s0 += kBatchSplits) {
+        float a[kBatchSplits][E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) x[e] += src[(int64_t)s * p_slice + e];
+        for (int i = 0; i < kBatchSplits; ++i)
+          if (s0 + i < splits) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) a[i][e] = src[(int64_t)(s0 + i) * p_slice + e];
+          }
+#pragma unroll
+        for (int i = 0; i < kBatchSplits; ++i)
+          if (s0 + i < splits) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) x[e] += a[i][e];
+          }
       }
     } else {
 #pragma unroll
@@ -352,12 +383,15 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(__nv_bfloat16* qkv, i
     if (is_q || is_k) {
       const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
       if (nw) {
+        float wn[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) wn[e] = bf2f(nw[lane * E + e]);
         float ss = 0.f;
 #pragma unroll
         for (int e = 0; e < E; ++e) ss += x[e] * x[e];
         const float inv = rsqrtf(warp_sum(ss) / (float)HD + eps);
 #pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = x[e] * inv * bf2f(nw[lane * E + e]);
+        for (int e = 0; e < E; ++e) x[e] = x[e] * inv * wn[e];
       }
       float y[E];
 #pragma unroll
