@@ -5,8 +5,9 @@
 // elements, and the 64-column box fills the columns past hd with zeros, so the
 // scores are exact and only the first hd output columns are stored.
 //
-// One CTA = 128 query rows of one head of one sequence, 192 threads:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
+// One work item = 128 query rows of one head of one sequence; one persistent
+// CTA per SM walks its share of the items (heaviest first), 192 threads:
+//   warp 0      TMA producer: each item's Q tile, then K and V tiles of 128 keys
 //               (64-column boxes, 128-byte swizzle) through rings guarded by
 //               full/empty mbarriers: 2 K stages; 2 V stages, 1 for 192-wide
 //               query/key heads (their tiles fill shared memory otherwise).
@@ -23,7 +24,9 @@
 //               shared memory in the swizzled K-major layout the MMA reads.
 //               The running max only moves when it grows by more than 2^8, so
 //               the O rows in TMEM are rescaled rarely; the final 1/l scaling
-//               and the bf16 store happen once, from TMEM.
+//               and the bf16 store happen once per item, from TMEM; the
+//               output accumulator is double-buffered, so the next item's
+//               first P.V does not wait for that store.
 // Every mbarrier wait is bounded and sets the device error word on timeout.
 // No TMA multicast (the library also runs in multi-GPU jobs).
 #include <math.h>
@@ -89,14 +92,53 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// One work item: 128 query rows (tile m) of head h of sequence sq.  Items are
+// ordered heaviest first (causal tiles late in a sequence see more keys) and
+// dealt round-robin to the persistent CTAs.
+struct FaItem {
+  int m, h, sq, start, len, m0, ntiles, kvh;
+};
+
+template <bool CAUSAL>
+__device__ __forceinline__ FaItem fa_item(int w, const int32_t* __restrict__ cu, int nq, int nkv, int nseq,
+                                          int mblocks) {
+  FaItem it;
+  const int per_m = nq * nseq;
+  it.m = mblocks - 1 - w / per_m;
+  const int r = w % per_m;
+  it.h = r % nq;
+  it.sq = r / nq;
+  it.start = cu[it.sq];
+  it.len = cu[it.sq + 1] - it.start;
+  it.m0 = it.m * kTile;
+  const int kt = (it.len + kTile - 1) / kTile;
+  it.ntiles = it.m0 >= it.len ? 0 : (CAUSAL ? min(kt, it.m + 1) : kt);
+  it.kvh = it.h / (nq / nkv);
+  return it;
+}
+
+// First item index >= w of this CTA's sequence (w, w + G, ...) that has work, or W.
+template <bool CAUSAL>
+__device__ __forceinline__ int fa_next(int w, int W, int G, const int32_t* __restrict__ cu, int nq, int nkv,
+                                       int nseq, int mblocks) {
+  for (; w < W; w += G)
+    if (fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks).ntiles > 0) return w;
+  return W;
+}
+
 // HEADS3D: the maps are [rows][heads][hd] views (coordinates: column 0, head
 // index, row) of heads narrower than the 64-column box; out_cols = hd.
+// Persistent: gridDim.x CTAs walk the W = mblocks * nq * num_seqs items; TMEM,
+// barriers and the K/V ring live across items, the output accumulator is
+// double-buffered in TMEM (the next item's P.V starts while the softmax warps
+// store the previous item), and the producer streams the next item's Q / K / V
+// while the current item finishes.
 template <int HDK, int HDV, bool CAUSAL, bool HEADS3D = false>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, int64_t os,
                             int64_t ohs, const int32_t* __restrict__ cu, int nq, int nkv, int64_t qhs, int64_t khs,
-                            int64_t vhs, float scale_log2, int mblocks, int out_cols, unsigned* err) {
+                            int64_t vhs, float scale_log2, int mblocks, int nseq, int out_cols, unsigned* err) {
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -107,32 +149,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + 3 * kTileBytes;
   uint8_t* sP = sV + VS * kVBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 3;
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_free = bars + 11;
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_full = bars;        // Q of the current item landed (once per item)
+  uint64_t* q_empty = bars + 1;   // the item's last S issued and done: Q may be replaced
+  uint64_t* k_full = bars + 2;    // [2]
+  uint64_t* k_empty = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;    // [2]
+  uint64_t* v_empty = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;   // [2]
+  uint64_t* s_free = bars + 12;   // [2]
+  uint64_t* p_full = bars + 14;   // P of a tile written (128 arrivals)
+  uint64_t* o_done = bars + 15;   // P.V of a tile done
+  uint64_t* o_free = bars + 16;   // [2] an output buffer read out (128 arrivals)
+  uint64_t* drain = bars + 18;    // MMA teardown after an abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // heavier (later) query tiles first: causal tiles see more keys
-  const int m = mblocks - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, sq = blockIdx.z;
-  pdl_wait();  // q / k / v and the sequence offsets come from earlier kernels
-  const int start = cu[sq];
-  const int len = cu[sq + 1] - start;
-  const int m0 = m * kTile;
-  if (m0 >= len) return;  // whole CTA: no barrier or TMEM touched yet
-  const int ntiles = CAUSAL ? min((len + kTile - 1) / kTile, m + 1) : (len + kTile - 1) / kTile;
-  const int kvh = h / (nq / nkv);
+  const int W = mblocks * nq * nseq;
+  const int G = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -140,9 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
+      mbar_init(&o_free[i], 128);
     }
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -157,52 +197,74 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // q / k / v and the sequence offsets come from earlier kernels
+  const int w_first = fa_next<CAUSAL>(blockIdx.x, W, G, cu, nq, nkv, nseq, mblocks);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const int qc = (int)(h * qhs), kc = (int)(kvh * khs), vc = (int)(kvh * vhs);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      if (HEADS3D) tma_load_3d(sQ, &tmQ, q_full, 0, h, start + m0);
-      else
-        for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
-          tma_load_2d(sQ + bx * kBoxBytes, &tmQ, q_full, qc + 64 * bx, start + m0);
-      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int row = start + j * kTile;
-        if (j >= 2 && !mbar_wait(&k_empty[st], ph ^ 1, err)) {
+      int g = 0, n = 0;  // K/V tiles and items so far
+      for (int w = w_first; w < W && !*abort_flag; w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
+        const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+        const int qc = (int)(it.h * qhs), kc = (int)(it.kvh * khs), vc = (int)(it.kvh * vhs);
+        bool ok = true;
+        for (int j = 0; j < it.ntiles; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          const int row = it.start + j * kTile;
+          if (g >= 2 && !mbar_wait(&k_empty[st], ph ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          if (HEADS3D) tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, it.kvh, row);
+          else
+            for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
+              tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
+          if (j == 0) {
+            // this item's Q, once the previous item's last scores are done with it
+            if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            if (HEADS3D) tma_load_3d(sQ, &tmQ, q_full, 0, it.h, it.start + it.m0);
+            else
+              for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
+                tma_load_2d(sQ + bx * kBoxBytes, &tmQ, q_full, qc + 64 * bx, it.start + it.m0);
+          }
+          const int vst = g % VS;
+          const uint32_t vph = (g / VS) & 1;
+          if (g >= VS && !mbar_wait(&v_empty[vst], vph ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[vst], kVBytes);
+          if (HEADS3D) tma_load_3d(sV + vst * kVBytes, &tmV, &v_full[vst], 0, it.kvh, row);
+          else
+            for (int bx = 0; bx < Cf::BOXES_V; ++bx)
+              tma_load_2d(sV + vst * kVBytes + bx * kBoxBytes, &tmV, &v_full[vst], vc + 64 * bx, row);
+        }
+        if (!ok) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        if (HEADS3D) tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, kvh, row);
-        else
-          for (int bx = 0; bx < Cf::BOXES_QK; ++bx)
-            tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
-        const int vst = j % VS;
-        const uint32_t vph = (j / VS) & 1;
-        if (j >= VS && !mbar_wait(&v_empty[vst], vph ^ 1, err)) {
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[vst], kVBytes);
-        if (HEADS3D) tma_load_3d(sV + vst * kVBytes, &tmV, &v_full[vst], 0, kvh, row);
-        else
-          for (int bx = 0; bx < Cf::BOXES_V; ++bx)
-            tma_load_2d(sV + vst * kVBytes + bx * kBoxBytes, &tmV, &v_full[vst], vc + 64 * bx, row);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // The (item, tile) sequence is flat: S of the next tile is issued before
+    // P.V of the current one, except across an item boundary, where P.V goes
+    // first (the next item's Q may still be in flight).
     if (lane == 0) {
-      const uint32_t tO = tmem + 256;
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+      bool ok = true;
+      // S_g = Q K_g^T into score buffer g & 1; commits q_empty after an item's last tile
+      auto issue_s = [&](int g, bool last) -> bool {
+        const int st = g & 1;
+        const uint32_t ph = (g >> 1) & 1;
         if (!mbar_wait(&k_full[st], ph, err)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[st], ph ^ 1, err)) return false;
+        if (g >= 2 && !mbar_wait(&s_free[st], ph ^ 1, err)) return false;
         tc_fence_after();
         const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
 #pragma unroll
@@ -212,142 +274,186 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&s_full[st]);
         umma_commit(&k_empty[st]);
+        if (last) umma_commit(q_empty);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, err);
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
-        if (j + 1 < ntiles && !(ok = issue_s(j + 1))) break;
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int vst = j % VS;
-        if (!mbar_wait(p_full, j & 1, err) || !mbar_wait(&v_full[vst], (j / VS) & 1, err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + vst * kVBytes);
+      int w = w_first;
+      if (w < W) {
+        FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+        int j = 0, g = 0, n = 0;
+        ok = mbar_wait(q_full, 0, err) && issue_s(0, it.ntiles == 1);
+        while (ok && !*abort_flag) {
+          const bool more = j + 1 < it.ntiles;
+          if (more && !(ok = issue_s(g + 1, j + 2 == it.ntiles))) break;
+          // O += P_g V_g into output buffer n & 1
+          const int vst = g % VS;
+          if (!mbar_wait(p_full, g & 1, err) || !mbar_wait(&v_full[vst], (g / VS) & 1, err)) {
+            ok = false;
+            break;
+          }
+          if (j == 0 && n >= 2 && !mbar_wait(&o_free[n & 1], ((n >> 1) - 1) & 1, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tO = tmem + 256 + (n & 1) * 128;
+          const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + vst * kVBytes);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
-                    smem_desc_mn128(v0 + ks * 2048, kBoxBytes), Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(o_done);
-        umma_commit(&v_empty[vst]);
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
+                      smem_desc_mn128(v0 + ks * 2048, kBoxBytes), Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&v_empty[vst]);
+          ++g;
+          if (more) {
+            ++j;
+            continue;
+          }
+          // next item: its Q, then its first scores
+          w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks);
+          if (w >= W) break;
+          it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+          ++n;
+          j = 0;
+          if (!(ok = mbar_wait(q_full, n & 1, err) && issue_s(g, it.ntiles == 1))) break;
+        }
       }
-      if (!ok) *abort_flag = 1;
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit(drain);  // every MMA issued so far completes before TMEM is freed
+        mbar_wait(drain, 0, err);
+      }
     }
     __syncwarp();
   } else {
     // ---------------- softmax (warps 2..5, one query row per thread) ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
-    const int qpos = m0 + row;     // query position within the sequence
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    float mref = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (*abort_flag || !mbar_wait(&s_full[st], ph, err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lanes + st * 128 + c * 32, sr + c * 32);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);
-      const int kv0 = j * kTile;
-      const bool full_tile = kv0 + kTile <= len && (!CAUSAL || kv0 + kTile - 1 <= m0);
-      // raw-score max (scale > 0), masked keys set to -inf
-      float mx = -INFINITY;
-      if (full_tile) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const int col = kv0 + c;
-          if (col >= len || (CAUSAL && col > qpos)) sr[c] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sr[c]));
-        }
-      }
-      mx *= scale_log2;
-      // running max (log2 domain): moved only when it grows by more than 2^kRescaleLog2
-      float alpha = 1.f;
-      bool rescale = false;
-      if (mx > mref + kRescaleLog2 || (mref == -INFINITY && mx > -INFINITY)) {
-        rescale = mref != -INFINITY;
-        alpha = rescale ? ex2(mref - mx) : 0.f;
-        l *= alpha;
-        mref = mx;
-      }
-      // P = 2^(s * scale - ref), packed to bf16 pairs in place, before waiting
-      // for the previous P.V product (this overlaps the exponentials with it)
-      const float ref = mref == -INFINITY ? 0.f : mref;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -ref));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -ref));
-        rs += p0 + p1;
-        sr[c] = pack2(p0, p1);
-      }
-      if (j > 0) {  // P_{j-1} consumed and O up to date
-        if (!mbar_wait(o_done, (j - 1) & 1, err)) {
+    int g = 0, n = 0;  // tiles and items so far
+    for (int w = w_first; w < W && ok; w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
+      const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+      const int qpos = it.m0 + row;  // query position within the sequence
+      const uint32_t tO = tmem + lanes + 256 + (n & 1) * 128;
+      float mref = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.ntiles; ++j, ++g) {
+        const int st = g & 1;
+        const uint32_t ph = (g >> 1) & 1;
+        // warp-uniform outcome: the TMEM loads below are warp-collective
+        if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&s_full[st], ph, err))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-          for (int c = 0; c < HDV / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
-            tmem_ld_wait();
+        uint32_t sr[128];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * (rescale ? alpha : 1.f));
-            tmem_st_32x32b_x32(tmem + lanes + 256 + c * 32, r);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lanes + st * 128 + c * 32, sr + c * 32);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&s_free[st]);
+        const int kv0 = j * kTile;
+        const bool full_tile = kv0 + kTile <= it.len && (!CAUSAL || kv0 + kTile - 1 <= it.m0);
+        // raw-score max (scale > 0), masked keys set to -inf; eight independent
+        // partial maxima (one dependent chain of 128 would idle this warp's
+        // scheduler for most of the reduction)
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+        if (full_tile) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            const int col = kv0 + c;
+            if (col >= it.len || (CAUSAL && col > qpos)) sr[c] = __float_as_uint(-INFINITY);
+            m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
           }
-          tmem_st_wait();
         }
-      }
-      uint8_t* prow = sP + row * 128;
+        float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        mx *= scale_log2;
+        // running max (log2 domain): moved only when it grows by more than 2^kRescaleLog2
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > mref + kRescaleLog2 || (mref == -INFINITY && mx > -INFINITY)) {
+          rescale = mref != -INFINITY;
+          alpha = rescale ? ex2(mref - mx) : 0.f;
+          l *= alpha;
+          mref = mx;
+        }
+        // P = 2^(s * scale - ref), packed to bf16 pairs in place, before waiting
+        // for the previous P.V product (this overlaps the exponentials with it)
+        const float ref = mref == -INFINITY ? 0.f : mref;
+        float r8[8];
 #pragma unroll
-      for (int k = 0; k < 16; ++k)  // 16-byte chunk k = keys 8k..8k+7
-        *reinterpret_cast<uint4*>(prow + (k >> 3) * kBoxBytes + (((k & 7) ^ (row & 7)) << 4)) =
-            make_uint4(sr[4 * k], sr[4 * k + 1], sr[4 * k + 2], sr[4 * k + 3]);
-      l += rs;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && !*abort_flag && mbar_wait(o_done, (ntiles - 1) & 1, err)) {
+        for (int i = 0; i < 8; ++i) r8[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -ref));
+          const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -ref));
+          r8[c & 7] += p0 + p1;
+          sr[c] = pack2(p0, p1);
+        }
+        const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+        if (g > 0) {  // the previous tile's P.V has consumed P (and, within an item, O is up to date)
+          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+            for (int c = 0; c < HDV / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tO + c * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * (rescale ? alpha : 1.f));
+              tmem_st_32x32b_x32(tO + c * 32, r);
+            }
+            tmem_st_wait();
+          }
+        }
+        uint8_t* prow = sP + row * 128;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)  // 16-byte chunk k = keys 8k..8k+7
+          *reinterpret_cast<uint4*>(prow + (k >> 3) * kBoxBytes + (((k & 7) ^ (row & 7)) << 4)) =
+              make_uint4(sr[4 * k], sr[4 * k + 1], sr[4 * k + 2], sr[4 * k + 3]);
+        l += rs;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!__all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait(o_done, (g - 1) & 1, err))) {
+        ok = false;
+        break;
+      }
+      // this item's output: O / l from TMEM, bf16 rows
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = qpos < len;
-      __nv_bfloat16* orow = out + (int64_t)(start + (valid ? qpos : 0)) * os + (int64_t)h * ohs;
+      const bool valid = qpos < it.len;
+      __nv_bfloat16* orow = out + (int64_t)(it.start + (valid ? qpos : 0)) * os + (int64_t)it.h * ohs;
 #pragma unroll 1
       for (int c = 0; c < HDV / 32; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lanes + 256 + c * 32, r);
+        tmem_ld_32x32b_x32(tO + c * 32, r);
         tmem_ld_wait();
         if (valid) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (HEADS3D && c * 32 + g * 8 >= out_cols) break;
+          for (int g4 = 0; g4 < 4; ++g4) {
+            if (HEADS3D && c * 32 + g4 * 8 >= out_cols) break;
             float f[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * g + i]) * inv;
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = pack8(f);
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * g4 + i]) * inv;
+            *reinterpret_cast<uint4*>(orow + c * 32 + g4 * 8) = pack8(f);
           }
         }
       }
-    } else {
-      *abort_flag = 1;
+      tc_fence_before();
+      mbar_arrive(&o_free[n & 1]);
     }
+    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -420,9 +526,15 @@ int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
       return B200_ERROR_UNSUPPORTED;
     attr_set[dev] = true;
   }
-  launch_kernel(k, dim3(mblocks, nq, num_seqs), kThreads, Cf::SMEM, st, mq, mk, mv,
-                static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq, nkv, qhs, khs, vhs, scale_log2, mblocks, out_cols,
-                b200::error_word(dev));
+  // persistent: one CTA per SM (shared memory allows no second), each walking
+  // every G-th work item
+  static int sms[64] = {0};
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int64_t items = (int64_t)mblocks * nq * num_seqs;
+  if (items > INT32_MAX) return B200_ERROR_UNSUPPORTED;
+  const int grid = (int)std::min<int64_t>(items, sms[dev] > 0 ? sms[dev] : 148);
+  launch_kernel(k, dim3(grid), kThreads, Cf::SMEM, st, mq, mk, mv, static_cast<__nv_bfloat16*>(out), os, ohs, cu, nq,
+                nkv, qhs, khs, vhs, scale_log2, mblocks, num_seqs, out_cols, b200::error_word(dev));
   B200_CHECK_LAUNCH();
   return B200_OK;
 }

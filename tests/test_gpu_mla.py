@@ -87,20 +87,35 @@ def test_mla_prep(q_hs, q_off):
     assert G.device_errors() == 0
 
 
-@pytest.mark.parametrize("nh,ctx,block,split", [
-    (16, [1, 63, 64, 65, 1000, 4096], 64, True),
-    (16, [1, 63, 64, 65, 1000, 4096], 128, False),
-    (32, [300, 17], 128, True),
+@pytest.mark.parametrize("nh,ctx,block,split,ramp", [
+    (16, [1, 63, 64, 65, 1000, 4096], 64, True, False),
+    (16, [1, 63, 64, 65, 1000, 4096], 128, False, False),
+    (32, [1300, 17], 128, True, False),
+    # 192-token blocks: a 128-token tile spans two cache blocks
+    (16, [129, 191, 193, 2000], 192, True, False),
+    # scores that grow along the context: the running max moves tile after tile
+    (16, [3000, 700, 128], 64, False, True),
+    (16, [3000, 700, 128], 128, True, True),
 ])
-def test_mla_decode(nh, ctx, block, split):
+def test_mla_decode(nh, ctx, block, split, ramp):
     rng = np.random.default_rng(nh + block)
     B = len(ctx)
     max_ctx = max(ctx)
     mb = (max_ctx + block - 1) // block
     nblocks = B * mb + 3
-    cache = G.rounded(rng.standard_normal((nblocks * block, 576)).astype(F))
+    cache = rng.standard_normal((nblocks * block, 576)).astype(F)
     tables = rng.permutation(nblocks)[:B * mb].reshape(B, mb).astype(np.int32)
-    q = G.rounded(rng.standard_normal((B, nh * 576)).astype(F) * 0.05)
+    q = G.rounded(rng.standard_normal((B, nh * 576)).astype(F) * (0.5 if ramp else 0.05))
+    if ramp:
+        # row j of block table entry k of sequence b holds token k*block + j:
+        # scale it by 1 + 3 * position / max_ctx (the same direction per token)
+        q[:, :] = np.abs(q)
+        for b in range(B):
+            for k in range(mb):
+                pos = k * block + np.arange(block)
+                rows = slice(tables[b, k] * block, (tables[b, k] + 1) * block)
+                cache[rows] = np.abs(cache[rows]) * (1.0 + 3.0 * pos / max_ctx)[:, None]
+    cache = G.rounded(cache)
     scale = mla.softmax_scale(CFG)
     out = torch.empty(B, nh * 512, dtype=torch.bfloat16, device=G.DEV)
     L = G.L()
