@@ -6,7 +6,7 @@
 // scores are exact and only the first hd output columns are stored.
 //
 // One work item = 128 query rows of one head of one sequence; one persistent
-// CTA per SM walks its share of the items (heaviest first), 192 threads:
+// CTA per SM walks its share of the items (heaviest first), 320 threads:
 //   warp 0      TMA producer: each item's Q tile, then K and V tiles of 128 keys
 //               (64-column boxes, 128-byte swizzle) through rings guarded by
 //               full/empty mbarriers: 2 K stages; 2 V stages, 1 for 192-wide
@@ -14,18 +14,24 @@
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma:
 //               S_j = Q K_j^T into one of two TMEM score buffers (M=128,
 //               N=128, K=128), and O += P_j V_j into the TMEM output
-//               accumulator (P from shared memory, V read MN-major so no
-//               transpose is ever materialised).  S_{j+1} is issued before
-//               waiting for P_j, so the tensor core computes the next scores
-//               while the softmax warps work on the current ones.
-//   warps 2-5   softmax, one query row per thread (TMEM lane = row): load the
-//               row's 128 scores, mask (causal rule j > i and the sequence
-//               end), online max / sum in the log2 domain, write P (bf16) into
-//               shared memory in the swizzled K-major layout the MMA reads.
-//               The running max only moves when it grows by more than 2^8, so
-//               the O rows in TMEM are rescaled rarely; the final 1/l scaling
-//               and the bf16 store happen once per item, from TMEM; the
-//               output accumulator is double-buffered, so the next item's
+//               accumulator (P read from tensor memory, where the softmax
+//               wrote it over its own scores; V read MN-major so no transpose
+//               is ever materialised).  S_{j+1} is issued before waiting for
+//               P_j, so the tensor core computes the next scores while the
+//               softmax warps work on the current ones; a score buffer is
+//               reused once the P.V that reads its P is done.
+//   warps 2-9   softmax, two threads per query row (TMEM lane = row; warps
+//               2-5 take key columns 0-63, warps 6-9 columns 64-127, so each
+//               scheduler runs two softmax warps): load the row's scores,
+//               mask (causal rule j > i and the sequence end), online max /
+//               sum in the log2 domain (the two halves of a row exchange their
+//               maxima through shared memory once per tile), write P (bf16
+//               pairs) into TMEM over the half's own score columns (keys 0-63
+//               at columns 0-31, keys 64-127 at 64-95), the layout the MMA
+//               reads as its A operand.  The running max only moves when it grows by more than
+//               2^8, so the O rows in TMEM are rescaled rarely; the final 1/l
+//               scaling and the bf16 store happen once per item, from TMEM;
+//               the output accumulator is double-buffered, so the next item's
 //               first P.V does not wait for that store.
 // Every mbarrier wait is bounded and sets the device error word on timeout.
 // No TMA multicast (the library also runs in multi-GPU jobs).
@@ -40,10 +46,10 @@ using namespace b200;
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kTile = 128;                    // query rows per CTA = keys per tile
 constexpr int kBoxBytes = kTile * 128;        // 128 rows x 64 bf16 (one 128-byte swizzle span)
-constexpr int kPBytes = 2 * kBoxBytes;        // P: 128 rows x 128 keys
+constexpr int kXBytes = (4 + 2) * 128 * 4;    // row-half exchange: maxima [2 tiles][2 halves], sums [2 halves]
 // query/key head width HDK (64, 128 or 192) and value width HDV (64 or 128):
 // Q and K tiles are HDK / 64 boxes of 128 rows, V tiles HDV / 64 boxes
 template <int HDK, int HDV>
@@ -52,7 +58,7 @@ struct TcCfg {
   static constexpr int TILE_QK = BOXES_QK * kBoxBytes, TILE_V = BOXES_V * kBoxBytes;
   static constexpr int V_STAGES = HDK > 128 ? 1 : 2;
   // Q, K x2, V x V_STAGES, P + alignment + barriers
-  static constexpr int SMEM = 3 * TILE_QK + V_STAGES * TILE_V + kPBytes + 1024 + 256;
+  static constexpr int SMEM = 3 * TILE_QK + V_STAGES * TILE_V + kXBytes + 1024 + 256;
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HDV) | (1u << 16);  // B operand (V) MN-major
 };
 constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256,384)
@@ -84,12 +90,36 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // 2^x on the special-function unit (PTX ex2.approx, relative error ~2^-22)
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (M x K, bf16 pairs per
+// 32-bit column, row m in lane m) read from tensor memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Named barrier `id` over `n` threads.
+__device__ __forceinline__ void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// Named barrier `id` over 64 threads returning the OR of `v` over them.
+__device__ __forceinline__ bool pair_or(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %2, 0;\n\tbar.red.or.pred q, %1, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
 }
 
 // One work item: 128 query rows (tile m) of head h of sequence sq.  Items are
@@ -147,8 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kTileBytes = Cf::TILE_QK, kVBytes = Cf::TILE_V, VS = Cf::V_STAGES;
   uint8_t* sK = smem + kTileBytes;
   uint8_t* sV = smem + 3 * kTileBytes;
-  uint8_t* sP = sV + VS * kVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  float* sMx = reinterpret_cast<float*>(sV + VS * kVBytes);  // [tile parity][half][row]
+  float* sL = sMx + 4 * 128;                            // [half][row]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + 2 * 128);
   uint64_t* q_full = bars;        // Q of the current item landed (once per item)
   uint64_t* q_empty = bars + 1;   // the item's last S issued and done: Q may be replaced
   uint64_t* k_full = bars + 2;    // [2]
@@ -156,10 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = bars + 6;    // [2]
   uint64_t* v_empty = bars + 8;   // [2]
   uint64_t* s_full = bars + 10;   // [2]
-  uint64_t* s_free = bars + 12;   // [2]
-  uint64_t* p_full = bars + 14;   // P of a tile written (128 arrivals)
-  uint64_t* o_done = bars + 15;   // P.V of a tile done
-  uint64_t* o_free = bars + 16;   // [2] an output buffer read out (128 arrivals)
+  uint64_t* pv_done = bars + 12;  // [2] P.V of the tile whose P sits in score buffer i done
+  uint64_t* p_full = bars + 14;   // P of a tile written (256 arrivals)
+  uint64_t* o_free = bars + 16;   // [2] an output buffer read out (256 arrivals)
   uint64_t* drain = bars + 18;    // MMA teardown after an abort
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -177,11 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&o_free[i], 128);
+      mbar_init(&pv_done[i], 1);
+      mbar_init(&o_free[i], 256);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    mbar_init(p_full, 256);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -264,7 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = g & 1;
         const uint32_t ph = (g >> 1) & 1;
         if (!mbar_wait(&k_full[st], ph, err)) return false;
-        if (g >= 2 && !mbar_wait(&s_free[st], ph ^ 1, err)) return false;
+        // the buffer holds P of tile g - 2 until that tile's P.V is done
+        if (g >= 2 && !mbar_wait(&pv_done[st], ph ^ 1, err)) return false;
         tc_fence_after();
         const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
 #pragma unroll
@@ -297,12 +327,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t tO = tmem + 256 + (n & 1) * 128;
-          const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + vst * kVBytes);
+          // P_g (bf16, in TMEM over its own scores: keys 0-63 at columns 0-31,
+          // keys 64-127 at columns 64-95 of score buffer g & 1) is the A operand
+          const uint32_t pa = tmem + (g & 1) * 128, v0 = smem_u32(sV + vst * kVBytes);
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            umma_bf16(tO, smem_desc_k128(p0 + (ks >> 2) * kBoxBytes + (ks & 3) * 32),
-                      smem_desc_mn128(v0 + ks * 2048, kBoxBytes), Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(o_done);
+            umma_bf16_ts(tO, pa + (ks >> 2) * 64 + (ks & 3) * 8, smem_desc_mn128(v0 + ks * 2048, kBoxBytes),
+                         Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&pv_done[g & 1]);
           umma_commit(&v_empty[vst]);
           ++g;
           if (more) {
@@ -326,52 +358,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax (warps 2..5, one query row per thread) ----------------
+    // ---------------- softmax (warps 2..9: two threads per query row) ----------------
+    // Warp w owns TMEM lanes 32 (w % 4) ..; warps 2-5 take key columns 0-63 of
+    // every score row, warps 6-9 columns 64-127 (and the matching halves of P
+    // and O).  The two threads of a row exchange their partial maxima through
+    // shared memory once per tile (barrier of the warp pair), so both take the
+    // same running-max decisions; row sums stay per thread until the item ends.
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const int pair_bar = 1 + quarter;  // named barrier of warps (quarter + 2, quarter + 6)
     bool ok = true;
     int g = 0, n = 0;  // tiles and items so far
     for (int w = w_first; w < W && ok; w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
       const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
       const int qpos = it.m0 + row;  // query position within the sequence
-      const uint32_t tO = tmem + lanes + 256 + (n & 1) * 128;
+      const uint32_t tO = tmem + lanes + 256 + (n & 1) * 128 + half * (HDV / 2);
       float mref = -INFINITY, l = 0.f;
       for (int j = 0; j < it.ntiles; ++j, ++g) {
         const int st = g & 1;
         const uint32_t ph = (g >> 1) & 1;
-        // warp-uniform outcome: the TMEM loads below are warp-collective
-        if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&s_full[st], ph, err))) {
+        // warp-uniform outcome (the TMEM loads below are warp-collective), and
+        // the same for both warps of the pair (they meet at named barriers)
+        const bool got = __all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait(&s_full[st], ph, err));
+        if (pair_or(pair_bar, !got)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sr[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lanes + st * 128 + c * 32, sr + c * 32);
+        uint32_t sr[64];
+        tmem_ld_32x32b_x32(tmem + lanes + st * 128 + half * 64, sr);
+        tmem_ld_32x32b_x32(tmem + lanes + st * 128 + half * 64 + 32, sr + 32);
         tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(&s_free[st]);
-        const int kv0 = j * kTile;
-        const bool full_tile = kv0 + kTile <= it.len && (!CAUSAL || kv0 + kTile - 1 <= it.m0);
-        // raw-score max (scale > 0), masked keys set to -inf; eight independent
-        // partial maxima (one dependent chain of 128 would idle this warp's
-        // scheduler for most of the reduction)
+        const int kv0 = j * kTile + half * 64;  // first key of this thread's columns
+        const bool full_half = kv0 + 64 <= it.len && (!CAUSAL || kv0 + 63 <= it.m0);
+        // raw-score max of this half (scale > 0), masked keys set to -inf
         float m8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-        if (full_tile) {
+        if (full_half) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
+          for (int c = 0; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
         } else {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
+          for (int c = 0; c < 64; ++c) {
             const int col = kv0 + c;
             if (col >= it.len || (CAUSAL && col > qpos)) sr[c] = __float_as_uint(-INFINITY);
             m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
           }
         }
         float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        // the row's other half (slots alternate by tile: the partner is at most one tile behind)
+        sMx[((g & 1) * 2 + half) * 128 + row] = mx;
+        named_bar_sync(pair_bar, 64);
+        mx = fmaxf(mx, sMx[((g & 1) * 2 + (half ^ 1)) * 128 + row]);
         mx *= scale_log2;
         // running max (log2 domain): moved only when it grows by more than 2^kRescaleLog2
         float alpha = 1.f;
@@ -382,29 +423,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= alpha;
           mref = mx;
         }
-        // P = 2^(s * scale - ref), packed to bf16 pairs in place, before waiting
-        // for the previous P.V product (this overlaps the exponentials with it)
+        // P = 2^(s * scale - ref), packed to bf16 pairs in place
         const float ref = mref == -INFINITY ? 0.f : mref;
         float r8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) r8[i] = 0.f;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < 32; ++c) {
           const float p0 = ex2(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -ref));
           const float p1 = ex2(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -ref));
           r8[c & 7] += p0 + p1;
           sr[c] = pack2(p0, p1);
         }
         const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
-        if (g > 0) {  // the previous tile's P.V has consumed P (and, within an item, O is up to date)
-          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, err))) {
-            ok = false;
-            break;
-          }
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          // O holds the item's tiles < j once the previous tile's P.V is done
+          // (per-buffer barrier: its previous phase, tile g - 3, is complete);
+          // a failed wait is acted on at the next tile's pair vote (no exit between pair barriers)
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err))) ok = false;
           tc_fence_after();
-          if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          if (ok) {
 #pragma unroll 1
-            for (int c = 0; c < HDV / 32; ++c) {
+            for (int c = 0; c < HDV / 64; ++c) {
               uint32_t r[32];
               tmem_ld_32x32b_x32(tO + c * 32, r);
               tmem_ld_wait();
@@ -415,34 +455,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_wait();
           }
         }
-        uint8_t* prow = sP + row * 128;
-#pragma unroll
-        for (int k = 0; k < 16; ++k)  // 16-byte chunk k = keys 8k..8k+7
-          *reinterpret_cast<uint4*>(prow + (k >> 3) * kBoxBytes + (((k & 7) ^ (row & 7)) << 4)) =
-              make_uint4(sr[4 * k], sr[4 * k + 1], sr[4 * k + 2], sr[4 * k + 3]);
+        // P over this half's own score columns (32 columns of bf16 pairs)
+        tmem_st_32x32b_x32(tmem + lanes + st * 128 + half * 64, sr);
+        tmem_st_wait();
         l += rs;
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
       }
-      if (!__all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait(o_done, (g - 1) & 1, err))) {
+      const bool done = __all_sync(0xffffffffu, ok && !*abort_flag &&
+                                                    mbar_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err));
+      if (pair_or(pair_bar, !done)) {
         ok = false;
         break;
       }
-      // this item's output: O / l from TMEM, bf16 rows
+      // the row sum: both halves
+      sL[half * 128 + row] = l;
+      named_bar_sync(pair_bar, 64);
+      l += sL[(half ^ 1) * 128 + row];
+      named_bar_sync(pair_bar, 64);  // sL is rewritten at the next item's end
+      // this item's output: O / l from TMEM, bf16 rows (this thread's half of the columns)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool valid = qpos < it.len;
-      __nv_bfloat16* orow = out + (int64_t)(it.start + (valid ? qpos : 0)) * os + (int64_t)it.h * ohs;
+      __nv_bfloat16* orow =
+          out + (int64_t)(it.start + (valid ? qpos : 0)) * os + (int64_t)it.h * ohs + half * (HDV / 2);
 #pragma unroll 1
-      for (int c = 0; c < HDV / 32; ++c) {
+      for (int c = 0; c < HDV / 64; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tO + c * 32, r);
         tmem_ld_wait();
         if (valid) {
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
-            if (HEADS3D && c * 32 + g4 * 8 >= out_cols) break;
+            if (HEADS3D && half * (HDV / 2) + c * 32 + g4 * 8 >= out_cols) break;
             float f[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * g4 + i]) * inv;
