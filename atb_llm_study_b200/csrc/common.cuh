@@ -138,6 +138,38 @@ B200_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
   }
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (up to `ns` nanoseconds, woken when the phase completes) instead
+// of returning at once, so it does not take issue slots from the other warps
+// of its scheduler.
+B200_DEV bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for roles that share a scheduler with busy warps: same bound and
+// error reporting, but the thread sleeps inside try_wait between checks.
+B200_DEV bool mbar_wait_idle(uint64_t* bar, uint32_t parity, unsigned* err) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait_hint(a, parity, 20000u)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      raise_error(err, DEV_ERR_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------

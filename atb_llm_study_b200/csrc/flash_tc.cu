@@ -12,14 +12,15 @@
 //               full/empty mbarriers: 2 K stages; 2 V stages, 1 for 192-wide
 //               query/key heads (their tiles fill shared memory otherwise).
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma:
-//               S_j = Q K_j^T into one of two TMEM score buffers (M=128,
+//               S_j = Q K_j^T into one of three TMEM score buffers (M=128,
 //               N=128, K=128), and O += P_j V_j into the TMEM output
 //               accumulator (P read from tensor memory, where the softmax
 //               wrote it over its own scores; V read MN-major so no transpose
-//               is ever materialised).  S_{j+1} is issued before waiting for
-//               P_j, so the tensor core computes the next scores while the
-//               softmax warps work on the current ones; a score buffer is
-//               reused once the P.V that reads its P is done.
+//               is ever materialised).  Each step issues P.V of the next tile
+//               once its P is ready and then scores up to two tiles ahead, so
+//               the tensor core computes S_{j+2} right behind P_j V_j while the
+//               softmax warps work on S_{j+1}; a score buffer is reused once
+//               the P.V that reads its P is done.
 //   warps 2-9   softmax, two threads per query row (TMEM lane = row; warps
 //               2-5 take key columns 0-63, warps 6-9 columns 64-127, so each
 //               scheduler runs two softmax warps): load the row's scores,
@@ -30,9 +31,9 @@
 //               at columns 0-31, keys 64-127 at 64-95), the layout the MMA
 //               reads as its A operand.  The running max only moves when it grows by more than
 //               2^8, so the O rows in TMEM are rescaled rarely; the final 1/l
-//               scaling and the bf16 store happen once per item, from TMEM;
-//               the output accumulator is double-buffered, so the next item's
-//               first P.V does not wait for that store.
+//               scaling and the bf16 store happen once per item, from TMEM
+//               (the next item's first P.V waits for that read; its scores do
+//               not).
 // Every mbarrier wait is bounded and sets the device error word on timeout.
 // No TMA multicast (the library also runs in multi-GPU jobs).
 #include <math.h>
@@ -61,7 +62,9 @@ struct TcCfg {
   static constexpr int SMEM = 3 * TILE_QK + V_STAGES * TILE_V + kXBytes + 1024 + 256;
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HDV) | (1u << 16);  // B operand (V) MN-major
 };
-constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kTmemCols = 512;           // score / P buffers at [0,128) [128,256) [256,384), O at [384,512)
+constexpr int kSBufs = 3;
+constexpr uint32_t kOCol = 384;
 constexpr float kRescaleLog2 = 8.f;           // move the running max only when it grows by > 2^8
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128);
 
@@ -159,10 +162,9 @@ __device__ __forceinline__ int fa_next(int w, int W, int G, const int32_t* __res
 // HEADS3D: the maps are [rows][heads][hd] views (coordinates: column 0, head
 // index, row) of heads narrower than the 64-column box; out_cols = hd.
 // Persistent: gridDim.x CTAs walk the W = mblocks * nq * num_seqs items; TMEM,
-// barriers and the K/V ring live across items, the output accumulator is
-// double-buffered in TMEM (the next item's P.V starts while the softmax warps
-// store the previous item), and the producer streams the next item's Q / K / V
-// while the current item finishes.
+// barriers and the K/V ring live across items, and the producer streams the
+// next item's Q / K / V (and the MMA thread its first scores) while the
+// current item finishes.
 template <int HDK, int HDV, bool CAUSAL, bool HEADS3D = false>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -186,12 +188,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = bars + 4;   // [2]
   uint64_t* v_full = bars + 6;    // [2]
   uint64_t* v_empty = bars + 8;   // [2]
-  uint64_t* s_full = bars + 10;   // [2]
-  uint64_t* pv_done = bars + 12;  // [2] P.V of the tile whose P sits in score buffer i done
-  uint64_t* p_full = bars + 14;   // P of a tile written (256 arrivals)
-  uint64_t* o_free = bars + 16;   // [2] an output buffer read out (256 arrivals)
-  uint64_t* drain = bars + 18;    // MMA teardown after an abort
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* s_full = bars + 10;   // [3] scores of the tile in buffer i ready
+  uint64_t* p_full = bars + 13;   // [3] P of the tile in buffer i written (256 arrivals)
+  uint64_t* pv_done = bars + 16;  // [3] P.V of the tile whose P sits in buffer i done
+  uint64_t* o_free = bars + 19;   // the output accumulator read out (256 arrivals)
+  uint64_t* drain = bars + 20;    // MMA teardown after an abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int W = mblocks * nq * nseq;
@@ -206,11 +208,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&pv_done[i], 1);
-      mbar_init(&o_free[i], 256);
     }
-    mbar_init(p_full, 256);
+    for (int i = 0; i < kSBufs; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(o_free, 256);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = g & 1;
           const uint32_t ph = (g >> 1) & 1;
           const int row = it.start + j * kTile;
-          if (g >= 2 && !mbar_wait(&k_empty[st], ph ^ 1, err)) {
+          if (g >= 2 && !mbar_wait_idle(&k_empty[st], ph ^ 1, err)) {
             ok = false;
             break;
           }
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sK + st * kTileBytes + bx * kBoxBytes, &tmK, &k_full[st], kc + 64 * bx, row);
           if (j == 0) {
             // this item's Q, once the previous item's last scores are done with it
-            if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, err)) {
+            if (n > 0 && !mbar_wait_idle(q_empty, (n - 1) & 1, err)) {
               ok = false;
               break;
             }
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int vst = g % VS;
           const uint32_t vph = (g / VS) & 1;
-          if (g >= VS && !mbar_wait(&v_empty[vst], vph ^ 1, err)) {
+          if (g >= VS && !mbar_wait_idle(&v_empty[vst], vph ^ 1, err)) {
             ok = false;
             break;
           }
@@ -283,72 +287,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    // The (item, tile) sequence is flat: S of the next tile is issued before
-    // P.V of the current one, except across an item boundary, where P.V goes
-    // first (the next item's Q may still be in flight).
+    // The (item, tile) sequence is flat.  Each step issues P.V of the next
+    // tile once its P is written, then the scores of the tiles up to two
+    // ahead (score buffer g % 3 is free once the P.V of tile g - 3 is done,
+    // which by then was issued a tile earlier), so the tensor core never waits
+    // for a P.V to finish before it gets more work.  A new item's first scores
+    // are held back while P.V work of the previous item remains and its Q has
+    // not landed.
     if (lane == 0) {
       bool ok = true;
-      // S_g = Q K_g^T into score buffer g & 1; commits q_empty after an item's last tile
+      // S_g = Q K_g^T into score buffer g % 3; commits q_empty after an item's last tile
       auto issue_s = [&](int g, bool last) -> bool {
-        const int st = g & 1;
-        const uint32_t ph = (g >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, err)) return false;
-        // the buffer holds P of tile g - 2 until that tile's P.V is done
-        if (g >= 2 && !mbar_wait(&pv_done[st], ph ^ 1, err)) return false;
+        const int b = g % kSBufs, u = g / kSBufs;
+        if (!mbar_wait_idle(&k_full[g & 1], (g >> 1) & 1, err)) return false;
+        if (g >= kSBufs && !mbar_wait_idle(&pv_done[b], (u - 1) & 1, err)) return false;
         tc_fence_after();
-        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * kTileBytes);
+        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + (g & 1) * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < HDK / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
-          umma_bf16(tmem + st * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
+          umma_bf16(tmem + b * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
-        umma_commit(&k_empty[st]);
+        umma_commit(&s_full[b]);
+        umma_commit(&k_empty[g & 1]);
         if (last) umma_commit(q_empty);
         return true;
       };
-      int w = w_first;
-      if (w < W) {
-        FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
-        int j = 0, g = 0, n = 0;
-        ok = mbar_wait(q_full, 0, err) && issue_s(0, it.ntiles == 1);
-        while (ok && !*abort_flag) {
-          const bool more = j + 1 < it.ntiles;
-          if (more && !(ok = issue_s(g + 1, j + 2 == it.ntiles))) break;
-          // O += P_g V_g into output buffer n & 1
-          const int vst = g % VS;
-          if (!mbar_wait(p_full, g & 1, err) || !mbar_wait(&v_full[vst], (g / VS) & 1, err)) {
-            ok = false;
-            break;
+      // cursors over the flat sequence: scores (s*) run up to two tiles ahead of P.V (p*)
+      int sw = w_first, sj = 0, sg = 0, sn = 0;
+      int pw = w_first, pj = 0, pg = 0, pn = 0;
+      FaItem sit{}, pit{};
+      if (sw < W) sit = pit = fa_item<CAUSAL>(sw, cu, nq, nkv, nseq, mblocks);
+      auto advance = [&](int& w, int& j, int& g, int& n, FaItem& it) {
+        ++g;
+        if (++j < it.ntiles) return;
+        j = 0;
+        ++n;
+        w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks);
+        if (w < W) it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+      };
+      auto fill = [&]() -> bool {
+        while (sw < W && sg <= pg + 1) {
+          if (sj == 0) {
+            // this item's Q: blocking only when no P.V work precedes these scores
+            if (sg > pg && !mbar_try_wait(smem_u32(q_full), sn & 1)) return true;
+            if (!mbar_wait_idle(q_full, sn & 1, err)) return false;
           }
-          if (j == 0 && n >= 2 && !mbar_wait(&o_free[n & 1], ((n >> 1) - 1) & 1, err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t tO = tmem + 256 + (n & 1) * 128;
-          // P_g (bf16, in TMEM over its own scores: keys 0-63 at columns 0-31,
-          // keys 64-127 at columns 64-95 of score buffer g & 1) is the A operand
-          const uint32_t pa = tmem + (g & 1) * 128, v0 = smem_u32(sV + vst * kVBytes);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_bf16_ts(tO, pa + (ks >> 2) * 64 + (ks & 3) * 8, smem_desc_mn128(v0 + ks * 2048, kBoxBytes),
-                         Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(&pv_done[g & 1]);
-          umma_commit(&v_empty[vst]);
-          ++g;
-          if (more) {
-            ++j;
-            continue;
-          }
-          // next item: its Q, then its first scores
-          w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks);
-          if (w >= W) break;
-          it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
-          ++n;
-          j = 0;
-          if (!(ok = mbar_wait(q_full, n & 1, err) && issue_s(g, it.ntiles == 1))) break;
+          if (!issue_s(sg, sj + 1 == sit.ntiles)) return false;
+          advance(sw, sj, sg, sn, sit);
         }
+        return true;
+      };
+      ok = fill();
+      while (ok && pw < W && !*abort_flag) {
+        // O += P_g V_g (the output accumulator is free once the previous item was stored)
+        const int b = pg % kSBufs, vst = pg % VS;
+        if (!mbar_wait_idle(&p_full[b], (pg / kSBufs) & 1, err) ||
+            !mbar_wait_idle(&v_full[vst], (pg / VS) & 1, err)) {
+          ok = false;
+          break;
+        }
+        if (pj == 0 && pn >= 1 && !mbar_wait_idle(o_free, (pn - 1) & 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // P_g (bf16, in TMEM over its own scores: keys 0-63 at columns 0-31,
+        // keys 64-127 at columns 64-95 of buffer g % 3) is the A operand
+        const uint32_t pa = tmem + b * 128, v0 = smem_u32(sV + vst * kVBytes);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16_ts(tmem + kOCol, pa + (ks >> 2) * 64 + (ks & 3) * 8, smem_desc_mn128(v0 + ks * 2048, kBoxBytes),
+                       Cf::IDESC_O, (pj > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(&pv_done[b]);
+        umma_commit(&v_empty[vst]);
+        advance(pw, pj, pg, pn, pit);
+        ok = fill();
       }
       if (!ok) {
         *abort_flag = 1;
@@ -374,14 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = w_first; w < W && ok; w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
       const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
       const int qpos = it.m0 + row;  // query position within the sequence
-      const uint32_t tO = tmem + lanes + 256 + (n & 1) * 128 + half * (HDV / 2);
+      const uint32_t tO = tmem + lanes + kOCol + half * (HDV / 2);
       float mref = -INFINITY, l = 0.f;
       for (int j = 0; j < it.ntiles; ++j, ++g) {
-        const int st = g & 1;
-        const uint32_t ph = (g >> 1) & 1;
+        const int st = g % kSBufs;
+        const uint32_t ph = (g / kSBufs) & 1;
         // warp-uniform outcome (the TMEM loads below are warp-collective), and
         // the same for both warps of the pair (they meet at named barriers)
-        const bool got = __all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait(&s_full[st], ph, err));
+        const bool got = __all_sync(0xffffffffu, ok && !*abort_flag && mbar_wait_idle(&s_full[st], ph, err));
         if (pair_or(pair_bar, !got)) {
           ok = false;
           break;
@@ -438,9 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
         if (j > 0 && __any_sync(0xffffffffu, rescale)) {
           // O holds the item's tiles < j once the previous tile's P.V is done
-          // (per-buffer barrier: its previous phase, tile g - 3, is complete);
+          // (per-buffer barrier: its previous phase, tile g - 4, is complete);
           // a failed wait is acted on at the next tile's pair vote (no exit between pair barriers)
-          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err))) ok = false;
+          if (!__all_sync(0xffffffffu, mbar_wait_idle(&pv_done[(g - 1) % kSBufs], ((g - 1) / kSBufs) & 1, err)))
+            ok = false;
           tc_fence_after();
           if (ok) {
 #pragma unroll 1
@@ -460,10 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
         l += rs;
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[st]);
       }
       const bool done = __all_sync(0xffffffffu, ok && !*abort_flag &&
-                                                    mbar_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err));
+                                                    mbar_wait_idle(&pv_done[(g - 1) % kSBufs], ((g - 1) / kSBufs) & 1, err));
       if (pair_or(pair_bar, !done)) {
         ok = false;
         break;
@@ -496,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&o_free[n & 1]);
+      mbar_arrive(o_free);
     }
     if (!ok) *abort_flag = 1;
   }
