@@ -51,13 +51,14 @@ def _moe_case(base):
     return C, w, list(moe.weight_items(C, w)), moe.ocfg(C)
 
 
-def _run_tp2(C, items, seqs, steps):
+def _run_tp2(C, items, seqs, steps, limits=None):
     import tp_worker
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, items, seqs, steps, "tp", q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_worker.run, args=(r, 2, port, C, items, seqs, steps, "tp", q, limits))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -128,3 +129,22 @@ def test_peer_wait_times_out_without_hanging(monkeypatch):
     assert res[0]["timeout_bits"] & 1, res[0]
     assert 1.0 < res[0]["seconds"] < 30.0, res[0]
     assert res[0]["context_ok"]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_long_prefill():
+    """A packed prefill of 2100 tokens (two prompts of 1100 and 1000): the
+    row-parallel projections take their prefill tiles and the NCCL all-reduce
+    path (beyond the fused peer all-reduce's 256 rows); the logits must match
+    the oracle as for short prompts."""
+    C, w, items, ocfg = _dense_case()
+    rng = np.random.default_rng(31)
+    seqs = [rng.integers(0, C["vocab_size"], n) for n in (1100, 1000)]
+    res = _run_tp2(C, items, seqs, 1, limits=(4, 1152, 2304))
+    (l0, t0), (l1, t1) = res[0]["prefill"], res[1]["prefill"]
+    np.testing.assert_array_equal(t0, t1)
+    full = np.concatenate([l0, l1], axis=1)
+    for i, s in enumerate(seqs):
+        ref = forward_last_logits(s, w, ocfg)
+        assert G.cosine(full[i], ref) >= 0.999, (i, G.cosine(full[i], ref))
+    np.testing.assert_array_equal(t0, np.argmax(full, 1))

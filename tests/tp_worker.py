@@ -46,14 +46,14 @@ def _bootstrap(rank, world, port, sym_bytes):
     return L, capi, dist, comm
 
 
-def run(rank, world, port, cfg, items, seqs, steps, mode, queue):
+def run(rank, world, port, cfg, items, seqs, steps, mode, queue, limits=None):
     try:
         import torch
 
         from test_gpu_engine import EngineConfig
 
         L, capi, dist, comm = _bootstrap(rank, world, port, 64 << 20)
-        ec = EngineConfig(None, json.dumps(cfg).encode(), rank, 8, 256, 512, 128, 5, 0.02)
+        ec = EngineConfig(None, json.dumps(cfg).encode(), rank, *(limits or (8, 256, 512)), 128, 5, 0.02)
         eng = ctypes.c_void_p()
         create = L.b200_engine_create_ep if mode == "ep" else L.b200_engine_create_tp
         capi.check(create(ctypes.byref(ec), comm, ctypes.byref(eng)), "engine_create_" + mode)
