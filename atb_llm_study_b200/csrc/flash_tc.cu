@@ -47,7 +47,8 @@ using namespace b200;
 
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;  // warps: 0 TMA, 1 score MMAs, 2-9 softmax, 10 P.V MMAs
+constexpr int kPvWarp = 10;
 constexpr int kTile = 128;                    // query rows per CTA = keys per tile
 constexpr int kBoxBytes = kTile * 128;        // 128 rows x 64 bf16 (one 128-byte swizzle span)
 constexpr int kXBytes = (4 + 2) * 128 * 4;    // row-half exchange: maxima [2 tiles][2 halves], sums [2 halves]
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = bars + 13;   // [3] P of the tile in buffer i written (256 arrivals)
   uint64_t* pv_done = bars + 16;  // [3] P.V of the tile whose P sits in buffer i done
   uint64_t* o_free = bars + 19;   // the output accumulator read out (256 arrivals)
-  uint64_t* drain = bars + 20;    // MMA teardown after an abort
+  uint64_t* drain = bars + 20;    // [2] MMA issuers' teardown after an abort
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -215,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(o_free, 256);
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -286,88 +288,80 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    // The (item, tile) sequence is flat.  Each step issues P.V of the next
-    // tile once its P is written, then the scores of the tiles up to two
-    // ahead (score buffer g % 3 is free once the P.V of tile g - 3 is done,
-    // which by then was issued a tile earlier), so the tensor core never waits
-    // for a P.V to finish before it gets more work.  A new item's first scores
-    // are held back while P.V work of the previous item remains and its Q has
-    // not landed.
+    // ---------------- score MMA issuer ----------------
+    // S_g = Q K_g^T into score buffer g % 3, as soon as K_g has landed and the
+    // P.V that read the buffer's previous P (tile g - 3) is done: the scores
+    // run up to two tiles ahead of P.V, which warp 10 issues independently.
     if (lane == 0) {
       bool ok = true;
-      // S_g = Q K_g^T into score buffer g % 3; commits q_empty after an item's last tile
-      auto issue_s = [&](int g, bool last) -> bool {
-        const int b = g % kSBufs, u = g / kSBufs;
-        if (!mbar_wait_idle(&k_full[g & 1], (g >> 1) & 1, err)) return false;
-        if (g >= kSBufs && !mbar_wait_idle(&pv_done[b], (u - 1) & 1, err)) return false;
-        tc_fence_after();
-        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + (g & 1) * kTileBytes);
-#pragma unroll
-        for (int ks = 0; ks < HDK / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
-          umma_bf16(tmem + b * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
+      int g = 0, n = 0;  // tiles and items so far
+      for (int w = w_first; w < W && ok && !*abort_flag;
+           w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
+        const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+        if (!mbar_wait_idle(q_full, n & 1, err)) {  // this item's Q
+          ok = false;
+          break;
         }
-        umma_commit(&s_full[b]);
-        umma_commit(&k_empty[g & 1]);
-        if (last) umma_commit(q_empty);
-        return true;
-      };
-      // cursors over the flat sequence: scores (s*) run up to two tiles ahead of P.V (p*)
-      int sw = w_first, sj = 0, sg = 0, sn = 0;
-      int pw = w_first, pj = 0, pg = 0, pn = 0;
-      FaItem sit{}, pit{};
-      if (sw < W) sit = pit = fa_item<CAUSAL>(sw, cu, nq, nkv, nseq, mblocks);
-      auto advance = [&](int& w, int& j, int& g, int& n, FaItem& it) {
-        ++g;
-        if (++j < it.ntiles) return;
-        j = 0;
-        ++n;
-        w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks);
-        if (w < W) it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
-      };
-      auto fill = [&]() -> bool {
-        while (sw < W && sg <= pg + 1) {
-          if (sj == 0) {
-            // this item's Q: blocking only when no P.V work precedes these scores
-            if (sg > pg && !mbar_try_wait(smem_u32(q_full), sn & 1)) return true;
-            if (!mbar_wait_idle(q_full, sn & 1, err)) return false;
+        for (int j = 0; j < it.ntiles; ++j, ++g) {
+          const int b = g % kSBufs, u = g / kSBufs;
+          if (!mbar_wait_idle(&k_full[g & 1], (g >> 1) & 1, err) ||
+              (g >= kSBufs && !mbar_wait_idle(&pv_done[b], (u - 1) & 1, err))) {
+            ok = false;
+            break;
           }
-          if (!issue_s(sg, sj + 1 == sit.ntiles)) return false;
-          advance(sw, sj, sg, sn, sit);
-        }
-        return true;
-      };
-      ok = fill();
-      while (ok && pw < W && !*abort_flag) {
-        // O += P_g V_g (the output accumulator is free once the previous item was stored)
-        const int b = pg % kSBufs, vst = pg % VS;
-        if (!mbar_wait_idle(&p_full[b], (pg / kSBufs) & 1, err) ||
-            !mbar_wait_idle(&v_full[vst], (pg / VS) & 1, err)) {
-          ok = false;
-          break;
-        }
-        if (pj == 0 && pn >= 1 && !mbar_wait_idle(o_free, (pn - 1) & 1, err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // P_g (bf16, in TMEM over its own scores: keys 0-63 at columns 0-31,
-        // keys 64-127 at columns 64-95 of buffer g % 3) is the A operand
-        const uint32_t pa = tmem + b * 128, v0 = smem_u32(sV + vst * kVBytes);
+          tc_fence_after();
+          const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + (g & 1) * kTileBytes);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16_ts(tmem + kOCol, pa + (ks >> 2) * 64 + (ks & 3) * 8, smem_desc_mn128(v0 + ks * 2048, kBoxBytes),
-                       Cf::IDESC_O, (pj > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&pv_done[b]);
-        umma_commit(&v_empty[vst]);
-        advance(pw, pj, pg, pn, pit);
-        ok = fill();
+          for (int ks = 0; ks < HDK / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kBoxBytes + (ks & 3) * 32;
+            umma_bf16(tmem + b * 128, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), kIdescS, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[b]);
+          umma_commit(&k_empty[g & 1]);
+          if (j + 1 == it.ntiles) umma_commit(q_empty);  // Q may be replaced once these scores are done
+        }
       }
       if (!ok) {
         *abort_flag = 1;
-        umma_commit(drain);  // every MMA issued so far completes before TMEM is freed
-        mbar_wait(drain, 0, err);
+        umma_commit(&drain[0]);  // every MMA issued by this thread completes before TMEM is freed
+        mbar_wait(&drain[0], 0, err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPvWarp) {
+    // ---------------- P.V MMA issuer ----------------
+    // O += P_g V_g once the softmax has written P_g (bf16, in TMEM over its
+    // own scores: keys 0-63 at columns 0-31, keys 64-127 at columns 64-95 of
+    // buffer g % 3, the A operand) and V_g has landed; an item's first P.V
+    // also waits until the softmax warps have read out the previous item.
+    if (lane == 0) {
+      bool ok = true;
+      int g = 0, n = 0;
+      for (int w = w_first; w < W && ok && !*abort_flag;
+           w = fa_next<CAUSAL>(w + G, W, G, cu, nq, nkv, nseq, mblocks), ++n) {
+        const FaItem it = fa_item<CAUSAL>(w, cu, nq, nkv, nseq, mblocks);
+        for (int j = 0; j < it.ntiles; ++j, ++g) {
+          const int b = g % kSBufs, vst = g % VS;
+          if (!mbar_wait_idle(&p_full[b], (g / kSBufs) & 1, err) ||
+              !mbar_wait_idle(&v_full[vst], (g / VS) & 1, err) ||
+              (j == 0 && n >= 1 && !mbar_wait_idle(o_free, (n - 1) & 1, err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t pa = tmem + b * 128, v0 = smem_u32(sV + vst * kVBytes);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16_ts(tmem + kOCol, pa + (ks >> 2) * 64 + (ks & 3) * 8, smem_desc_mn128(v0 + ks * 2048, kBoxBytes),
+                         Cf::IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&pv_done[b]);
+          umma_commit(&v_empty[vst]);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit(&drain[1]);
+        mbar_wait(&drain[1], 0, err);
       }
     }
     __syncwarp();
