@@ -113,6 +113,13 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// max(a, b, c) in one instruction (three-input max.f32 of sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Named barrier `id` over `n` threads.
 __device__ __forceinline__ void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 // Named barrier `id` over 64 threads returning the OR of `v` over them.
@@ -402,21 +409,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kv0 = j * kTile + half * 64;  // first key of this thread's columns
         const bool full_half = kv0 + 64 <= it.len && (!CAUSAL || kv0 + 63 <= it.m0);
         // raw-score max of this half (scale > 0), masked keys set to -inf
-        float m8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-        if (full_half) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
-        } else {
+        if (!full_half) {
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
             const int col = kv0 + c;
             if (col >= it.len || (CAUSAL && col > qpos)) sr[c] = __float_as_uint(-INFINITY);
-            m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
           }
         }
-        float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        // eight independent chains of three-input maxima (two scores per instruction)
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmax3(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]), -INFINITY);
+#pragma unroll
+        for (int c = 8; c < 32; ++c)
+          m8[c & 7] = fmax3(m8[c & 7], __uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1]));
+        float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         // the row's other half (slots alternate by tile: the partner is at most one tile behind)
         sMx[((g & 1) * 2 + half) * 128 + row] = mx;
         named_bar_sync(pair_bar, 64);
