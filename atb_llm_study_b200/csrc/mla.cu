@@ -105,12 +105,6 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(const __grid_const
     *abort_flag = 0;
     fence_barrier_init();
   }
-  // the 16 query heads of this group, 576 dims each, into the boxed layout
-  for (int i = threadIdx.x; i < 16 * (kD / 8); i += blockDim.x) {
-    const int r = i / (kD / 8), c = i % (kD / 8);
-    const uint4 val = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride + (int64_t)(hg * 16 + r) * kD + c * 8);
-    *reinterpret_cast<uint4*>(sQ + lat_off(r, c, 16 * 128)) = val;
-  }
   __syncthreads();
 
   if (warp == kProducer) {
@@ -149,6 +143,14 @@ __global__ void __launch_bounds__(kThreads) mla_decode_kernel(const __grid_const
 
   // ---- compute warps 0-3: all 16 heads; S over tokens 16w..16w+15 of a tile,
   //      O over latent dims 128w..128w+127 ----
+  // The 16 query heads of this group, 576 dims each, into the boxed layout,
+  // while the TMA warp already streams the first two tiles.
+  for (int i = threadIdx.x; i < 16 * (kD / 8); i += 128) {
+    const int r = i / (kD / 8), c = i % (kD / 8);
+    const uint4 val = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride + (int64_t)(hg * 16 + r) * kD + c * 8);
+    *reinterpret_cast<uint4*>(sQ + lat_off(r, c, 16 * 128)) = val;
+  }
+  bar_compute();
   float o[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;

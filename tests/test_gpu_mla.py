@@ -96,6 +96,8 @@ def test_mla_prep(q_hs, q_off):
     # scores that grow along the context: the running max moves tile after tile
     (16, [3000, 700, 128], 64, False, True),
     (16, [3000, 700, 128], 128, True, True),
+    # more (sequence, head group) pairs than SMs: several waves of split CTAs
+    (16, [(37 * i) % 400 + 1 for i in range(150)], 64, True, False),
 ])
 def test_mla_decode(nh, ctx, block, split, ramp):
     rng = np.random.default_rng(nh + block)
